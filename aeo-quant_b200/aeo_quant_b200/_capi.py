@@ -1,0 +1,108 @@
+"""ctypes binding of the sm_100a C-ABI library ``libaeoq_b200.so``.
+
+The library is built in-tree by ``aeo-quant_b200/build.py`` (or
+``__graft_entry__.build()``). There is no fallback: if the library is
+missing, or the process has no sm_100 GPU, every op raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import torch
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libaeoq_b200.so")
+
+BF16, F16, F32, I32, I64 = 0, 1, 2, 3, 4
+FP8_WEIGHT, FP8_ACTIVATION = 0, 1
+
+_DT = {torch.bfloat16: BF16, torch.float16: F16, torch.float32: F32, torch.int32: I32,
+       torch.int64: I64}
+
+_P, _I, _L, _Z = C.c_void_p, C.c_int, C.c_int64, C.c_size_t
+
+# name -> argtypes (every entry point returns int status unless listed in _RESTYPE)
+_SIGS = {
+    "aeoq_version": [],
+    "aeoq_last_error": [],
+    "aeoq_nvfp4_quantize_workspace_size": [_L, _L],
+    "aeoq_nvfp4_quantize": [_P, _I, _L, _L, _L, _P, _P, _P, _P, _Z, _P],
+    "aeoq_nvfp4_quantize_with_scale": [_P, _I, _L, _L, _L, _P, _P, _P, _P],
+    "aeoq_nvfp4_dequantize": [_P, _P, _P, _I, _L, _L, _P, _P],
+    "aeoq_fp8_quantize_rows": [_P, _I, _L, _L, _L, _P, _L, _P, _I, _P],
+    "aeoq_nvfp4_gemm": [_P, _P, _P, _I, _L, _L, _L, _L,
+                        _P, _P, _P, _I, _L, _L, _L, _L,
+                        _P, _I, _L, _L, _L, _L, _L, _P, _I, _L, _L, _P],
+    "aeoq_moe_nvfp4_decode_workspace_size": [_L, _L, _L],
+    "aeoq_moe_nvfp4_decode": [_P, _P, _I, _P, _L, _P, _P, _P, _I, _P, _P, _P, _I, _L, _L, _L,
+                              _P, _P, _Z, _P],
+}
+_SIGS["aeoq_moe_nvfp4_decode_gate_up"] = _SIGS["aeoq_moe_nvfp4_decode"]
+_SIGS["aeoq_moe_nvfp4_decode_down"] = _SIGS["aeoq_moe_nvfp4_decode"]
+_RESTYPE = {"aeoq_last_error": C.c_char_p, "aeoq_nvfp4_quantize_workspace_size": C.c_size_t,
+            "aeoq_moe_nvfp4_decode_workspace_size": C.c_size_t}
+
+_lib = None
+
+
+class AeoqError(RuntimeError):
+    pass
+
+
+def lib_path() -> str:
+    return _LIB_PATH
+
+
+def load():
+    """Load the library (once) and declare its signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(_LIB_PATH):
+        raise AeoqError(f"aeo_quant_b200 native library not built: {_LIB_PATH} is missing "
+                        "(run aeo-quant_b200/build.py)")
+    lib = C.CDLL(_LIB_PATH)
+    for name, args in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = _RESTYPE.get(name, C.c_int)
+    _lib = lib
+    return lib
+
+
+def exported_symbols():
+    return list(_SIGS)
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DT[dt]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {dt}") from None
+
+
+def check(rc: int) -> None:
+    if rc != 0:
+        msg = load().aeoq_last_error().decode(errors="replace")
+        if rc == -1:
+            raise ValueError(msg)
+        raise AeoqError(f"aeoq status {rc}: {msg}")
+
+
+def require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if not t.is_cuda:
+            raise AeoqError("aeo_quant_b200 runs on CUDA tensors only (no CPU path); "
+                            f"got a tensor on {t.device}")
+    dev = tensors[0].device
+    major, _ = torch.cuda.get_device_capability(dev)
+    if major != 10:
+        raise AeoqError(f"aeo_quant_b200 is built for sm_100a (B200); device {dev} is sm_{major}x")
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()

@@ -1,0 +1,306 @@
+// Shared device numerics for the quantized MoE expert path (sm_100a).
+//
+// Formats (aeo_quant src/aeo_quant/gpu/quant.py:15-27):
+//   * FP4 E2M1 nibble: bit 3 = sign, bits 0-2 = magnitude index into
+//     {0, .5, 1, 1.5, 2, 3, 4, 6}; two nibbles per byte, HIGH nibble = even k.
+//   * e4m3fn block scale per 16 elements along K.
+//   * per-tensor scale in the input dtype (bf16 for activations).
+// All arithmetic that decides a quantized bit is IEEE round-to-nearest: the
+// library is built without fast-math, and divisions use __fdiv_rn explicitly.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/aeoq.h"
+
+namespace aeoq {
+
+// ---------------------------------------------------------------------------
+// host-side error plumbing
+// ---------------------------------------------------------------------------
+int set_error(int code, const char* fmt, ...);
+int check_launch(const char* what);
+
+#define AEOQ_REQUIRE(cond, code, ...)                     \
+  do {                                                    \
+    if (!(cond)) return ::aeoq::set_error((code), __VA_ARGS__); \
+  } while (0)
+
+constexpr float kFp4Max = 6.0f;
+constexpr float kFp8Max = 448.0f;
+constexpr float kNvfp4Denom = 2688.0f;  // 6 * 448
+
+// ---------------------------------------------------------------------------
+// input dtypes
+// ---------------------------------------------------------------------------
+template <int DT> struct In;
+template <> struct In<AEOQ_BF16> {
+  using T = __nv_bfloat16;
+  static __device__ __forceinline__ float load(const T* p) { return __bfloat162float(*p); }
+  static __device__ __forceinline__ float to_f(T v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ float round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+  static __device__ __forceinline__ void store(void* p, float v) { *reinterpret_cast<T*>(p) = __float2bfloat16_rn(v); }
+  // |x| as an order-preserving integer; NaN patterns sort above infinity.
+  static __device__ __forceinline__ uint32_t abs_key(T v) { return __bfloat16_as_ushort(v) & 0x7FFFu; }
+  static __device__ __forceinline__ float key_to_f(uint32_t k) { return __bfloat162float(__ushort_as_bfloat16((unsigned short)k)); }
+};
+template <> struct In<AEOQ_F16> {
+  using T = __half;
+  static __device__ __forceinline__ float load(const T* p) { return __half2float(*p); }
+  static __device__ __forceinline__ float to_f(T v) { return __half2float(v); }
+  static __device__ __forceinline__ float round(float v) { return __half2float(__float2half_rn(v)); }
+  static __device__ __forceinline__ void store(void* p, float v) { *reinterpret_cast<T*>(p) = __float2half_rn(v); }
+  static __device__ __forceinline__ uint32_t abs_key(T v) { return __half_as_ushort(v) & 0x7FFFu; }
+  static __device__ __forceinline__ float key_to_f(uint32_t k) { return __half2float(__ushort_as_half((unsigned short)k)); }
+};
+template <> struct In<AEOQ_F32> {
+  using T = float;
+  static __device__ __forceinline__ float load(const T* p) { return *p; }
+  static __device__ __forceinline__ float to_f(T v) { return v; }
+  static __device__ __forceinline__ float round(float v) { return v; }
+  static __device__ __forceinline__ void store(void* p, float v) { *reinterpret_cast<T*>(p) = v; }
+  static __device__ __forceinline__ uint32_t abs_key(T v) { return __float_as_uint(v) & 0x7FFFFFFFu; }
+  static __device__ __forceinline__ float key_to_f(uint32_t k) { return __uint_as_float(k); }
+};
+
+__device__ __forceinline__ float nan_max(float a, float b) {
+  // max that propagates NaN like torch.amax / clamp
+  return (a != a || b != b) ? __int_as_float(0x7FC00000) : fmaxf(a, b);
+}
+
+// ---------------------------------------------------------------------------
+// float -> e4m3fn code, round-to-nearest-even; values that round past 448,
+// infinities and NaN map to the NaN code 0x7F (sign kept). This is torch's
+// float8_e4m3fn conversion rule, written from the format definition.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t e4m3_encode(float x) {
+  uint32_t b = __float_as_uint(x);
+  uint32_t sign = (b >> 24) & 0x80u;
+  uint32_t a = b & 0x7FFFFFFFu;
+  uint32_t code;
+  if (a >= 0x7F800000u) {
+    code = 0x7Fu;
+  } else if (a >= 0x3C800000u) {            // >= 2^-6: normal
+    code = ((a + 0x7FFFFu + ((a >> 20) & 1u)) >> 20) - (120u << 3);
+    if (code > 0x7Eu) code = 0x7Fu;
+  } else {                                  // subnormal: k * 2^-9, k in [0, 8]
+    code = __float2uint_rn(__uint_as_float(a) * 512.0f);
+  }
+  return sign | code;
+}
+
+__device__ __forceinline__ float e4m3_decode(uint32_t c) {
+  uint32_t e = (c >> 3) & 0xFu, m = c & 7u;
+  float v;
+  if (e == 0) v = (float)m * (1.0f / 512.0f);
+  else v = __uint_as_float(((e + 120u) << 23) | (m << 20));
+  if ((c & 0x7Fu) == 0x7Fu) v = __int_as_float(0x7FC00000);
+  return (c & 0x80u) ? -v : v;
+}
+
+// two e4m3 codes (low byte first) -> half2 (exact; e4m3 is a subset of fp16)
+__device__ __forceinline__ __half2 e4m3x2_to_half2(uint16_t two) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(two));
+  return *reinterpret_cast<__half2*>(&r);
+}
+
+// ---------------------------------------------------------------------------
+// FP4 E2M1 binning: count of midpoints {.25,.75,1.25,1.75,2.5,3.5,5} strictly
+// below |q| (ties go to the smaller magnitude), NaN -> 7, sign = (q < 0).
+// Restates _round_to_fp4_e2m1 (quant.py:121-130) incl. its clamp (:177).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t fp4_nibble(float q) {
+  if (q != q) return 7u;
+  float m = fabsf(q);
+  uint32_t idx = (m > 0.25f) + (m > 0.75f) + (m > 1.25f) + (m > 1.75f) +
+                 (m > 2.5f) + (m > 3.5f) + (m > 5.0f);
+  return ((q < 0.0f) ? 8u : 0u) | idx;
+}
+
+// Exact FP4 magnitude of a nibble as float (for building exact operands).
+__device__ __forceinline__ float fp4_value(uint32_t nib) {
+  const uint32_t m = nib & 7u;
+  // 0, .5, 1, 1.5, 2, 3, 4, 6  == (m<2 ? m*.5 : (2+(m&1)) * 2^((m>>1)-2))
+  float v = (m < 2u) ? 0.5f * (float)m : (float)(2u + (m & 1u)) * __uint_as_float((127u + (m >> 1) - 2u) << 23);
+  return (nib & 8u) ? -v : v;
+}
+
+// Tensor scale from the (abs) amax, in the input dtype: quant.py:167-168.
+template <int DT>
+__device__ __forceinline__ float nvfp4_tensor_scale(float amax) {
+  float t = In<DT>::round(__fdiv_rn(amax, kNvfp4Denom));
+  float floor_v = In<DT>::round(1e-12f);
+  return nan_max(t, floor_v);
+}
+
+// Quantize one 16-element block given the tensor scale (quant.py:169-183).
+// v[16] holds the input values as float. Returns the e4m3 code; writes the
+// 8 packed bytes (high nibble = even k) into *packed_lo / *packed_hi words.
+__device__ __forceinline__ uint32_t nvfp4_quant_block(const float (&v)[16], float ts,
+                                                      uint32_t& w0, uint32_t& w1) {
+  float wp[16];
+  float bmax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    wp[i] = __fdiv_rn(v[i], ts);
+    bmax = nan_max(bmax, fabsf(wp[i]));
+  }
+  float bm = (bmax != bmax) ? bmax : fmaxf(bmax, 1e-8f);
+  uint32_t sf = e4m3_encode(__fdiv_rn(bm, kFp4Max));
+  float bs = e4m3_decode(sf);
+  uint32_t words[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 16; i += 2) {
+    uint32_t hi = fp4_nibble(__fdiv_rn(wp[i], bs));
+    uint32_t lo = fp4_nibble(__fdiv_rn(wp[i + 1], bs));
+    uint32_t byte = (hi << 4) | lo;
+    words[i >> 3] |= byte << (8 * ((i >> 1) & 3));
+  }
+  w0 = words[0];
+  w1 = words[1];
+  return sf;
+}
+
+// ---------------------------------------------------------------------------
+// FP4 -> fp16 decode for the CUDA-core dot products.
+// A 32-bit word holds 8 nibbles; byte b has element 2b in its high nibble and
+// 2b+1 in its low nibble. Each output half2 pairs the nibbles 16 bits apart.
+// Placing the 3 magnitude bits at fp16 bits [11:9] and the sign at bit 15
+// yields exactly value * 2^-14 (code 001 lands on the fp16 subnormal 2^-15).
+//   h[0] = (e1, e5)   h[1] = (e0, e4)   h[2] = (e3, e7)   h[3] = (e2, e6)
+// Any operand decoded with this routine pairs with any other decoded with it.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void fp4x8_to_half2x4_scaled(uint32_t w, __half2 (&h)[4]) {
+  uint32_t r0 = ((w << 9) & 0x0E000E00u) | ((w << 12) & 0x80008000u);
+  uint32_t r1 = ((w << 5) & 0x0E000E00u) | ((w << 8) & 0x80008000u);
+  uint32_t r2 = ((w << 1) & 0x0E000E00u) | ((w << 4) & 0x80008000u);
+  uint32_t r3 = ((w >> 3) & 0x0E000E00u) | (w & 0x80008000u);
+  h[0] = *reinterpret_cast<__half2*>(&r0);
+  h[1] = *reinterpret_cast<__half2*>(&r1);
+  h[2] = *reinterpret_cast<__half2*>(&r2);
+  h[3] = *reinterpret_cast<__half2*>(&r3);
+}
+
+// Exact (unscaled) FP4 values in the same pairing, for the activation side.
+__device__ __forceinline__ void fp4x8_to_half2x4_exact(uint32_t w, __half2 (&h)[4]) {
+  fp4x8_to_half2x4_scaled(w, h);
+  const __half2 k = __floats2half2_rn(16384.0f, 16384.0f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __hmul2(h[i], k);
+}
+
+// ---------------------------------------------------------------------------
+// warp helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+__device__ __forceinline__ uint32_t warp_umax(uint32_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  // tanh-approximated GELU in float32, as torch's gelu(approximate="tanh")
+  const float kBeta = 0.7978845608028654f;   // sqrt(2/pi)
+  const float kKappa = 0.044715f;
+  float inner = kBeta * (x + kKappa * (x * x * x));
+  return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+__device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+}  // namespace aeoq
+
+namespace aeoq {
+
+// Scalar loads of a 0-d device tensor of a given dtype code.
+__device__ __forceinline__ float load_scalar_f(const void* p, int dt) {
+  if (dt == AEOQ_BF16) return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(p));
+  if (dt == AEOQ_F16) return __half2float(*reinterpret_cast<const __half*>(p));
+  return *reinterpret_cast<const float*>(p);
+}
+__device__ __forceinline__ int64_t load_index(const void* p, int dt, int64_t i) {
+  if (dt == AEOQ_I64) return reinterpret_cast<const int64_t*>(p)[i];
+  return reinterpret_cast<const int32_t*>(p)[i];
+}
+
+// Dot product of one 16-byte chunk (32 FP4 values = 2 blocks of 16) of an
+// activation already decoded to exact halves `a[16]` with a packed weight
+// chunk `w`, given the activation block scales pre-multiplied by 2^14 and the
+// two weight e4m3 codes. Each block's 16 products are accumulated in fp16,
+// where they are exact (|sum| < 2^-5 at a 2^-16 grid), then scaled exactly
+// and added to the float accumulator.
+__device__ __forceinline__ float chunk_dot(const __half2 (&a)[16], const float (&sa16k)[2], uint4 w,
+                                           uint16_t wsf, float acc) {
+  const float2 sw = __half22float2(e4m3x2_to_half2(wsf));
+  const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int b = 0; b < 2; ++b) {
+    __half2 h = __float2half2_rn(0.0f);
+    __half2 d[4];
+    fp4x8_to_half2x4_scaled(words[2 * b], d);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h = __hfma2(a[8 * b + i], d[i], h);
+    fp4x8_to_half2x4_scaled(words[2 * b + 1], d);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h = __hfma2(a[8 * b + 4 + i], d[i], h);
+    const float2 f = __half22float2(h);
+    acc = fmaf(f.x + f.y, sa16k[b] * (b ? sw.y : sw.x), acc);
+  }
+  return acc;
+}
+
+// Decode a packed activation chunk (uint4 + two e4m3 codes) into exact
+// halves and 2^14-scaled block scales for chunk_dot.
+__device__ __forceinline__ void decode_act_chunk(uint4 p, uint16_t sf2, __half2 (&a)[16],
+                                                 float (&sa16k)[2]) {
+  const uint32_t words[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 t[4];
+    fp4x8_to_half2x4_exact(words[i], t);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) a[4 * i + j] = t[j];
+  }
+  const float2 s = __half22float2(e4m3x2_to_half2(sf2));
+  sa16k[0] = s.x * 16384.0f;
+  sa16k[1] = s.y * 16384.0f;
+}
+
+// Quantize 32 consecutive bf16 values (one chunk) with tensor scale ts and
+// return the chunk in chunk_dot's activation form.
+__device__ __forceinline__ void quant_act_chunk_bf16(const __nv_bfloat16* src, float ts,
+                                                     __half2 (&a)[16], float (&sa16k)[2]) {
+  float v[2][16];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 u = *reinterpret_cast<const uint4*>(src + 8 * q);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[q >> 1][8 * (q & 1) + j] = __bfloat162float(e[j]);
+  }
+  uint32_t w[4];
+  const uint32_t s0 = nvfp4_quant_block(v[0], ts, w[0], w[1]);
+  const uint32_t s1 = nvfp4_quant_block(v[1], ts, w[2], w[3]);
+  decode_act_chunk(make_uint4(w[0], w[1], w[2], w[3]), (uint16_t)(s0 | (s1 << 8)), a, sa16k);
+}
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+}  // namespace aeoq

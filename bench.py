@@ -1,0 +1,386 @@
+"""Benchmark: one-token NVFP4 MoE expert decode (batch 1).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B]
+
+A step is one token through one Gemma-4-26B-A4B MoE layer: 128 NVFP4
+experts (gate_up [1408, 2816], down [2816, 704]), top-8 routing, through
+``Gemma4TextExpertsNVFP4.forward`` (the reference's class-swap module API).
+Weights: bf16 N(0, 0.02) quantized on the device with the library's
+quantizer; hidden bf16 N(0, 1); ids uniform without replacement; weights
+softmax(N(0, 1)). 32 independent layers are resident and steps cycle through
+them, so each step streams cold weights from HBM (26.8 MB per step, 830 MB
+between revisits; L2 is 126 MB): inputs larger than L2, no flush needed.
+
+Multi-GPU: one-token decode does not shard (expert parallelism only pays at
+prefill sizes), so N GPUs run N independent replicas; value = all ranks'
+tokens / max-over-ranks device time ("scaling": "weak").
+
+``--impl reference`` times the reference algorithm on the host CPU: the
+numpy port in ``oracle/`` (the reference's own path needs a GPU and Triton)
+on a bounded token sample with all host threads, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "aeo-quant_b200"))
+sys.path.insert(0, ROOT)
+
+E, H, I, TOPK = 128, 2816, 704, 8
+EXPERT_BYTES = 1408 * 1408 + 1408 * 176 + 2816 * 352 + 2816 * 44  # packed + scales, 3,345,408
+GATEUP_BYTES = 1408 * 1408 + 1408 * 176
+DOWN_BYTES = 2816 * 352 + 2816 * 44
+METRIC = "MoE decode tok/s (M=1 gather) + NVFP4 prefill TFLOPS, % of roofline"
+FALLBACK_HBM_GBS = 6650.0
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the gate_up
+# kernel at this workload, from the ncu capture summarised in
+# profiles/moe_decode_gateup_b1.md (None until captured).
+NCU_TRAFFIC_GATEUP = None
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=320)
+    p.add_argument("--warmup", type=int, default=32)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--layers", type=int, default=32)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=15.0)
+    return p.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = str(gpu_index)
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) > 8 for i in range(4)
+                          if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def make_layers(torch, L, device, seed=0):
+    from aeo_quant_b200.gpu import quant as Q
+    layers = []
+    for li in range(L):
+        g = torch.Generator(device=device).manual_seed(seed * 1000 + li)
+        w = torch.randn(E, 2 * I, H, generator=g, device=device, dtype=torch.bfloat16).mul_(0.02)
+        gp, gs, gt = Q.quantize_3d_to_nvfp4(w)
+        del w
+        w = torch.randn(E, H, I, generator=g, device=device, dtype=torch.bfloat16).mul_(0.02)
+        dp, ds, dt = Q.quantize_3d_to_nvfp4(w)
+        del w
+        layers.append((gp, gs, gt.float(), dp, ds, dt.float()))
+    torch.cuda.synchronize()
+    return layers
+
+
+def make_module(torch, device, layer):
+    import types
+    from aeo_quant_b200.bridges.gemma4.modeling_nvfp4 import Gemma4TextExpertsNVFP4
+    cfg = types.SimpleNamespace(num_experts=E, hidden_size=H, moe_intermediate_size=I,
+                                hidden_activation="gelu_pytorch_tanh")
+    m = Gemma4TextExpertsNVFP4(cfg)
+    gp, gs, gt, dp, ds, dt = layer
+    # buffers alias the resident layer tensors (no copies)
+    m.gate_up_proj, m.gate_up_proj_scale, m.gate_up_proj_scale_2 = gp, gs, gt
+    m.down_proj, m.down_proj_scale, m.down_proj_scale_2 = dp, ds, dt
+    return m
+
+
+def routing(torch, S, B, seed):
+    g = torch.Generator().manual_seed(seed)
+    idx = torch.stack([torch.stack([torch.randperm(E, generator=g)[:TOPK] for _ in range(B)]) for _ in range(S)])
+    w = torch.softmax(torch.randn(S, B, TOPK, generator=g), -1).to(torch.bfloat16)
+    h = torch.randn(S, B, H, generator=g).to(torch.bfloat16)
+    return idx, w, h
+
+
+def cpu_baseline(seconds, kind_note="port"):
+    """Time the numpy port of the reference decode (oracle/) on the host."""
+    import numpy as np
+    import torch
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import moe as OM
+    from oracle import quant as OQ
+    pool_e = TOPK
+    g = torch.Generator().manual_seed(7)
+    wgu = (torch.randn(pool_e, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+    wd = (torch.randn(pool_e, H, I, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+    gp, gs, gt = OQ.quantize_nvfp4(wgu)
+    dp, ds, dt = OQ.quantize_nvfp4(wd)
+    m = OM.NVFP4Experts(gp, gs, gt, dp, ds, dt)
+    threads = os.cpu_count() or 1
+
+    def one(i):
+        rng = np.random.default_rng(i)
+        h = np.asarray(torch.randn(1, H, generator=torch.Generator().manual_seed(i)).to(torch.bfloat16).float())
+        idx = rng.permutation(pool_e)[None, :TOPK]
+        w = np.full((1, TOPK), 1.0 / TOPK, np.float32)
+        OM.nvfp4_experts_forward(m, h, idx, w)
+
+    one(0)  # warm-up
+    done, t0 = 0, time.perf_counter()
+    with ThreadPoolExecutor(threads) as ex:
+        while time.perf_counter() - t0 < seconds:
+            list(ex.map(one, range(done + 1, done + 1 + threads)))
+            done += threads
+    dt_s = time.perf_counter() - t0
+    return {"value": done / dt_s, "unit": "tok/s", "cores": threads, "kind": kind_note,
+            "sample": f"{done} tokens x 1 layer of the numpy port (oracle/moe.py nvfp4_decode_3d), "
+                      f"top-8 over an 8-expert pool (per-token work identical to 128 experts), "
+                      f"{threads} threads, {dt_s:.1f} s"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    t_budget = max(5.0, min(60.0, args.steps * 0.05))
+    cb = cpu_baseline(t_budget)
+    print(json.dumps({
+        "metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp4(e2m1)+e4m3 scales, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": "config1: M=1 NVFP4 expert-gather decode, one MoE layer, batch 1",
+                   "experts": E, "hidden": H, "intermediate": I, "top_k": TOPK},
+        "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    import torch
+    import torch.distributed as dist
+    from aeo_quant_b200 import _capi as A
+
+    if world > 1:
+        dist.init_process_group("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, K, W = args.batch, args.steps, max(3, args.warmup)
+    L = args.layers
+
+    layers = make_layers(torch, L, dev, seed=rank + 1)
+    mods = [make_module(torch, dev, lay) for lay in layers]
+    S = K + W
+    idx, wts, hid = routing(torch, S, B, 11 + rank)
+    idx_d, wts_d, hid_d = idx.to(dev), wts.to(dev), hid.to(dev)
+
+    def step(s):
+        return mods[s % L](hid_d[s], idx_d[s], wts_d[s])
+
+    # warm-up (eager, public API)
+    for s in range(W):
+        step(s)
+    torch.cuda.synchronize()
+
+    # capture the K timed steps in one CUDA graph (launch overhead out of the
+    # device timeline; every step still launches its own kernels)
+    cs = torch.cuda.Stream(dev)
+    cs.wait_stream(torch.cuda.current_stream(dev))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(cs):
+        step(W)
+        with torch.cuda.graph(graph, stream=cs):
+            outs = [step(W + s) for s in range(K)]
+    torch.cuda.current_stream(dev).wait_stream(cs)
+    torch.cuda.synchronize()
+    graph.replay()   # warm replay
+    torch.cuda.synchronize()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        cur = torch.cuda.current_stream(dev)
+        ev0.record(cur)
+        graph.replay()
+        ev1.record(cur)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * B * K / (ms_max / 1000.0)
+
+    # ---- per-kernel timing for the roofline (same stream, CUDA events) ----
+    lib = A.load()
+    ws_n = lib.aeoq_moe_nvfp4_decode_workspace_size(TOPK, H, I)
+    ws = torch.empty(ws_n, dtype=torch.uint8, device=dev)
+    out = torch.empty(1, H, dtype=torch.bfloat16, device=dev)
+
+    def stage(fn, s):
+        gp, gs, gt, dp, ds, dt = layers[s % L]
+        return fn(hid_d[s].data_ptr(), idx_d[s].data_ptr(), A.I64, wts_d[s].data_ptr(), TOPK,
+                  gp.data_ptr(), gs.data_ptr(), gt.data_ptr(), A.F32, dp.data_ptr(), ds.data_ptr(),
+                  dt.data_ptr(), A.F32, E, H, I, out.data_ptr(), ws.data_ptr(), ws_n,
+                  torch.cuda.current_stream(dev).cuda_stream)
+
+    stage_ms = {}
+    if B == 1:
+        for name, fn in (("gate_up", lib.aeoq_moe_nvfp4_decode_gate_up), ("down", lib.aeoq_moe_nvfp4_decode_down)):
+            for s in range(W):
+                A.check(stage(fn, s))
+            torch.cuda.synchronize()
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record()
+            for s in range(K):
+                A.check(stage(fn, W + s))
+            a1.record()
+            torch.cuda.synchronize()
+            stage_ms[name] = a0.elapsed_time(a1) / K
+
+    # ---- end to end through the public module API with host buffers ----
+    hid_h = hid.pin_memory()
+    idx_h = idx.pin_memory()
+    wts_h = wts.pin_memory()
+    out_h = torch.empty(B, H, dtype=torch.bfloat16).pin_memory()
+    h_in = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
+    i_in = torch.empty(B, TOPK, dtype=torch.int64, device=dev)
+    w_in = torch.empty(B, TOPK, dtype=torch.bfloat16, device=dev)
+    n_e2e = min(K, 200)
+
+    def e2e_step(s):
+        h_in.copy_(hid_h[s], non_blocking=True)
+        i_in.copy_(idx_h[s], non_blocking=True)
+        w_in.copy_(wts_h[s], non_blocking=True)
+        y = mods[s % L](h_in, i_in, w_in)
+        out_h.copy_(y, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+
+    for s in range(W):
+        e2e_step(s)
+    if world > 1:
+        dist.barrier()
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record()
+    for s in range(n_e2e):
+        e2e_step(W + s)
+    b1.record()
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([b0.elapsed_time(b1)], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_val = world * B * n_e2e / (float(e2e_ms.item()) / 1000.0)
+
+    if rank == 0:
+        hbm, peak_src = peaks()
+        roof = None
+        if "gate_up" in stage_ms:
+            alg = TOPK * GATEUP_BYTES + H * 2 + TOPK * I * 2
+            ach = alg / (stage_ms["gate_up"] / 1000.0) / 1e9
+            roof = {"bound": "hbm", "kernel": "moe_decode_gateup_kernel", "achieved": round(ach, 1),
+                    "peak": hbm, "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else "fallback",
+                    "unit": "GB/s", "frac": round(ach / hbm, 4),
+                    "traffic": NCU_TRAFFIC_GATEUP, "algorithmic_bytes": alg,
+                    "launch_us": round(stage_ms["gate_up"] * 1000, 3)}
+            alg_d = TOPK * DOWN_BYTES + TOPK * I * 2 + H * 2
+            roof["down_kernel"] = {"kernel": "moe_decode_down_kernel", "launch_us": round(stage_ms["down"] * 1000, 3),
+                                   "achieved": round(alg_d / (stage_ms["down"] / 1000.0) / 1e9, 1),
+                                   "algorithmic_bytes": alg_d}
+        step_bytes = TOPK * EXPERT_BYTES + 2 * H * 2
+        res = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp4(e2m1)+e4m3 scales, fp32 accumulate, bf16 io",
+            "data": "synthetic (bf16 N(0,0.02) weights quantized on device; N(0,1) hidden; uniform top-8)",
+            "config": {"workload": f"config1: M=1 NVFP4 expert-gather decode, one MoE layer, batch {B}",
+                       "experts": E, "hidden": H, "intermediate": I, "top_k": TOPK, "batch": B,
+                       "resident_layers": L, "l2": f"inputs larger than L2: {L} layers cycled, "
+                       f"{L * 428} MB resident, 26.8 MB streamed per step",
+                       "parallelism": f"replicas x{world}", "timing": "one CUDA graph of K steps, CUDA events"},
+            "step_hbm_gbs": round(step_bytes / (ms_max / K / 1000.0) / 1e9, 1),
+            "gpu_launches": 2 * K,
+            "clocks": clk.summary(),
+            "e2e": {"value": round(e2e_val, 1), "unit": "tok/s", "steps": n_e2e,
+                    "h2d_bytes_per_step": B * H * 2 + B * TOPK * 8 + B * TOPK * 2,
+                    "d2h_bytes_per_step": B * H * 2,
+                    "path": "Gemma4TextExpertsNVFP4.forward eager, pinned host in/out, sync per step"},
+            "roofline": roof,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            res["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,172 @@
+/*
+ * aeoq.h — C ABI of the B200 (sm_100a) quantized MoE expert library.
+ *
+ * Every entry point takes plain device pointers, element counts, byte strides
+ * and a cudaStream_t passed as void*. None allocates device memory: callers
+ * pass outputs and, where a kernel needs scratch, a workspace whose size the
+ * matching *_workspace_size() function returns. All calls are asynchronous
+ * on the given stream, never synchronize the host, and never abort: they
+ * return AEOQ_OK (0) or a negative status, with a message available from
+ * aeoq_last_error() (thread-local).
+ *
+ * The Python package aeo_quant_b200 binds these with ctypes and mirrors the
+ * aeo_quant Python API that each entry point replaces; citations below are
+ * path:line inside the aeo_quant project.
+ */
+#ifndef AEOQ_H_
+#define AEOQ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define AEOQ_API __attribute__((visibility("default")))
+#else
+#define AEOQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element type codes */
+#define AEOQ_BF16 0
+#define AEOQ_F16 1
+#define AEOQ_F32 2
+#define AEOQ_I32 3
+#define AEOQ_I64 4
+
+/* status codes */
+#define AEOQ_OK 0
+#define AEOQ_ERR_INVALID (-1)     /* bad shape, stride, dtype or alignment */
+#define AEOQ_ERR_CUDA (-2)        /* a CUDA launch or runtime call failed */
+#define AEOQ_ERR_WORKSPACE (-3)   /* workspace missing or too small */
+#define AEOQ_ERR_UNSUPPORTED (-4) /* device is not sm_100 */
+
+/* FP8 row-quantizer modes */
+#define AEOQ_FP8_WEIGHT 0     /* quant.py:51-106 — bf16 scale per row */
+#define AEOQ_FP8_ACTIVATION 1 /* bridges/gemma4/modeling.py:101-104 — f32 scale */
+
+/* Library version (major*10000 + minor*100 + patch). */
+AEOQ_API int aeoq_version(void);
+
+/* Message for the last failing call on this host thread ("" if none). */
+AEOQ_API const char* aeoq_last_error(void);
+
+/* ------------------------------------------------------------------------
+ * NVFP4 two-level quantizer.
+ * Replaces quantize_2d_to_nvfp4 / quantize_3d_to_nvfp4
+ * (src/aeo_quant/gpu/quant.py:138-185, :215-230) and the activation alias
+ * _quantize_bf16_activation_to_nvfp4 (src/aeo_quant/gpu/nvfp4_matmul.py:338-354).
+ *
+ * x        rows x K elements of `dtype` (AEOQ_BF16/F16/F32), row stride `ld`
+ *          elements; leading dims of the reference tensor are flattened.
+ * packed   rows x K/2 bytes, contiguous (high nibble = even k).
+ * sf       rows x K/16 e4m3fn codes, contiguous.
+ * ts_out   one element of `dtype`: clamp(amax/2688, 1e-12) in that dtype.
+ * Bit-exact with the reference. K % 16 == 0 required (quant.py:161-164).
+ * ------------------------------------------------------------------------ */
+AEOQ_API size_t aeoq_nvfp4_quantize_workspace_size(int64_t rows, int64_t K);
+AEOQ_API int aeoq_nvfp4_quantize(const void* x, int dtype, int64_t rows, int64_t K, int64_t ld,
+                        uint8_t* packed, uint8_t* sf, void* ts_out,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Same, with a caller-provided tensor scale (`ts_in`, one `dtype` element on
+ * the device) instead of the global amax. Used where one scale is shared
+ * across a batch that is quantized in pieces. */
+AEOQ_API int aeoq_nvfp4_quantize_with_scale(const void* x, int dtype, int64_t rows, int64_t K, int64_t ld,
+                                   const void* ts_in, uint8_t* packed, uint8_t* sf, void* stream);
+
+/* NVFP4 dequantizer: bf16(value * block_scale * ts), rows x K out, contiguous.
+ * Replaces dequant_2d_from_nvfp4 / dequant_3d_from_nvfp4 (quant.py:188-212,
+ * :233-246). `ts` is one element of ts_dtype on the device. */
+AEOQ_API int aeoq_nvfp4_dequantize(const uint8_t* packed, const uint8_t* sf, const void* ts, int ts_dtype,
+                          int64_t rows, int64_t K, void* out, void* stream);
+
+/* ------------------------------------------------------------------------
+ * FP8 e4m3fn per-row quantizer.
+ * mode AEOQ_FP8_WEIGHT replaces quantize_2d_to_fp8 / quantize_3d_to_fp8
+ * (src/aeo_quant/gpu/quant.py:51-106): scale_out is rows bf16 values.
+ * mode AEOQ_FP8_ACTIVATION replaces the per-row dynamic input quant of
+ * Gemma4TextExpertsFP8._fp8_linear (src/aeo_quant/bridges/gemma4/modeling.py:101-104):
+ * scale_out is rows f32 values. Bit-exact with the reference.
+ * ------------------------------------------------------------------------ */
+AEOQ_API int aeoq_fp8_quantize_rows(const void* x, int dtype, int64_t rows, int64_t K, int64_t ld,
+                           uint8_t* q, int64_t q_ld, void* scale_out, int mode, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Block-scaled NVFP4 GEMM with optional expert gather.
+ * Replaces nvfp4_linear_prequantized, nvfp4_linear_3d_prequantized and
+ * nvfp4_linear_3d_gather (src/aeo_quant/gpu/nvfp4_matmul.py:399-519,
+ * :522-686, :689-864), i.e. the Triton kernels _nvfp4_matmul_kernel,
+ * _nvfp4_matmul_kernel_3d and _nvfp4_matmul_kernel_3d_gather (:51-325).
+ *
+ *   C[s][m][n] = out( alpha * sum_k A[s][m][k] * W[e(s)][n][k] )
+ *   e(s) = expert_ids ? expert_ids[s] : s;   alpha = f32(*a_ts) * f32(*w_ts)
+ *
+ * Operands are packed FP4 bytes with e4m3 block scales (16 along K). All
+ * strides are in BYTES; a_slot_stride == 0 shares one activation across the
+ * slots (the reference's stride_ae = 0). Packed rows must be 16-byte aligned.
+ * An expert id outside [0, num_experts) contributes zeros (the reference's
+ * forward skips id == num_experts, modeling_nvfp4.py:220).
+ * c_dtype is AEOQ_BF16 or AEOQ_F32.
+ * ------------------------------------------------------------------------ */
+AEOQ_API int aeoq_nvfp4_gemm(const uint8_t* a, const uint8_t* a_sf, const void* a_ts, int a_ts_dtype,
+                    int64_t a_slot_stride, int64_t a_row_stride,
+                    int64_t a_sf_slot_stride, int64_t a_sf_row_stride,
+                    const uint8_t* w, const uint8_t* w_sf, const void* w_ts, int w_ts_dtype,
+                    int64_t w_expert_stride, int64_t w_row_stride,
+                    int64_t w_sf_expert_stride, int64_t w_sf_row_stride,
+                    const void* expert_ids, int ids_dtype, int64_t num_experts,
+                    int64_t slots, int64_t M, int64_t N, int64_t K,
+                    void* c, int c_dtype, int64_t c_slot_stride, int64_t c_row_stride,
+                    void* stream);
+
+/* ------------------------------------------------------------------------
+ * One-token NVFP4 MoE expert forward, fully fused (two launches).
+ * Replaces Gemma4TextExpertsNVFP4._forward_decode_3d
+ * (src/aeo_quant/bridges/gemma4/modeling_nvfp4.py:132-186): hidden quant ->
+ * gathered gate_up GEMV -> GeGLU (bf16) -> shared-scale re-quant -> gathered
+ * down GEMV -> bf16 weighted combine. Same bf16 rounding points.
+ *
+ * hidden      [1, H] bf16        top_k_index [1, k] int32/int64 (idx_dtype)
+ * top_k_w     [1, k] bf16        out         [1, H] bf16
+ * gate_up     [E, 2I, H/2] u8 contiguous, gate_up_sf [E, 2I, H/16] e4m3
+ * down        [E, H, I/2]  u8 contiguous, down_sf    [E, H, I/16]  e4m3
+ * *_ts        0-d tensor scale (f32 or bf16, *_ts_dtype)
+ * Requires H % 64 == 0, I % 64 == 0, 1 <= k <= 16.
+ * ------------------------------------------------------------------------ */
+AEOQ_API size_t aeoq_moe_nvfp4_decode_workspace_size(int64_t top_k, int64_t hidden, int64_t inter);
+AEOQ_API int aeoq_moe_nvfp4_decode(const void* hidden, const void* top_k_index, int idx_dtype,
+                          const void* top_k_weights, int64_t top_k,
+                          const uint8_t* gate_up, const uint8_t* gate_up_sf,
+                          const void* gate_up_ts, int gate_up_ts_dtype,
+                          const uint8_t* down, const uint8_t* down_sf,
+                          const void* down_ts, int down_ts_dtype,
+                          int64_t num_experts, int64_t hidden_dim, int64_t inter_dim,
+                          void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The two launches of aeoq_moe_nvfp4_decode issued one at a time, same
+ * arguments. gate_up leaves the GeGLU output and its amax in the workspace;
+ * down consumes them. Used to time and profile each stage on its own. */
+AEOQ_API int aeoq_moe_nvfp4_decode_gate_up(const void* hidden, const void* top_k_index, int idx_dtype,
+                                           const void* top_k_weights, int64_t top_k,
+                                           const uint8_t* gate_up, const uint8_t* gate_up_sf,
+                                           const void* gate_up_ts, int gate_up_ts_dtype,
+                                           const uint8_t* down, const uint8_t* down_sf,
+                                           const void* down_ts, int down_ts_dtype,
+                                           int64_t num_experts, int64_t hidden_dim, int64_t inter_dim,
+                                           void* out, void* workspace, size_t workspace_bytes, void* stream);
+AEOQ_API int aeoq_moe_nvfp4_decode_down(const void* hidden, const void* top_k_index, int idx_dtype,
+                                        const void* top_k_weights, int64_t top_k,
+                                        const uint8_t* gate_up, const uint8_t* gate_up_sf,
+                                        const void* gate_up_ts, int gate_up_ts_dtype,
+                                        const uint8_t* down, const uint8_t* down_sf,
+                                        const void* down_ts, int down_ts_dtype,
+                                        int64_t num_experts, int64_t hidden_dim, int64_t inter_dim,
+                                        void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AEOQ_H_ */

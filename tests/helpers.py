@@ -1,0 +1,47 @@
+"""Shared test helpers: seeded inputs and torch <-> oracle conversions."""
+import numpy as np
+import torch
+
+from oracle import numerics as N
+
+
+def bf16_to_np(t: torch.Tensor) -> np.ndarray:
+    """bf16 tensor (any device) -> float32 numpy array of the same values."""
+    return t.detach().to(torch.float32).cpu().numpy()
+
+
+def np_to_bf16(a, device="cuda") -> torch.Tensor:
+    bits = N.bf16_bits(np.asarray(a, np.float32)).view(np.int16)
+    return torch.from_numpy(bits.copy()).view(torch.bfloat16).to(device)
+
+
+def bits_to_bf16(bits, device="cuda") -> torch.Tensor:
+    return torch.from_numpy(np.asarray(bits, np.uint16).view(np.int16).copy()).view(torch.bfloat16).to(device)
+
+
+def u8(t: torch.Tensor) -> np.ndarray:
+    return t.detach().contiguous().view(torch.uint8).cpu().numpy()
+
+
+def randn_bf16(shape, std, seed, device="cuda") -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * std).to(torch.bfloat16).to(device)
+
+
+def max_rel_err(out, ref):
+    out = np.asarray(out, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.max(np.abs(out - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+# Output tolerance for GEMM / MoE results against the fp32 dequantize-then-
+# matmul oracle: max|err| <= 2e-3 * max|ref|.
+TOL = 2e-3
+
+
+def routing(T, E, k, seed):
+    """top-k ids uniform without replacement and softmax(N(0,1)) weights."""
+    g = torch.Generator().manual_seed(seed)
+    idx = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)])
+    w = torch.softmax(torch.randn(T, k, generator=g), -1).to(torch.bfloat16)
+    return idx, w

@@ -1,0 +1,94 @@
+"""CPU checks of the C-ABI library: it loads, exports every declared symbol,
+and rejects bad arguments before touching the GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "aeoq.h")
+
+
+def declared_symbols():
+    with open(HEADER) as f:
+        src = f.read()
+    return sorted(set(re.findall(r"AEOQ_API\s+[\w\s\*]+?\b(aeoq_\w+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from aeo_quant_b200 import _capi
+    return _capi.load()
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    assert "aeoq_nvfp4_quantize" in syms and "aeoq_moe_nvfp4_decode" in syms
+    assert len(syms) >= 8
+
+
+def test_library_exports_every_declared_symbol(lib):
+    from aeo_quant_b200 import _capi
+    raw = ctypes.CDLL(_capi.lib_path())
+    for s in declared_symbols():
+        assert hasattr(raw, s), f"{s} declared in include/aeoq.h but not exported"
+    # and the ctypes table binds exactly the header
+    assert sorted(_capi.exported_symbols()) == declared_symbols()
+
+
+def test_version_and_error_string(lib):
+    assert lib.aeoq_version() >= 100
+    assert isinstance(lib.aeoq_last_error(), bytes)
+
+
+def test_argument_validation_without_gpu(lib):
+    # K not a multiple of 16: rejected before any CUDA call
+    rc = lib.aeoq_nvfp4_quantize(None, 0, 4, 24, 24, None, None, None, None, 0, None)
+    assert rc == -1
+    assert b"divisible by block_size" in lib.aeoq_last_error()
+    rc = lib.aeoq_nvfp4_quantize(None, 7, 4, 32, 32, None, None, None, None, 0, None)
+    assert rc == -1
+    rc = lib.aeoq_fp8_quantize_rows(None, 0, 4, 32, 32, None, 32, None, 5, None)
+    assert rc == -1 and b"mode" in lib.aeoq_last_error()
+    rc = lib.aeoq_moe_nvfp4_decode(None, None, 4, None, 8, None, None, None, 2, None, None, None, 2,
+                                   128, 2816, 704, None, None, 0, None)
+    assert rc == -1
+    rc = lib.aeoq_moe_nvfp4_decode(None, None, 4, None, 99, None, None, None, 2, None, None, None, 2,
+                                   128, 2816, 704, None, None, 0, None)
+    assert rc == -1 and b"top_k" in lib.aeoq_last_error()
+
+
+def test_workspace_sizes(lib):
+    assert lib.aeoq_nvfp4_quantize_workspace_size(1, 2816) == 0
+    assert lib.aeoq_nvfp4_quantize_workspace_size(1408, 2816) > 0
+    assert lib.aeoq_moe_nvfp4_decode_workspace_size(8, 2816, 704) >= 8 * 704 * 2
+
+
+def test_python_api_refuses_cpu_tensors():
+    import torch
+    from aeo_quant_b200.gpu import quant as Q
+    from aeo_quant_b200 import AeoqError
+    with pytest.raises(AeoqError):
+        Q.quantize_2d_to_nvfp4(torch.zeros(2, 32, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="expects a 2D tensor"):
+        Q.quantize_2d_to_nvfp4(torch.zeros(2, 2, 32, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="must be divisible by block_size"):
+        Q.quantize_3d_to_nvfp4(torch.zeros(1, 2, 24, dtype=torch.bfloat16))
+
+
+def test_matmul_shape_errors_match_reference():
+    import torch
+    from aeo_quant_b200.gpu import nvfp4_matmul as NM
+    a = torch.zeros(4, 64, dtype=torch.uint8)
+    s = torch.zeros(4, 8, dtype=torch.uint8)
+    t = torch.zeros(())
+    with pytest.raises(ValueError, match="must be divisible by BLOCK_N=128"):
+        NM.nvfp4_linear_prequantized(a, s, t, torch.zeros(100, 64, dtype=torch.uint8), s, t)
+    with pytest.raises(ValueError, match="w_packed must be 3D"):
+        NM.nvfp4_linear_3d_gather(a, s, t, torch.zeros(128, 64, dtype=torch.uint8), s, t,
+                                  torch.zeros(2, dtype=torch.int64))
+    with pytest.raises(ValueError, match="expert_ids must be 1D"):
+        NM.nvfp4_linear_3d_gather(a, s, t, torch.zeros(2, 128, 64, dtype=torch.uint8), s, t,
+                                  torch.zeros(2, 1, dtype=torch.int64))

@@ -1,0 +1,117 @@
+"""Gemma4TextExpertsNVFP4 forwards on the GPU vs the oracle restatement of the
+reference forwards, and vs the reference-generated golden outputs."""
+import types
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import TOL, bf16_to_np, bits_to_bf16, max_rel_err, randn_bf16, routing, u8
+from oracle import moe as OM
+from oracle import numerics as N
+
+pytestmark = pytest.mark.gpu
+
+
+def make_module(E, H, I, gp, gs, gt, dp, ds, dt):
+    from aeo_quant_b200.bridges.gemma4.modeling_nvfp4 import Gemma4TextExpertsNVFP4
+    cfg = types.SimpleNamespace(num_experts=E, hidden_size=H, moe_intermediate_size=I,
+                                hidden_activation="gelu_pytorch_tanh")
+    m = Gemma4TextExpertsNVFP4(cfg).cuda()
+    m.gate_up_proj.copy_(gp)
+    m.gate_up_proj_scale.copy_(gs)
+    m.gate_up_proj_scale_2.copy_(gt)
+    m.down_proj.copy_(dp)
+    m.down_proj_scale.copy_(ds)
+    m.down_proj_scale_2.copy_(dt)
+    return m
+
+
+@pytest.fixture(scope="module")
+def golden_module(moe_golden):
+    g = moe_golden
+    t = lambda k, dt=torch.uint8: torch.from_numpy(g[k].copy()).view(dt).cuda()
+    E, twoI, Hh = g["nv/gate_up_proj"].shape
+    return make_module(E, Hh * 2, twoI // 2, t("nv/gate_up_proj"),
+                       t("nv/gate_up_proj_scale").view(torch.float8_e4m3fn),
+                       torch.tensor(g["nv/gate_up_proj_scale_2"][0]),
+                       t("nv/down_proj"), t("nv/down_proj_scale").view(torch.float8_e4m3fn),
+                       torch.tensor(g["nv/down_proj_scale_2"][0]))
+
+
+@pytest.mark.parametrize("T", [1, 7, 33])
+def test_golden_forward(golden_module, moe_golden, T):
+    g = moe_golden
+    h = bits_to_bf16(g[f"nv/T{T}/hidden"])
+    idx = torch.from_numpy(g[f"nv/T{T}/idx"]).cuda()
+    w = bits_to_bf16(g[f"nv/T{T}/w"])
+    y = golden_module(h, idx, w)
+    assert y.shape == h.shape and y.dtype == torch.bfloat16
+    ref = N.bf16_from_bits(g[f"nv/T{T}/out"])
+    assert max_rel_err(bf16_to_np(y), ref) <= TOL
+
+
+@pytest.fixture(scope="module")
+def full_layer():
+    """BASELINE config 1 layer: 128 experts, H=2816, I=704, NVFP4 per projection."""
+    from aeo_quant_b200.gpu import quant as Q
+    E, H, I = 128, 2816, 704
+    wgu = randn_bf16((E, 2 * I, H), 0.02, 100)
+    gp, gs, gt = Q.quantize_3d_to_nvfp4(wgu)
+    del wgu
+    wd = randn_bf16((E, H, I), 0.02, 101)
+    dp, ds, dt = Q.quantize_3d_to_nvfp4(wd)
+    del wd
+    m = make_module(E, H, I, gp, gs, gt.float(), dp, ds, dt.float())
+    return m
+
+
+def oracle_module(m, experts):
+    """Oracle view holding only the experts that the routing touches."""
+    sel = sorted(set(int(e) for e in experts))
+    remap = {e: i for i, e in enumerate(sel)}
+    ix = torch.tensor(sel, device="cuda")
+    om = OM.NVFP4Experts(u8(m.gate_up_proj[ix]), u8(m.gate_up_proj_scale[ix]), float(m.gate_up_proj_scale_2),
+                         u8(m.down_proj[ix]), u8(m.down_proj_scale[ix]), float(m.down_proj_scale_2))
+    return om, remap
+
+
+@pytest.mark.parametrize("B,seed", [(1, 0), (1, 1), (1, 2), (4, 3), (16, 4)])
+def test_full_size_vs_oracle(full_layer, B, seed):
+    m = full_layer
+    h = randn_bf16((B, 2816), 1.0, 200 + seed)
+    idx, w = routing(B, 128, 8, 300 + seed)
+    y = m(h, idx.cuda(), w.cuda())
+    om, remap = oracle_module(m, idx.flatten().tolist())
+    idx_r = np.vectorize(remap.get)(idx.numpy())
+    ref = OM.nvfp4_experts_forward(om, bf16_to_np(h), idx_r, bf16_to_np(w))
+    assert max_rel_err(bf16_to_np(y), ref) <= TOL
+
+
+def test_decode_int32_ids_and_repeatable(full_layer):
+    m = full_layer
+    h = randn_bf16((1, 2816), 1.0, 400)
+    idx, w = routing(1, 128, 8, 401)
+    y64 = m(h, idx.cuda(), w.cuda())
+    y32 = m(h, idx.to(torch.int32).cuda(), w.cuda())
+    y64b = m(h, idx.cuda(), w.cuda())
+    assert torch.equal(y64, y32) and torch.equal(y64, y64b)
+
+
+def test_decode_graph_capture(full_layer):
+    m = full_layer
+    h = randn_bf16((1, 2816), 1.0, 500)
+    idx, w = routing(1, 128, 8, 501)
+    idx, w = idx.cuda(), w.cuda()
+    ref = m(h, idx, w)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        m(h, idx, w)
+        with torch.cuda.graph(g, stream=s):
+            out = m(h, idx, w)
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
