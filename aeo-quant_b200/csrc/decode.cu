@@ -25,8 +25,10 @@ namespace aeoq {
 
 constexpr int kDecThreads = 256;
 constexpr int kDecWarps = kDecThreads / 32;
-constexpr int kDownRows = 16;    // output rows per CTA in launch 2
+constexpr int kDownRows = 8;     // output rows per CTA in launch 3
 constexpr int kMaxTopK = 16;
+constexpr int kMaxHidden = 4096;
+constexpr int kQuantThreadsH = 512;
 
 template <int CPL>
 struct RowPair {
@@ -64,6 +66,8 @@ __global__ void __launch_bounds__(kDecThreads, 2) moe_decode_gateup_kernel(
     const uint8_t* __restrict__ gu, const uint8_t* __restrict__ gu_sf, const void* gu_ts, int gu_ts_dt,
     int64_t E, int64_t H, int64_t I, __nv_bfloat16* __restrict__ h_out, uint32_t* __restrict__ parts) {
   __shared__ uint32_t red[32];
+  __shared__ __align__(16) __half2 act_s[kMaxHidden / 16 * 8];
+  __shared__ float sa_s[kMaxHidden / 16];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t total = (int64_t)k * I;
   const int64_t per = (total + gridDim.x - 1) / gridDim.x;
@@ -83,7 +87,8 @@ __global__ void __launch_bounds__(kDecThreads, 2) moe_decode_gateup_kernel(
     load_row_pair<CPL>(cur, gu, gu_sf, cur_e, cur_valid, p - slot * I, I, H, lane);
   }
 
-  // Activation quant: global amax -> tensor scale (bf16) -> lane chunks.
+  // Activation quant, once per CTA: global amax -> bf16 tensor scale ->
+  // one 16-element block per thread, decoded to exact halves in shared memory.
   uint32_t key = 0;
   for (int64_t i = threadIdx.x; i < H / 8; i += blockDim.x) {
     const uint4 u = *reinterpret_cast<const uint4*>(hidden + 8 * i);
@@ -99,12 +104,38 @@ __global__ void __launch_bounds__(kDecThreads, 2) moe_decode_gateup_kernel(
   for (int w = 0; w < kDecWarps; ++w) key = max(key, red[w]);
   const float ts = nvfp4_tensor_scale<AEOQ_BF16>(In<AEOQ_BF16>::key_to_f(key));
   const float alpha = ts * load_scalar_f(gu_ts, gu_ts_dt);
+  for (int64_t b = threadIdx.x; b < H / 16; b += blockDim.x) {
+    float v[16];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const uint4 u = *reinterpret_cast<const uint4*>(hidden + 16 * b + 8 * q);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[8 * q + j] = __bfloat162float(e[j]);
+    }
+    uint32_t w0, w1;
+    const uint32_t sf = nvfp4_quant_block(v, ts, w0, w1);
+    __half2 t[4];
+    fp4x8_to_half2x4_exact(w0, t);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) act_s[8 * b + i] = t[i];
+    fp4x8_to_half2x4_exact(w1, t);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) act_s[8 * b + 4 + i] = t[i];
+    sa_s[b] = e4m3_decode(sf) * 16384.0f;
+  }
+  __syncthreads();
   __half2 act[CPL][16];
   float sa[CPL][2];
 #pragma unroll
   for (int j = 0; j < CPL; ++j) {
     const int64_t c = lane + 32 * j;
-    if (c < nchunk) quant_act_chunk_bf16(hidden + 32 * c, ts, act[j], sa[j]);
+    if (c < nchunk) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) act[j][i] = act_s[16 * c + i];
+      sa[j][0] = sa_s[2 * c];
+      sa[j][1] = sa_s[2 * c + 1];
+    }
   }
   pdl_trigger();
 
@@ -149,9 +180,44 @@ __global__ void __launch_bounds__(kDecThreads, 2) moe_decode_gateup_kernel(
   }
 }
 
+// Launch 2: the shared-scale re-quant of the k x I GeGLU output
+// (modeling_nvfp4.py:164-172). One CTA: reduce the per-CTA amax keys of
+// launch 1, then one 16-element block per thread into the workspace.
+__global__ void __launch_bounds__(kQuantThreadsH) moe_decode_hquant_kernel(
+    const __nv_bfloat16* __restrict__ h, const uint32_t* __restrict__ parts, int nparts, int64_t n,
+    uint8_t* __restrict__ hq, uint8_t* __restrict__ hsf, float* __restrict__ hts) {
+  __shared__ uint32_t red[kQuantThreadsH / 32];
+  pdl_trigger();
+  pdl_wait();
+  uint32_t key = 0;
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) key = max(key, parts[i]);
+  key = warp_umax(key);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = key;
+  __syncthreads();
+  key = 0;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) key = max(key, red[w]);
+  const float ts = nvfp4_tensor_scale<AEOQ_BF16>(In<AEOQ_BF16>::key_to_f(key));
+  if (threadIdx.x == 0) *hts = ts;
+  for (int64_t b = threadIdx.x; b < n / 16; b += blockDim.x) {
+    float v[16];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const uint4 u = *reinterpret_cast<const uint4*>(h + 16 * b + 8 * q);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[8 * q + j] = __bfloat162float(e[j]);
+    }
+    uint32_t w0, w1;
+    hsf[b] = (uint8_t)nvfp4_quant_block(v, ts, w0, w1);
+    *reinterpret_cast<uint2*>(hq + 8 * b) = make_uint2(w0, w1);
+  }
+}
+
+// Launch 3: down GEMV + weighted combine. CTA per kDownRows output rows,
+// warp per slot; weight rows are prefetched before the dependency wait.
 template <int CPL2>
-__global__ void __launch_bounds__(kDecThreads) moe_decode_down_kernel(
-    const __nv_bfloat16* __restrict__ h, const uint32_t* __restrict__ parts, int nparts,
+__global__ void __launch_bounds__(kDecThreads, 2) moe_decode_down_kernel(
+    const uint8_t* __restrict__ hq, const uint8_t* __restrict__ hsf, const float* __restrict__ hts,
     const void* __restrict__ ids, int ids_dt, const __nv_bfloat16* __restrict__ topw, int k,
     const uint8_t* __restrict__ dw, const uint8_t* __restrict__ dw_sf, const void* d_ts, int d_ts_dt,
     int64_t E, int64_t H, int64_t I, __nv_bfloat16* __restrict__ out) {
@@ -186,19 +252,16 @@ __global__ void __launch_bounds__(kDecThreads) moe_decode_down_kernel(
       pdl_wait();
       waited = true;
     }
-    // shared tensor scale of the k x I intermediate (one amax key per launch-1 CTA)
-    uint32_t key = 0;
-    for (int i = lane; i < nparts; i += 32) key = max(key, parts[i]);
-    key = warp_umax(key);
-    const float ts = nvfp4_tensor_scale<AEOQ_BF16>(In<AEOQ_BF16>::key_to_f(key));
-    const float alpha = ts * load_scalar_f(d_ts, d_ts_dt);
+    const float alpha = *hts * load_scalar_f(d_ts, d_ts_dt);
     const float wj = __bfloat162float(topw[j]);
     __half2 act[CPL2][16];
     float sa[CPL2][2];
 #pragma unroll
     for (int q = 0; q < CPL2; ++q) {
       const int64_t c = lane + 32 * q;
-      if (c < nchunk) quant_act_chunk_bf16(h + j * I + 32 * c, ts, act[q], sa[q]);
+      if (c < nchunk)
+        decode_act_chunk(*reinterpret_cast<const uint4*>(hq + j * rb + 16 * c),
+                         *reinterpret_cast<const uint16_t*>(hsf + j * sb + 2 * c), act[q], sa[q]);
     }
 #pragma unroll
     for (int r = 0; r < kDownRows; ++r) {
@@ -238,50 +301,81 @@ static int gateup_grid(int64_t k, int64_t I) {
   return (int)(want < cap ? want : cap);
 }
 
+struct DecodeWs {
+  __nv_bfloat16* h;
+  uint32_t* parts;
+  uint8_t* hq;
+  uint8_t* hsf;
+  float* hts;
+  size_t bytes;
+};
+
+static size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+static DecodeWs decode_ws(void* base, int64_t k, int64_t I) {
+  char* p = reinterpret_cast<char*>(base);
+  DecodeWs w{};
+  size_t off = 0;
+  w.h = reinterpret_cast<__nv_bfloat16*>(p + off); off += align256((size_t)(k * I) * 2);
+  w.parts = reinterpret_cast<uint32_t*>(p + off); off += align256((size_t)gateup_grid(k, I) * 4);
+  w.hq = reinterpret_cast<uint8_t*>(p + off); off += align256((size_t)(k * I) / 2);
+  w.hsf = reinterpret_cast<uint8_t*>(p + off); off += align256((size_t)(k * I) / 16);
+  w.hts = reinterpret_cast<float*>(p + off); off += 256;
+  w.bytes = off;
+  return w;
+}
+
 }  // namespace aeoq
 
 using namespace aeoq;
 
 extern "C" size_t aeoq_moe_nvfp4_decode_workspace_size(int64_t top_k, int64_t hidden, int64_t inter) {
   (void)hidden;
-  const size_t h_bytes = ((size_t)(top_k * inter) * 2 + 255) / 256 * 256;
-  return h_bytes + (size_t)gateup_grid(top_k, inter) * sizeof(uint32_t);
+  return decode_ws(nullptr, top_k, inter).bytes;
 }
 
-// stages: bit 0 = gate_up launch, bit 1 = down launch (both for the fused op)
-template <int CPL, int CPL2>
-static int launch_decode(int stages, const void* hidden, const void* ids, int ids_dt, const void* topw, int k,
-                         const uint8_t* gu, const uint8_t* gu_sf, const void* gu_ts, int gu_ts_dt,
-                         const uint8_t* dw, const uint8_t* dw_sf, const void* d_ts, int d_ts_dt,
-                         int64_t E, int64_t H, int64_t I, void* out, void* ws, cudaStream_t st) {
-  const int g1 = gateup_grid(k, I);
-  const size_t h_bytes = ((size_t)(k * I) * 2 + 255) / 256 * 256;
-  __nv_bfloat16* hbuf = reinterpret_cast<__nv_bfloat16*>(ws);
-  uint32_t* parts = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(ws) + h_bytes);
-  if (stages & 1) {
-    moe_decode_gateup_kernel<CPL><<<g1, kDecThreads, 0, st>>>(
-        reinterpret_cast<const __nv_bfloat16*>(hidden), ids, ids_dt, k, gu, gu_sf, gu_ts, gu_ts_dt, E, H, I,
-        hbuf, parts);
-    int rc = check_launch("moe_decode_gateup_kernel");
-    if (rc) return rc;
-  }
-  if (!(stages & 2)) return AEOQ_OK;
-
+template <typename... KArgs, typename... Args>
+static int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, const char* name,
+                      Args... args) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((H + kDownRows - 1) / kDownRows));
-  cfg.blockDim = dim3(kDecThreads);
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, moe_decode_down_kernel<CPL2>, (const __nv_bfloat16*)hbuf,
-                                     (const uint32_t*)parts, g1, ids, ids_dt,
-                                     reinterpret_cast<const __nv_bfloat16*>(topw), k, dw, dw_sf, d_ts,
-                                     d_ts_dt, E, H, I, reinterpret_cast<__nv_bfloat16*>(out));
-  if (e != cudaSuccess) return set_error(AEOQ_ERR_CUDA, "moe_decode_down_kernel: %s", cudaGetErrorString(e));
-  return check_launch("moe_decode_down_kernel");
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+  if (e != cudaSuccess) return set_error(AEOQ_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
+  return check_launch(name);
+}
+
+// stages: bit 0 = gate_up launch, bit 1 = re-quant + down launches
+template <int CPL, int CPL2>
+static int launch_decode(int stages, const void* hidden, const void* ids, int ids_dt, const void* topw, int k,
+                         const uint8_t* gu, const uint8_t* gu_sf, const void* gu_ts, int gu_ts_dt,
+                         const uint8_t* dw, const uint8_t* dw_sf, const void* d_ts, int d_ts_dt,
+                         int64_t E, int64_t H, int64_t I, void* out, void* wsp, cudaStream_t st) {
+  const int g1 = gateup_grid(k, I);
+  DecodeWs ws = decode_ws(wsp, k, I);
+  if (stages & 1) {
+    moe_decode_gateup_kernel<CPL><<<g1, kDecThreads, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(hidden), ids, ids_dt, k, gu, gu_sf, gu_ts, gu_ts_dt, E, H, I,
+        ws.h, ws.parts);
+    int rc = check_launch("moe_decode_gateup_kernel");
+    if (rc) return rc;
+  }
+  if (!(stages & 2)) return AEOQ_OK;
+  int rc = launch_pdl(moe_decode_hquant_kernel, dim3(1), dim3(kQuantThreadsH), st, "moe_decode_hquant_kernel",
+                      (const __nv_bfloat16*)ws.h, (const uint32_t*)ws.parts, g1, (int64_t)(k * I), ws.hq, ws.hsf,
+                      ws.hts);
+  if (rc) return rc;
+  return launch_pdl(moe_decode_down_kernel<CPL2>, dim3((unsigned)((H + kDownRows - 1) / kDownRows)),
+                    dim3(kDecThreads), st, "moe_decode_down_kernel", (const uint8_t*)ws.hq,
+                    (const uint8_t*)ws.hsf, (const float*)ws.hts, ids, ids_dt,
+                    reinterpret_cast<const __nv_bfloat16*>(topw), k, dw, dw_sf, d_ts, d_ts_dt, E, H, I,
+                    reinterpret_cast<__nv_bfloat16*>(out));
 }
 
 static int decode_entry(int stages, const void* hidden, const void* top_k_index, int idx_dtype,

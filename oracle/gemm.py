@@ -22,13 +22,18 @@ from .numerics import F32, bf16, e4m3_decode
 from .quant import dequant_nvfp4_unscaled, quantize_nvfp4
 
 
-def nvfp4_gemm(a_packed, a_sf, a_ts, w_packed, w_sf, w_ts):
-    """``nvfp4_linear_prequantized`` semantics (nvfp4_matmul.py:399-519)."""
+def nvfp4_gemm(a_packed, a_sf, a_ts, w_packed, w_sf, w_ts, out="bf16"):
+    """``nvfp4_linear_prequantized`` semantics (nvfp4_matmul.py:399-519).
+
+    ``out="f32"`` returns the float32 epilogue value (the ``out_dtype=float32``
+    path of the reference launchers) instead of rounding it to bf16.
+    """
     a = dequant_nvfp4_unscaled(a_packed, a_sf).astype(np.float64)
     w = dequant_nvfp4_unscaled(w_packed, w_sf).astype(np.float64)
     acc = (a @ w.T).astype(F32)
     alpha = F32(F32(a_ts) * F32(w_ts))
-    return bf16(acc * alpha)
+    y = (acc * alpha).astype(F32)
+    return y if out == "f32" else bf16(y)
 
 
 def nvfp4_linear(x, w_packed, w_sf, w_ts, dtype: str = "bf16"):
