@@ -19,6 +19,8 @@
 //     amax keys to the shared tensor scale of (:164-172), quantizes its
 //     chunk of h, finishes the GEMV, and combines the k slots as
 //     bf16(sum_j bf16(bf16(a*d_j) * w_j)) (:174-186).
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace aeoq {
@@ -184,13 +186,15 @@ __global__ void __launch_bounds__(kDecThreads, 2) moe_decode_gateup_kernel(
 // (modeling_nvfp4.py:164-172). One CTA: reduce the per-CTA amax keys of
 // launch 1, then one 16-element block per thread into the workspace.
 __global__ void __launch_bounds__(kQuantThreadsH) moe_decode_hquant_kernel(
-    const __nv_bfloat16* __restrict__ h, const uint32_t* __restrict__ parts, int nparts, int64_t n,
+    const __nv_bfloat16* h, const uint32_t* parts, int nparts, int64_t n,
     uint8_t* __restrict__ hq, uint8_t* __restrict__ hsf, float* __restrict__ hts) {
   __shared__ uint32_t red[kQuantThreadsH / 32];
   pdl_trigger();
   pdl_wait();
+  // Data written by the preceding grid is read with L2-coherent loads
+  // (ld.global.cg): this grid may have started before those writes.
   uint32_t key = 0;
-  for (int i = threadIdx.x; i < nparts; i += blockDim.x) key = max(key, parts[i]);
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) key = max(key, __ldcg(parts + i));
   key = warp_umax(key);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = key;
   __syncthreads();
@@ -202,7 +206,7 @@ __global__ void __launch_bounds__(kQuantThreadsH) moe_decode_hquant_kernel(
     float v[16];
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
-      const uint4 u = *reinterpret_cast<const uint4*>(h + 16 * b + 8 * q);
+      const uint4 u = __ldcg(reinterpret_cast<const uint4*>(h + 16 * b + 8 * q));
       const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[8 * q + j] = __bfloat162float(e[j]);
@@ -217,7 +221,7 @@ __global__ void __launch_bounds__(kQuantThreadsH) moe_decode_hquant_kernel(
 // warp per slot; weight rows are prefetched before the dependency wait.
 template <int CPL2>
 __global__ void __launch_bounds__(kDecThreads, 2) moe_decode_down_kernel(
-    const uint8_t* __restrict__ hq, const uint8_t* __restrict__ hsf, const float* __restrict__ hts,
+    const uint8_t* hq, const uint8_t* hsf, const float* hts,
     const void* __restrict__ ids, int ids_dt, const __nv_bfloat16* __restrict__ topw, int k,
     const uint8_t* __restrict__ dw, const uint8_t* __restrict__ dw_sf, const void* d_ts, int d_ts_dt,
     int64_t E, int64_t H, int64_t I, __nv_bfloat16* __restrict__ out) {
@@ -252,7 +256,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) moe_decode_down_kernel(
       pdl_wait();
       waited = true;
     }
-    const float alpha = *hts * load_scalar_f(d_ts, d_ts_dt);
+    const float alpha = __ldcg(hts) * load_scalar_f(d_ts, d_ts_dt);
     const float wj = __bfloat162float(topw[j]);
     __half2 act[CPL2][16];
     float sa[CPL2][2];
@@ -260,8 +264,8 @@ __global__ void __launch_bounds__(kDecThreads, 2) moe_decode_down_kernel(
     for (int q = 0; q < CPL2; ++q) {
       const int64_t c = lane + 32 * q;
       if (c < nchunk)
-        decode_act_chunk(*reinterpret_cast<const uint4*>(hq + j * rb + 16 * c),
-                         *reinterpret_cast<const uint16_t*>(hsf + j * sb + 2 * c), act[q], sa[q]);
+        decode_act_chunk(__ldcg(reinterpret_cast<const uint4*>(hq + j * rb + 16 * c)),
+                         __ldcg(reinterpret_cast<const unsigned short*>(hsf + j * sb + 2 * c)), act[q], sa[q]);
     }
 #pragma unroll
     for (int r = 0; r < kDownRows; ++r) {
@@ -334,6 +338,16 @@ extern "C" size_t aeoq_moe_nvfp4_decode_workspace_size(int64_t top_k, int64_t hi
   return decode_ws(nullptr, top_k, inter).bytes;
 }
 
+// Programmatic dependent launch can be switched off with AEOQ_NO_PDL=1
+// (plain stream order; used to isolate ordering issues).
+static bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("AEOQ_NO_PDL");
+    return !(v && v[0] == '1');
+  }();
+  return on;
+}
+
 template <typename... KArgs, typename... Args>
 static int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, const char* name,
                       Args... args) {
@@ -345,7 +359,7 @@ static int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
   if (e != cudaSuccess) return set_error(AEOQ_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
   return check_launch(name);

@@ -88,42 +88,50 @@ class ClockSampler:
         self.gpu = str(gpu_index)
         self.rows = []
         self.proc = None
-        self.thread = None
+        self.path = f"/tmp/aeoq_clocks_{os.getpid()}.csv"
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100", "-f", self.path],
+                                         stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
         except Exception:
             self.proc = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
-
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
-            self.thread.join(timeout=2)
+        if not self.proc:
+            return
+        time.sleep(0.2)
+        self.proc.send_signal(2)
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        try:
+            with open(self.path) as f:
+                self.rows = [[c.strip() for c in line.split(",")] for line in f if line.strip()]
+            os.remove(self.path)
+        except Exception:
+            self.rows = []
 
     def summary(self):
-        if not self.rows:
+        rows = [r for r in self.rows if len(r) > 8]
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [v for v in (num(r[1]) for r in rows) if v is not None]
+        mx = [v for v in (num(r[2]) for r in rows) if v is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows if len(r) > 8 for i in range(4)
-                          if r[5 + i].lower().startswith("active")})
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+                "reasons": reasons, "samples": len(rows)}
 
 
 def make_layers(torch, L, device, seed=0):
@@ -296,13 +304,22 @@ def main():
     stage_ms = {}
     if B == 1:
         for name, fn in (("gate_up", lib.aeoq_moe_nvfp4_decode_gate_up), ("down", lib.aeoq_moe_nvfp4_decode_down)):
-            for s in range(W):
-                A.check(stage(fn, s))
+            sg = torch.cuda.Stream(dev)
+            sg.wait_stream(torch.cuda.current_stream(dev))
+            g2 = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(sg):
+                for s in range(3):
+                    A.check(stage(fn, s))
+                with torch.cuda.graph(g2, stream=sg):
+                    for s in range(K):
+                        A.check(stage(fn, W + s))
+            torch.cuda.current_stream(dev).wait_stream(sg)
+            torch.cuda.synchronize()
+            g2.replay()
             torch.cuda.synchronize()
             a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a0.record()
-            for s in range(K):
-                A.check(stage(fn, W + s))
+            g2.replay()
             a1.record()
             torch.cuda.synchronize()
             stage_ms[name] = a0.elapsed_time(a1) / K
@@ -352,7 +369,7 @@ def main():
                     "traffic": NCU_TRAFFIC_GATEUP, "algorithmic_bytes": alg,
                     "launch_us": round(stage_ms["gate_up"] * 1000, 3)}
             alg_d = TOPK * DOWN_BYTES + TOPK * I * 2 + H * 2
-            roof["down_kernel"] = {"kernel": "moe_decode_down_kernel", "launch_us": round(stage_ms["down"] * 1000, 3),
+            roof["down_kernel"] = {"kernel": "moe_decode_hquant_kernel + moe_decode_down_kernel", "launch_us": round(stage_ms["down"] * 1000, 3),
                                    "achieved": round(alg_d / (stage_ms["down"] / 1000.0) / 1e9, 1),
                                    "algorithmic_bytes": alg_d}
         step_bytes = TOPK * EXPERT_BYTES + 2 * H * 2
@@ -367,7 +384,7 @@ def main():
                        f"{L * 428} MB resident, 26.8 MB streamed per step",
                        "parallelism": f"replicas x{world}", "timing": "one CUDA graph of K steps, CUDA events"},
             "step_hbm_gbs": round(step_bytes / (ms_max / K / 1000.0) / 1e9, 1),
-            "gpu_launches": 2 * K,
+            "gpu_launches": 3 * K,
             "clocks": clk.summary(),
             "e2e": {"value": round(e2e_val, 1), "unit": "tok/s", "steps": n_e2e,
                     "h2d_bytes_per_step": B * H * 2 + B * TOPK * 8 + B * TOPK * 2,
