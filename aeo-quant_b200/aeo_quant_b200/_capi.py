@@ -39,8 +39,12 @@ _SIGS = {
 }
 _SIGS["aeoq_moe_nvfp4_decode_gate_up"] = _SIGS["aeoq_moe_nvfp4_decode"]
 _SIGS["aeoq_moe_nvfp4_decode_down"] = _SIGS["aeoq_moe_nvfp4_decode"]
+_SIGS["aeoq_moe_nvfp4_decode_fused"] = _SIGS["aeoq_moe_nvfp4_decode"]
+_SIGS["aeoq_moe_nvfp4_decode_fused_supported"] = [_L, _L, _L]
+_SIGS["aeoq_moe_nvfp4_decode_fused_workspace_size"] = [_L, _L, _L]
 _RESTYPE = {"aeoq_last_error": C.c_char_p, "aeoq_nvfp4_quantize_workspace_size": C.c_size_t,
-            "aeoq_moe_nvfp4_decode_workspace_size": C.c_size_t}
+            "aeoq_moe_nvfp4_decode_workspace_size": C.c_size_t,
+            "aeoq_moe_nvfp4_decode_fused_workspace_size": C.c_size_t}
 
 _lib = None
 

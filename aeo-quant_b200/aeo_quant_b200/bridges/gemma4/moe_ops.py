@@ -14,8 +14,25 @@ from ...gpu import nvfp4_matmul as NM
 from ...gpu.quant import quantize_2d_to_nvfp4
 
 
-def nvfp4_decode(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf, dw_ts):
-    """One-token forward (modeling_nvfp4.py:132-186) in two fused launches."""
+_FUSED_WS: dict = {}
+
+
+def _fused_workspace(lib, device, k, H, I):
+    """Zero-initialised workspace of the cooperative decode kernel, one per
+    (device, shape). The kernel leaves its counters zero on exit, so the
+    buffer is reused by every stream-ordered call (not by overlapping ones)."""
+    key = (device.index, k, H, I)
+    ws = _FUSED_WS.get(key)
+    if ws is None:
+        n = lib.aeoq_moe_nvfp4_decode_fused_workspace_size(k, H, I)
+        ws = torch.zeros(n, dtype=torch.uint8, device=device)
+        _FUSED_WS[key] = ws
+    return ws
+
+
+def nvfp4_decode(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf, dw_ts, fused=None):
+    """One-token forward (modeling_nvfp4.py:132-186): one cooperative kernel
+    when the shape fits its shared-memory plan, else three chained launches."""
     A.require_cuda(hidden, top_k_index, top_k_weights, gu, dw)
     lib = A.load()
     if hidden.dtype != torch.bfloat16:
@@ -29,9 +46,16 @@ def nvfp4_decode(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf
     idx = top_k_index.reshape(-1)[:k].contiguous()
     w = top_k_weights.reshape(-1)[:k].to(torch.bfloat16).contiguous()
     out = torch.empty(1, H, dtype=torch.bfloat16, device=hidden.device)
-    ws_n = lib.aeoq_moe_nvfp4_decode_workspace_size(k, H, I)
-    ws = torch.empty(ws_n, dtype=torch.uint8, device=hidden.device)
-    A.check(lib.aeoq_moe_nvfp4_decode(
+    if fused is None:
+        fused = bool(lib.aeoq_moe_nvfp4_decode_fused_supported(k, H, I))
+    if fused:
+        ws = _fused_workspace(lib, hidden.device, k, H, I)
+        fn, ws_n = lib.aeoq_moe_nvfp4_decode_fused, ws.numel()
+    else:
+        ws_n = lib.aeoq_moe_nvfp4_decode_workspace_size(k, H, I)
+        ws = torch.empty(ws_n, dtype=torch.uint8, device=hidden.device)
+        fn = lib.aeoq_moe_nvfp4_decode
+    A.check(fn(
         hidden.data_ptr(), idx.data_ptr(), A.dtype_code(idx.dtype), w.data_ptr(), k,
         gu.data_ptr(), gu_sf.data_ptr(), gu_ts.data_ptr(), A.dtype_code(gu_ts.dtype),
         dw.data_ptr(), dw_sf.data_ptr(), dw_ts.data_ptr(), A.dtype_code(dw_ts.dtype),

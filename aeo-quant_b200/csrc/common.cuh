@@ -304,3 +304,77 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 }  // namespace aeoq
+
+namespace aeoq {
+
+// ---------------------------------------------------------------------------
+// FP4 -> exact fp16 via the hardware converter (cvt.rn.f16x2.e2m1x2): byte b
+// of w becomes h[b] = (low nibble, high nibble) = (element 2b+1, element 2b).
+// Activations and weights decoded with this routine pair element-for-element.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void fp4x8_to_half2x4(uint32_t w, __half2 (&h)[4]) {
+  uint32_t r0, r1, r2, r3;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+      : "r"(w));
+  h[0] = *reinterpret_cast<__half2*>(&r0);
+  h[1] = *reinterpret_cast<__half2*>(&r1);
+  h[2] = *reinterpret_cast<__half2*>(&r2);
+  h[3] = *reinterpret_cast<__half2*>(&r3);
+}
+
+// One 16-byte chunk (two 16-value blocks) of exact activation halves `a`
+// (with per-block scales sa) against a packed weight chunk. Within a block,
+// each fp16 lane sums 8 products of E2M1 values (multiples of 1/4, |sum| <=
+// 288): exact in fp16. The block sum times the two e4m3 scales is exact in
+// fp32; only the running sum across blocks rounds.
+__device__ __forceinline__ float chunk_dot_x(const __half2 (&a)[16], const float (&sa)[2], uint4 w,
+                                             uint16_t wsf, float acc) {
+  const float2 sw = __half22float2(e4m3x2_to_half2(wsf));
+  const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int b = 0; b < 2; ++b) {
+    __half2 h = __float2half2_rn(0.0f);
+    __half2 d[4];
+    fp4x8_to_half2x4(words[2 * b], d);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h = __hfma2(a[8 * b + i], d[i], h);
+    fp4x8_to_half2x4(words[2 * b + 1], d);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h = __hfma2(a[8 * b + 4 + i], d[i], h);
+    const float2 f = __half22float2(h);
+    acc = fmaf(f.x + f.y, sa[b] * (b ? sw.y : sw.x), acc);
+  }
+  return acc;
+}
+
+// Packed activation chunk -> exact halves + block scales for chunk_dot_x.
+__device__ __forceinline__ void decode_act_chunk_x(uint4 p, uint16_t sf2, __half2 (&a)[16], float (&sa)[2]) {
+  const uint32_t words[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 t[4];
+    fp4x8_to_half2x4(words[i], t);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) a[4 * i + j] = t[j];
+  }
+  const float2 s = __half22float2(e4m3x2_to_half2(sf2));
+  sa[0] = s.x;
+  sa[1] = s.y;
+}
+
+// ---------------------------------------------------------------- bulk copy
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          (uint32_t)__cvta_generic_to_shared(dst)),
+      "l"(src), "r"(bytes), "r"((uint32_t)__cvta_generic_to_shared(bar))
+      : "memory");
+}
+
+}  // namespace aeoq

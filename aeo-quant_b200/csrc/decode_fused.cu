@@ -1,0 +1,412 @@
+// One-token NVFP4 MoE expert forward as ONE persistent cooperative kernel.
+//
+// Restates Gemma4TextExpertsNVFP4._forward_decode_3d (aeo_quant
+// src/aeo_quant/bridges/gemma4/modeling_nvfp4.py:132-186). At one token the
+// cost is streaming the k selected experts' packed weights (26.8 MB for
+// Gemma-4-26B-A4B: k=8, H=2816, I=704), so the kernel is organised around
+// HBM, not arithmetic:
+//
+//  1. Each of the G = #SM CTAs owns a contiguous slice of the k*I gate/up
+//     row pairs and a slice of the H down rows (for all k slots). At entry
+//     one thread issues cp.async.bulk copies of the whole slice into shared
+//     memory (~180 KB per CTA), so every SM streams from HBM from t = 0.
+//  2. Meanwhile the CTA quantizes the hidden vector (global amax, bf16 tensor
+//     scale, per-16 e4m3 scales, E2M1 nibbles: quantize_2d_to_nvfp4, :150-153)
+//     into exact fp16 operands in shared memory.
+//  3. gate/up dot products from shared memory (fp16 exact per 16-block, f32
+//     across blocks), GeGLU in bf16 (:155-162); h goes to global memory and
+//     the CTA's |h| maximum to a per-CTA slot.
+//  4. One grid barrier (bounded spin on an arrival counter; cooperative launch
+//     guarantees co-residency). Every CTA then reduces the G maxima to the
+//     shared tensor scale (:164-172) and re-quantizes all of h itself.
+//  5. down dot products from shared memory, bf16(bf16(a*d_j) * w_j), summed
+//     over the k slots and rounded once (:174-186).
+// The counters self-reset: the last CTA to leave zeroes them, so a zeroed
+// workspace stays valid call after call on one stream.
+#include <cstdlib>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace aeoq {
+
+constexpr int kFThreads = 512;
+constexpr int kFWarps = kFThreads / 32;
+constexpr int kFMaxTopK = 16;
+constexpr int kFMaxDownRows = 32;
+constexpr int kSmemCap = 232448;   // 227 KB dynamic shared memory per CTA
+
+struct FusedShape {
+  int64_t E, H, I;
+  int k, G;
+  int ppc;      // gate/up row pairs per CTA
+  int rpc;      // down rows per CTA
+  size_t off_gate, off_up, off_gsf, off_usf, off_dn, off_dsf, off_act, off_asa, off_hact, off_hsa, off_prod,
+      bytes;
+};
+
+__host__ __device__ inline size_t al128(size_t v) { return (v + 127) / 128 * 128; }
+
+__host__ __device__ inline FusedShape fused_shape(int64_t E, int64_t H, int64_t I, int k, int G) {
+  FusedShape s{};
+  s.E = E; s.H = H; s.I = I; s.k = k; s.G = G;
+  s.ppc = (int)((k * I + G - 1) / G);
+  s.rpc = (int)((H + G - 1) / G);
+  const size_t rb = H / 2, sb = H / 16, rb2 = I / 2, sb2 = I / 16;
+  size_t o = 0;
+  s.off_gate = o; o = al128(o + s.ppc * rb);
+  s.off_up = o;   o = al128(o + s.ppc * rb);
+  s.off_gsf = o;  o = al128(o + s.ppc * sb);
+  s.off_usf = o;  o = al128(o + s.ppc * sb);
+  s.off_dn = o;   o = al128(o + (size_t)s.rpc * k * rb2);
+  s.off_dsf = o;  o = al128(o + (size_t)s.rpc * k * sb2);
+  s.off_act = o;  o = al128(o + (H / 16) * 8 * sizeof(__half2));
+  s.off_asa = o;  o = al128(o + (H / 16) * sizeof(float));
+  s.off_hact = o; o = al128(o + (k * I / 16) * 8 * sizeof(__half2));
+  s.off_hsa = o;  o = al128(o + (k * I / 16) * sizeof(float));
+  s.off_prod = o; o = al128(o + (size_t)kFMaxTopK * kFMaxDownRows * sizeof(float));
+  s.bytes = o + 128;   // two mbarriers
+  return s;
+}
+
+struct FusedArgs {
+  const __nv_bfloat16* hidden;
+  const void* ids; int ids_dt;
+  const __nv_bfloat16* topw;
+  const uint8_t* gu; const uint8_t* gu_sf; const void* gu_ts; int gu_ts_dt;
+  const uint8_t* dw; const uint8_t* dw_sf; const void* d_ts; int d_ts_dt;
+  __nv_bfloat16* out;
+  __nv_bfloat16* h;      // k*I bf16 intermediate
+  uint32_t* parts;       // G amax keys
+  uint32_t* sync;        // [0] arrivals, [1] departures, [2] error code
+};
+
+// Quantize 16 bf16 values (global, written by other CTAs -> L2-coherent
+// loads when `coherent`) and store exact halves + scale into shared memory.
+template <bool kCoherent>
+__device__ __forceinline__ void quant_block_to_smem(const __nv_bfloat16* src, float ts, __half2* dst, float* sa) {
+  float v[16];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const uint4 u = kCoherent ? __ldcg(reinterpret_cast<const uint4*>(src + 8 * q))
+                              : *reinterpret_cast<const uint4*>(src + 8 * q);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[8 * q + j] = __bfloat162float(e[j]);
+  }
+  uint32_t w0, w1;
+  const uint32_t sf = nvfp4_quant_block(v, ts, w0, w1);
+  __half2 t[4];
+  fp4x8_to_half2x4(w0, t);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[i] = t[i];
+  fp4x8_to_half2x4(w1, t);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[4 + i] = t[i];
+  *sa = e4m3_decode(sf);
+}
+
+__global__ void __launch_bounds__(kFThreads, 1) moe_decode_fused_kernel(FusedArgs a, FusedShape s) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ uint32_t red[kFWarps];
+  uint64_t* bar_gu = reinterpret_cast<uint64_t*>(smem + s.bytes - 128);
+  uint64_t* bar_dn = bar_gu + 1;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t H = s.H, I = s.I;
+  const int k = s.k;
+  const size_t rb = H / 2, sb = H / 16, rb2 = I / 2, sb2 = I / 16;
+  const int64_t p0 = (int64_t)blockIdx.x * s.ppc;
+  const int64_t p1 = min((int64_t)k * I, p0 + s.ppc);
+  const int np = (int)max((int64_t)0, p1 - p0);
+  const int64_t r0 = (int64_t)blockIdx.x * s.rpc;
+  const int nr = (int)max((int64_t)0, min(H, r0 + s.rpc) - r0);
+  uint8_t* gate_s = smem + s.off_gate;
+  uint8_t* up_s = smem + s.off_up;
+  uint8_t* gsf_s = smem + s.off_gsf;
+  uint8_t* usf_s = smem + s.off_usf;
+  uint8_t* dn_s = smem + s.off_dn;
+  uint8_t* dsf_s = smem + s.off_dsf;
+  __half2* act_s = reinterpret_cast<__half2*>(smem + s.off_act);
+  float* asa_s = reinterpret_cast<float*>(smem + s.off_asa);
+  __half2* hact_s = reinterpret_cast<__half2*>(smem + s.off_hact);
+  float* hsa_s = reinterpret_cast<float*>(smem + s.off_hsa);
+  float* prod_s = reinterpret_cast<float*>(smem + s.off_prod);
+  int* err = reinterpret_cast<int*>(a.sync + 2);
+
+  // ---- 1. issue every weight copy of this CTA's slice -------------------
+  if (tid == 0) {
+    sm100::mbar_init(bar_gu, 1);
+    sm100::mbar_init(bar_dn, 1);
+    sm100::fence_barrier_init();
+    uint32_t gu_bytes = (uint32_t)(np * (2 * rb + 2 * sb));
+    uint32_t dn_bytes = (uint32_t)((size_t)nr * k * rb2);
+    sm100::mbar_arrive_expect_tx(bar_gu, gu_bytes);
+    sm100::mbar_arrive_expect_tx(bar_dn, dn_bytes);
+    // gate/up rows: the pair range spans at most a few slots; copy per segment
+    int64_t p = p0;
+    int dst = 0;
+    while (p < p1) {
+      const int64_t slot = p / I, n = p - slot * I;
+      const int64_t len = min(p1 - p, I - n);
+      const int64_t e = load_index(a.ids, a.ids_dt, slot);
+      if (e >= 0 && e < s.E) {
+        const uint8_t* g = a.gu + (e * 2 * I + n) * rb;
+        const uint8_t* gs = a.gu_sf + (e * 2 * I + n) * sb;
+        bulk_g2s(gate_s + dst * rb, g, (uint32_t)(len * rb), bar_gu);
+        bulk_g2s(up_s + dst * rb, g + I * rb, (uint32_t)(len * rb), bar_gu);
+        bulk_g2s(gsf_s + dst * sb, gs, (uint32_t)(len * sb), bar_gu);
+        bulk_g2s(usf_s + dst * sb, gs + I * sb, (uint32_t)(len * sb), bar_gu);
+      } else {
+        // invalid expert id: no copy; account for the bytes so the barrier completes
+        asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(sm100::smem_u32(bar_gu)),
+                     "r"((uint32_t)(len * (2 * rb + 2 * sb)))
+                     : "memory");
+      }
+      dst += (int)len;
+      p += len;
+    }
+    for (int j = 0; j < k && nr > 0; ++j) {
+      const int64_t e = load_index(a.ids, a.ids_dt, j);
+      if (e >= 0 && e < s.E) {
+        bulk_g2s(dn_s + (size_t)j * nr * rb2, a.dw + (e * H + r0) * rb2, (uint32_t)(nr * rb2), bar_dn);
+      } else {
+        asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(sm100::smem_u32(bar_dn)),
+                     "r"((uint32_t)(nr * rb2))
+                     : "memory");
+      }
+    }
+  }
+  // down scale rows (44 B per row: not bulk-copy aligned) with plain loads
+  {
+    const int words = (int)(nr * sb2 / 4);   // per slot
+    for (int idx = tid; idx < k * words; idx += kFThreads) {
+      const int j = idx / words, wdx = idx - j * words;
+      const int64_t e = load_index(a.ids, a.ids_dt, j);
+      uint32_t v = 0;
+      if (e >= 0 && e < s.E)
+        v = *reinterpret_cast<const uint32_t*>(a.dw_sf + (e * H + r0) * sb2 + 4 * wdx);
+      reinterpret_cast<uint32_t*>(dsf_s + (size_t)j * nr * sb2)[wdx] = v;
+    }
+  }
+
+  // ---- 2. hidden quant: amax -> ts -> exact halves in shared memory ----
+  uint32_t key = 0;
+  for (int64_t i = tid; i < H / 8; i += kFThreads) {
+    const uint4 u = *reinterpret_cast<const uint4*>(a.hidden + 8 * i);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) key = max(key, In<AEOQ_BF16>::abs_key(e[j]));
+  }
+  key = warp_umax(key);
+  if (lane == 0) red[warp] = key;
+  __syncthreads();   // also publishes the barrier init and the down scales
+  key = 0;
+#pragma unroll
+  for (int w = 0; w < kFWarps; ++w) key = max(key, red[w]);
+  const float ts = nvfp4_tensor_scale<AEOQ_BF16>(In<AEOQ_BF16>::key_to_f(key));
+  const float alpha = ts * load_scalar_f(a.gu_ts, a.gu_ts_dt);
+  for (int64_t b = tid; b < H / 16; b += kFThreads)
+    quant_block_to_smem<false>(a.hidden + 16 * b, ts, act_s + 8 * b, asa_s + b);
+  __syncthreads();
+
+  // ---- 3. gate/up GEMV + GeGLU ------------------------------------------
+  const int nchunk = (int)(H / 32);
+  uint32_t hkey = 0;
+  const bool ok_gu = sm100::mbar_wait(bar_gu, 0, err, 1);
+  if (ok_gu) {
+    for (int i = warp; i < np; i += kFWarps) {
+      const int64_t slot = (p0 + i) / I;
+      const int64_t e = load_index(a.ids, a.ids_dt, slot);
+      const bool valid = e >= 0 && e < s.E;   // an invalid id contributes zeros
+      float ag = 0.f, au = 0.f;
+      for (int c = lane; c < nchunk && valid; c += 32) {
+        __half2 av[16];
+        const uint4* ap = reinterpret_cast<const uint4*>(act_s + 16 * c);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(&av[4 * q]) = ap[q];
+        const float sa2[2] = {asa_s[2 * c], asa_s[2 * c + 1]};
+        const uint4 gw = *reinterpret_cast<const uint4*>(gate_s + i * rb + 16 * c);
+        const uint4 uw = *reinterpret_cast<const uint4*>(up_s + i * rb + 16 * c);
+        const uint16_t gs = *reinterpret_cast<const uint16_t*>(gsf_s + i * sb + 2 * c);
+        const uint16_t us = *reinterpret_cast<const uint16_t*>(usf_s + i * sb + 2 * c);
+        ag = chunk_dot_x(av, sa2, gw, gs, ag);
+        au = chunk_dot_x(av, sa2, uw, us, au);
+      }
+      ag = warp_sum(ag);
+      au = warp_sum(au);
+      if (lane == 0) {
+        const float g = bf16r(ag * alpha), u = bf16r(au * alpha);
+        const __nv_bfloat16 hv = __float2bfloat16_rn(bf16r(gelu_tanh(g)) * u);
+        a.h[p0 + i] = hv;
+        hkey = max(hkey, In<AEOQ_BF16>::abs_key(hv));
+      }
+    }
+  }
+  hkey = warp_umax(hkey);
+  __threadfence();   // h stores of every writer ordered before the arrival below
+  __syncthreads();
+  if (lane == 0) red[warp] = hkey;
+  __syncthreads();
+
+  // ---- 4. grid barrier ----------------------------------------------------
+  if (tid == 0) {
+    uint32_t m = 0;
+    for (int w = 0; w < kFWarps; ++w) m = max(m, red[w]);
+    a.parts[blockIdx.x] = m;
+    __threadfence();
+    atomicAdd(a.sync + 0, 1u);
+    bool done = false;
+    for (uint32_t it = 0; it < sm100::kSpinLimit; ++it) {
+      uint32_t v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync + 0) : "memory");
+      if (v >= (uint32_t)s.G) { done = true; break; }
+      __nanosleep(64);
+    }
+    if (!done) atomicCAS(err, 0, 2);
+  }
+  __syncthreads();
+
+  // shared tensor scale of h over all CTAs, then re-quantize all of h here
+  uint32_t hk = 0;
+  for (int i = tid; i < s.G; i += kFThreads) hk = max(hk, __ldcg(a.parts + i));
+  hk = warp_umax(hk);
+  if (lane == 0) red[warp] = hk;
+  __syncthreads();
+  hk = 0;
+#pragma unroll
+  for (int w = 0; w < kFWarps; ++w) hk = max(hk, red[w]);
+  const float hts = nvfp4_tensor_scale<AEOQ_BF16>(In<AEOQ_BF16>::key_to_f(hk));
+  const float alpha_d = hts * load_scalar_f(a.d_ts, a.d_ts_dt);
+  for (int64_t b = tid; b < (int64_t)k * I / 16; b += kFThreads)
+    quant_block_to_smem<true>(a.h + 16 * b, hts, hact_s + 8 * b, hsa_s + b);
+  __syncthreads();
+
+  // ---- 5. down GEMV + weighted combine -----------------------------------
+  const bool ok_dn = sm100::mbar_wait(bar_dn, 0, err, 3);
+  const int nchunk2 = (int)(I / 32);
+  if (ok_dn) {
+    for (int it = warp; it < nr * k; it += kFWarps) {
+      const int j = it / nr, r = it - j * nr;
+      const int64_t e = load_index(a.ids, a.ids_dt, j);
+      const bool valid = e >= 0 && e < s.E;
+      float acc = 0.f;
+      for (int c = lane; c < nchunk2 && valid; c += 32) {
+        __half2 av[16];
+        const uint4* ap = reinterpret_cast<const uint4*>(hact_s + (j * (I / 16) + 2 * c) * 8);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(&av[4 * q]) = ap[q];
+        const int hb = (int)(j * (I / 16) + 2 * c);
+        const float sa2[2] = {hsa_s[hb], hsa_s[hb + 1]};
+        const size_t row = (size_t)j * nr + r;
+        const uint4 wv = *reinterpret_cast<const uint4*>(dn_s + row * rb2 + 16 * c);
+        const uint16_t ws = *reinterpret_cast<const uint16_t*>(dsf_s + row * sb2 + 2 * c);
+        acc = chunk_dot_x(av, sa2, wv, ws, acc);
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) prod_s[j * kFMaxDownRows + r] = bf16r(bf16r(acc * alpha_d) * __bfloat162float(a.topw[j]));
+    }
+  }
+  __syncthreads();
+  if (tid < nr) {
+    float acc = 0.f;
+    for (int j = 0; j < k; ++j) acc += prod_s[j * kFMaxDownRows + tid];
+    a.out[r0 + tid] = __float2bfloat16_rn(acc);
+  }
+
+  // ---- departure: the last CTA out resets the counters ------------------
+  if (tid == 0) {
+    const uint32_t d = atomicAdd(a.sync + 1, 1u);
+    if (d == (uint32_t)s.G - 1) {
+      a.sync[0] = 0;
+      a.sync[1] = 0;
+      __threadfence();
+    }
+  }
+}
+
+static int fused_grid() {
+  static int g = 0;
+  if (!g) {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    g = n > 0 ? n : 148;
+  }
+  return g;
+}
+
+}  // namespace aeoq
+
+using namespace aeoq;
+
+// Workspace: [sync 256 B][parts G*4][h k*I bf16], all 256-aligned.
+extern "C" size_t aeoq_moe_nvfp4_decode_fused_workspace_size(int64_t top_k, int64_t hidden, int64_t inter) {
+  (void)hidden;
+  const size_t G = (size_t)fused_grid();
+  return 256 + (G * 4 + 255) / 256 * 256 + ((size_t)(top_k * inter) * 2 + 255) / 256 * 256;
+}
+
+extern "C" int aeoq_moe_nvfp4_decode_fused_supported(int64_t top_k, int64_t hidden, int64_t inter) {
+  if (top_k < 1 || top_k > kFMaxTopK) return 0;
+  if (hidden % 256 != 0 || inter % 64 != 0 || hidden <= 0 || inter <= 0) return 0;
+  const FusedShape s = fused_shape(0, hidden, inter, (int)top_k, fused_grid());
+  if (s.rpc > kFMaxDownRows) return 0;
+  return s.bytes <= (size_t)kSmemCap ? 1 : 0;
+}
+
+extern "C" int aeoq_moe_nvfp4_decode_fused(const void* hidden, const void* top_k_index, int idx_dtype,
+                                           const void* top_k_weights, int64_t top_k, const uint8_t* gate_up,
+                                           const uint8_t* gate_up_sf, const void* gate_up_ts, int gate_up_ts_dtype,
+                                           const uint8_t* down, const uint8_t* down_sf, const void* down_ts,
+                                           int down_ts_dtype, int64_t num_experts, int64_t hidden_dim,
+                                           int64_t inter_dim, void* out, void* workspace, size_t workspace_bytes,
+                                           void* stream) {
+  AEOQ_REQUIRE(aeoq_moe_nvfp4_decode_fused_supported(top_k, hidden_dim, inter_dim), AEOQ_ERR_INVALID,
+               "moe_decode_fused: unsupported shape (top_k=%lld hidden=%lld inter=%lld)", (long long)top_k,
+               (long long)hidden_dim, (long long)inter_dim);
+  AEOQ_REQUIRE(idx_dtype == AEOQ_I32 || idx_dtype == AEOQ_I64, AEOQ_ERR_INVALID,
+               "moe_decode_fused: top_k_index must be int32 or int64");
+  AEOQ_REQUIRE(hidden && top_k_index && top_k_weights && gate_up && gate_up_sf && gate_up_ts && down && down_sf &&
+                   down_ts && out,
+               AEOQ_ERR_INVALID, "moe_decode_fused: null pointer");
+  AEOQ_REQUIRE(((uintptr_t)hidden % 16 == 0) && ((uintptr_t)gate_up % 16 == 0) && ((uintptr_t)down % 16 == 0) &&
+                   ((uintptr_t)gate_up_sf % 16 == 0) && ((uintptr_t)down_sf % 4 == 0),
+               AEOQ_ERR_INVALID, "moe_decode_fused: weights must be 16-byte aligned (down scales 4-byte)");
+  const size_t need = aeoq_moe_nvfp4_decode_fused_workspace_size(top_k, hidden_dim, inter_dim);
+  AEOQ_REQUIRE(workspace && workspace_bytes >= need && (uintptr_t)workspace % 256 == 0, AEOQ_ERR_WORKSPACE,
+               "moe_decode_fused: workspace of %zu bytes (256-aligned, first 256 B zero) needed, %zu given", need,
+               workspace_bytes);
+  const int G = fused_grid();
+  const FusedShape s = fused_shape(num_experts, hidden_dim, inter_dim, (int)top_k, G);
+  char* w = reinterpret_cast<char*>(workspace);
+  FusedArgs a{};
+  a.hidden = reinterpret_cast<const __nv_bfloat16*>(hidden);
+  a.ids = top_k_index; a.ids_dt = idx_dtype;
+  a.topw = reinterpret_cast<const __nv_bfloat16*>(top_k_weights);
+  a.gu = gate_up; a.gu_sf = gate_up_sf; a.gu_ts = gate_up_ts; a.gu_ts_dt = gate_up_ts_dtype;
+  a.dw = down; a.dw_sf = down_sf; a.d_ts = down_ts; a.d_ts_dt = down_ts_dtype;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out);
+  a.sync = reinterpret_cast<uint32_t*>(w);
+  a.parts = reinterpret_cast<uint32_t*>(w + 256);
+  a.h = reinterpret_cast<__nv_bfloat16*>(w + 256 + ((size_t)G * 4 + 255) / 256 * 256);
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(moe_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmemCap);
+    if (e != cudaSuccess) return set_error(AEOQ_ERR_CUDA, "moe_decode_fused: %s", cudaGetErrorString(e));
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)G);
+  cfg.blockDim = dim3(kFThreads);
+  cfg.dynamicSmemBytes = s.bytes;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, moe_decode_fused_kernel, a, s);
+  if (e != cudaSuccess) return set_error(AEOQ_ERR_CUDA, "moe_decode_fused_kernel: %s", cudaGetErrorString(e));
+  return check_launch("moe_decode_fused_kernel");
+}

@@ -41,10 +41,10 @@ DOWN_BYTES = 2816 * 352 + 2816 * 44
 METRIC = "MoE decode tok/s (M=1 gather) + NVFP4 prefill TFLOPS, % of roofline"
 FALLBACK_HBM_GBS = 6650.0
 
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of the gate_up
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the fused decode
 # kernel at this workload, from the ncu capture summarised in
-# profiles/moe_decode_gateup_b1.md (None until captured).
-NCU_TRAFFIC_GATEUP = None
+# profiles/moe_decode_fused_b1.md (None until captured).
+NCU_TRAFFIC_FUSED = None
 
 
 def parse():
@@ -290,39 +290,44 @@ def main():
 
     # ---- per-kernel timing for the roofline (same stream, CUDA events) ----
     lib = A.load()
-    ws_n = lib.aeoq_moe_nvfp4_decode_workspace_size(TOPK, H, I)
-    ws = torch.empty(ws_n, dtype=torch.uint8, device=dev)
     out = torch.empty(1, H, dtype=torch.bfloat16, device=dev)
+    fws_n = lib.aeoq_moe_nvfp4_decode_fused_workspace_size(TOPK, H, I)
+    fws = torch.zeros(fws_n, dtype=torch.uint8, device=dev)
+    uws_n = lib.aeoq_moe_nvfp4_decode_workspace_size(TOPK, H, I)
+    uws = torch.empty(uws_n, dtype=torch.uint8, device=dev)
 
-    def stage(fn, s):
+    def launch(fn, s, ws, ws_n):
         gp, gs, gt, dp, ds, dt = layers[s % L]
         return fn(hid_d[s].data_ptr(), idx_d[s].data_ptr(), A.I64, wts_d[s].data_ptr(), TOPK,
                   gp.data_ptr(), gs.data_ptr(), gt.data_ptr(), A.F32, dp.data_ptr(), ds.data_ptr(),
                   dt.data_ptr(), A.F32, E, H, I, out.data_ptr(), ws.data_ptr(), ws_n,
                   torch.cuda.current_stream(dev).cuda_stream)
 
+    def time_graph(fn, ws, ws_n):
+        sg = torch.cuda.Stream(dev)
+        sg.wait_stream(torch.cuda.current_stream(dev))
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(sg):
+            for s in range(3):
+                A.check(launch(fn, s, ws, ws_n))
+            with torch.cuda.graph(g2, stream=sg):
+                for s in range(K):
+                    A.check(launch(fn, W + s, ws, ws_n))
+        torch.cuda.current_stream(dev).wait_stream(sg)
+        torch.cuda.synchronize()
+        g2.replay()
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        g2.replay()
+        a1.record()
+        torch.cuda.synchronize()
+        return a0.elapsed_time(a1) / K
+
     stage_ms = {}
     if B == 1:
-        for name, fn in (("gate_up", lib.aeoq_moe_nvfp4_decode_gate_up), ("down", lib.aeoq_moe_nvfp4_decode_down)):
-            sg = torch.cuda.Stream(dev)
-            sg.wait_stream(torch.cuda.current_stream(dev))
-            g2 = torch.cuda.CUDAGraph()
-            with torch.cuda.stream(sg):
-                for s in range(3):
-                    A.check(stage(fn, s))
-                with torch.cuda.graph(g2, stream=sg):
-                    for s in range(K):
-                        A.check(stage(fn, W + s))
-            torch.cuda.current_stream(dev).wait_stream(sg)
-            torch.cuda.synchronize()
-            g2.replay()
-            torch.cuda.synchronize()
-            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a0.record()
-            g2.replay()
-            a1.record()
-            torch.cuda.synchronize()
-            stage_ms[name] = a0.elapsed_time(a1) / K
+        stage_ms["fused"] = time_graph(lib.aeoq_moe_nvfp4_decode_fused, fws, fws_n)
+        stage_ms["unfused"] = time_graph(lib.aeoq_moe_nvfp4_decode, uws, uws_n)
 
     # ---- end to end through the public module API with host buffers ----
     hid_h = hid.pin_memory()
@@ -360,18 +365,15 @@ def main():
     if rank == 0:
         hbm, peak_src = peaks()
         roof = None
-        if "gate_up" in stage_ms:
-            alg = TOPK * GATEUP_BYTES + H * 2 + TOPK * I * 2
-            ach = alg / (stage_ms["gate_up"] / 1000.0) / 1e9
-            roof = {"bound": "hbm", "kernel": "moe_decode_gateup_kernel", "achieved": round(ach, 1),
-                    "peak": hbm, "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else "fallback",
-                    "unit": "GB/s", "frac": round(ach / hbm, 4),
-                    "traffic": NCU_TRAFFIC_GATEUP, "algorithmic_bytes": alg,
-                    "launch_us": round(stage_ms["gate_up"] * 1000, 3)}
-            alg_d = TOPK * DOWN_BYTES + TOPK * I * 2 + H * 2
-            roof["down_kernel"] = {"kernel": "moe_decode_hquant_kernel + moe_decode_down_kernel", "launch_us": round(stage_ms["down"] * 1000, 3),
-                                   "achieved": round(alg_d / (stage_ms["down"] / 1000.0) / 1e9, 1),
-                                   "algorithmic_bytes": alg_d}
+        if "fused" in stage_ms:
+            alg = TOPK * EXPERT_BYTES + 2 * H * 2 + TOPK * I * 2 * 2
+            ach = alg / (stage_ms["fused"] / 1000.0) / 1e9
+            roof = {"bound": "hbm", "kernel": "moe_decode_fused_kernel", "achieved": round(ach, 1),
+                    "peak": hbm, "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
+                    else "of fallback", "unit": "GB/s", "frac": round(ach / hbm, 4),
+                    "traffic": NCU_TRAFFIC_FUSED, "algorithmic_bytes": alg,
+                    "launch_us": round(stage_ms["fused"] * 1000, 3),
+                    "three_launch_path_us": round(stage_ms["unfused"] * 1000, 3)}
         step_bytes = TOPK * EXPERT_BYTES + 2 * H * 2
         res = {
             "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": K,
@@ -384,7 +386,7 @@ def main():
                        f"{L * 428} MB resident, 26.8 MB streamed per step",
                        "parallelism": f"replicas x{world}", "timing": "one CUDA graph of K steps, CUDA events"},
             "step_hbm_gbs": round(step_bytes / (ms_max / K / 1000.0) / 1e9, 1),
-            "gpu_launches": 3 * K,
+            "gpu_launches": K,
             "clocks": clk.summary(),
             "e2e": {"value": round(e2e_val, 1), "unit": "tok/s", "steps": n_e2e,
                     "h2d_bytes_per_step": B * H * 2 + B * TOPK * 8 + B * TOPK * 2,

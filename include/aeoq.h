@@ -166,6 +166,30 @@ AEOQ_API int aeoq_moe_nvfp4_decode_down(const void* hidden, const void* top_k_in
                                         int64_t num_experts, int64_t hidden_dim, int64_t inter_dim,
                                         void* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------
+ * One-token NVFP4 MoE expert forward as ONE persistent cooperative kernel
+ * (same math and arguments as aeoq_moe_nvfp4_decode; replaces the same
+ * reference function, modeling_nvfp4.py:132-186). Each SM copies its whole
+ * weight slice to shared memory at launch; one grid barrier separates the
+ * gate/up and down halves.
+ * Workspace contract: aeoq_moe_nvfp4_decode_fused_workspace_size() bytes,
+ * 256-aligned, whose first 256 bytes are zero before the first call; each
+ * call leaves them zero again, so one workspace serves successive calls on
+ * one stream (calls that overlap on the device must not share it).
+ * aeoq_moe_nvfp4_decode_fused_supported() tells whether a shape fits
+ * (hidden % 256 == 0, inter % 64 == 0, top_k <= 16, shared memory budget).
+ * ------------------------------------------------------------------------ */
+AEOQ_API int aeoq_moe_nvfp4_decode_fused_supported(int64_t top_k, int64_t hidden, int64_t inter);
+AEOQ_API size_t aeoq_moe_nvfp4_decode_fused_workspace_size(int64_t top_k, int64_t hidden, int64_t inter);
+AEOQ_API int aeoq_moe_nvfp4_decode_fused(const void* hidden, const void* top_k_index, int idx_dtype,
+                                         const void* top_k_weights, int64_t top_k,
+                                         const uint8_t* gate_up, const uint8_t* gate_up_sf,
+                                         const void* gate_up_ts, int gate_up_ts_dtype,
+                                         const uint8_t* down, const uint8_t* down_sf,
+                                         const void* down_ts, int down_ts_dtype,
+                                         int64_t num_experts, int64_t hidden_dim, int64_t inter_dim,
+                                         void* out, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
