@@ -361,7 +361,10 @@ static int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
-  if (e != cudaSuccess) return set_error(AEOQ_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(AEOQ_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
+  }
   return check_launch(name);
 }
 

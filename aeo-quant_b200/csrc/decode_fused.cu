@@ -34,7 +34,7 @@ constexpr int kFThreads = 512;
 constexpr int kFWarps = kFThreads / 32;
 constexpr int kFMaxTopK = 16;
 constexpr int kFMaxDownRows = 32;
-constexpr int kSmemCap = 232448;   // 227 KB dynamic shared memory per CTA
+constexpr int kSmemCap = 232448 - 1024;   // opt-in shared memory per CTA less static use
 
 struct FusedShape {
   int64_t E, H, I;
@@ -389,12 +389,16 @@ extern "C" int aeoq_moe_nvfp4_decode_fused(const void* hidden, const void* top_k
   a.sync = reinterpret_cast<uint32_t*>(w);
   a.parts = reinterpret_cast<uint32_t*>(w + 256);
   a.h = reinterpret_cast<__nv_bfloat16*>(w + 256 + ((size_t)G * 4 + 255) / 256 * 256);
-  static bool attr_set = false;
-  if (!attr_set) {
+  static size_t attr_bytes = 0;
+  if (attr_bytes < s.bytes) {
     cudaError_t e = cudaFuncSetAttribute(moe_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kSmemCap);
-    if (e != cudaSuccess) return set_error(AEOQ_ERR_CUDA, "moe_decode_fused: %s", cudaGetErrorString(e));
-    attr_set = true;
+                                         (int)s.bytes);
+    if (e != cudaSuccess) {
+      cudaGetLastError();   // do not leave the error for the next launch check
+      return set_error(AEOQ_ERR_CUDA, "moe_decode_fused: shared memory attribute (%zu B): %s", s.bytes,
+                       cudaGetErrorString(e));
+    }
+    attr_bytes = s.bytes;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)G);
@@ -407,6 +411,9 @@ extern "C" int aeoq_moe_nvfp4_decode_fused(const void* hidden, const void* top_k
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, moe_decode_fused_kernel, a, s);
-  if (e != cudaSuccess) return set_error(AEOQ_ERR_CUDA, "moe_decode_fused_kernel: %s", cudaGetErrorString(e));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(AEOQ_ERR_CUDA, "moe_decode_fused_kernel: %s", cudaGetErrorString(e));
+  }
   return check_launch("moe_decode_fused_kernel");
 }
