@@ -138,27 +138,58 @@ __device__ __forceinline__ float nvfp4_tensor_scale(float amax) {
 }
 
 // Quantize one 16-element block given the tensor scale (quant.py:169-183).
-// v[16] holds the input values as float. Returns the e4m3 code; writes the
-// 8 packed bytes (high nibble = even k) into *packed_lo / *packed_hi words.
+// v[16] holds the input values as float. Returns the e4m3 code and the 8
+// packed bytes (high nibble = even k) in w0 (elements 0-7) / w1 (8-15).
+//
+// The reference computes q = RN(RN(x/ts)/bs) with two IEEE divisions per
+// element. Here:
+//  * the block maximum of RN(|x|/ts) is RN(max|x| / ts) (division by a
+//    positive scale is monotone), so the block needs one division for it and
+//    one for the e4m3 scale;
+//  * each element's bin is taken from qa = x * RN(1/RN(ts*bs)), whose
+//    relative distance to the exact q is below 5 * 2^-24; whenever qa lies
+//    within 2^-16 (relative) of a bin boundary, is tiny, or the scales are
+//    not finite positive normals, the element falls back to the exact two
+//    divisions. Every nibble therefore equals the reference's.
 __device__ __forceinline__ uint32_t nvfp4_quant_block(const float (&v)[16], float ts,
                                                       uint32_t& w0, uint32_t& w1) {
-  float wp[16];
-  float bmax = 0.0f;
+  float amax = 0.0f;
+  bool anynan = false;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    wp[i] = __fdiv_rn(v[i], ts);
-    bmax = nan_max(bmax, fabsf(wp[i]));
+    const float a = fabsf(v[i]);
+    anynan |= (a != a);
+    amax = fmaxf(amax, a);
   }
-  float bm = (bmax != bmax) ? bmax : fmaxf(bmax, 1e-8f);
-  uint32_t sf = e4m3_encode(__fdiv_rn(bm, kFp4Max));
-  float bs = e4m3_decode(sf);
+  float bmax = anynan ? __int_as_float(0x7FC00000) : __fdiv_rn(amax, ts);
+  const float bm = (bmax != bmax) ? bmax : fmaxf(bmax, 1e-8f);
+  const uint32_t sf = e4m3_encode(__fdiv_rn(bm, kFp4Max));
+  const float bs = e4m3_decode(sf);
+  const float prod = ts * bs;
+  const bool fast = (prod > 1e-30f) && (prod < 1e30f) && (ts < 3.0e38f) && (bs < 3.0e38f);
+  const float inv = fast ? __frcp_rn(prod) : 0.0f;
   uint32_t words[2] = {0u, 0u};
 #pragma unroll
-  for (int i = 0; i < 16; i += 2) {
-    uint32_t hi = fp4_nibble(__fdiv_rn(wp[i], bs));
-    uint32_t lo = fp4_nibble(__fdiv_rn(wp[i + 1], bs));
-    uint32_t byte = (hi << 4) | lo;
-    words[i >> 3] |= byte << (8 * ((i >> 1) & 3));
+  for (int i = 0; i < 16; ++i) {
+    const float qa = v[i] * inv;
+    const float m = fabsf(qa);
+    const float e = 1.52587890625e-05f;   // 2^-16
+    bool near = !fast || (m < 1e-30f && v[i] != 0.0f);
+    near |= fabsf(m - 0.25f) <= 0.25f * e;
+    near |= fabsf(m - 0.75f) <= 0.75f * e;
+    near |= fabsf(m - 1.25f) <= 1.25f * e;
+    near |= fabsf(m - 1.75f) <= 1.75f * e;
+    near |= fabsf(m - 2.5f) <= 2.5f * e;
+    near |= fabsf(m - 3.5f) <= 3.5f * e;
+    near |= fabsf(m - 5.0f) <= 5.0f * e;
+    uint32_t nib;
+    if (near) {
+      nib = fp4_nibble(__fdiv_rn(__fdiv_rn(v[i], ts), bs));
+    } else {
+      nib = ((qa < 0.0f) ? 8u : 0u) | (uint32_t)((m > 0.25f) + (m > 0.75f) + (m > 1.25f) + (m > 1.75f) +
+                                                  (m > 2.5f) + (m > 3.5f) + (m > 5.0f));
+    }
+    words[i >> 3] |= nib << (4 * ((i & 7) ^ 1));
   }
   w0 = words[0];
   w1 = words[1];

@@ -81,10 +81,25 @@ struct FusedArgs {
   uint32_t* sync;        // [0] arrivals, [1] departures, [2] error code
 };
 
-// Quantize 16 bf16 values (global, written by other CTAs -> L2-coherent
-// loads when `coherent`) and store exact halves + scale into shared memory.
+// Phase timestamps for development builds (-DAEOQ_DECODE_TRACE): thread 0 of
+// each CTA records %globaltimer at each phase boundary into the workspace.
+#ifdef AEOQ_DECODE_TRACE
+#define TRACE(i)                                                                               \
+  do {                                                                                         \
+    if (tid == 0) {                                                                            \
+      uint64_t t_;                                                                             \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                   \
+      reinterpret_cast<uint64_t*>(a.h + (size_t)s.k * s.I)[blockIdx.x * 16 + (i)] = t_;      \
+    }                                                                                          \
+  } while (0)
+#else
+#define TRACE(i) do {} while (0)
+#endif
+
+// Quantize 16 bf16 values (global; read L2-coherently when another CTA of
+// this grid wrote them) and store exact halves + 2^14-scaled block scale.
 template <bool kCoherent>
-__device__ __forceinline__ void quant_block_to_smem(const __nv_bfloat16* src, float ts, __half2* dst, float* sa) {
+__device__ __forceinline__ void quant_block_to_smem(const __nv_bfloat16* src, float ts, __half2* dst, float* sa16k) {
   float v[16];
 #pragma unroll
   for (int q = 0; q < 2; ++q) {
@@ -97,20 +112,23 @@ __device__ __forceinline__ void quant_block_to_smem(const __nv_bfloat16* src, fl
   uint32_t w0, w1;
   const uint32_t sf = nvfp4_quant_block(v, ts, w0, w1);
   __half2 t[4];
-  fp4x8_to_half2x4(w0, t);
+  fp4x8_to_half2x4_exact(w0, t);
 #pragma unroll
   for (int i = 0; i < 4; ++i) dst[i] = t[i];
-  fp4x8_to_half2x4(w1, t);
+  fp4x8_to_half2x4_exact(w1, t);
 #pragma unroll
   for (int i = 0; i < 4; ++i) dst[4 + i] = t[i];
-  *sa = e4m3_decode(sf);
+  *sa16k = e4m3_decode(sf) * 16384.0f;
 }
+
+constexpr int kPairsPerBar = 16;   // gate/up pairs per arrival barrier
+constexpr int kMaxGuBars = 8;
 
 __global__ void __launch_bounds__(kFThreads, 1) moe_decode_fused_kernel(FusedArgs a, FusedShape s) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ uint32_t red[kFWarps];
-  uint64_t* bar_gu = reinterpret_cast<uint64_t*>(smem + s.bytes - 128);
-  uint64_t* bar_dn = bar_gu + 1;
+  __shared__ int64_t ids_s[kFMaxTopK];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + s.bytes - 128);   // [0..kMaxGuBars) gate/up, [kMaxGuBars] down
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t H = s.H, I = s.I;
   const int k = s.k;
@@ -118,6 +136,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_decode_fused_kernel(FusedArg
   const int64_t p0 = (int64_t)blockIdx.x * s.ppc;
   const int64_t p1 = min((int64_t)k * I, p0 + s.ppc);
   const int np = (int)max((int64_t)0, p1 - p0);
+  const int nbar = (np + kPairsPerBar - 1) / kPairsPerBar;
   const int64_t r0 = (int64_t)blockIdx.x * s.rpc;
   const int nr = (int)max((int64_t)0, min(H, r0 + s.rpc) - r0);
   uint8_t* gate_s = smem + s.off_gate;
@@ -132,64 +151,61 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_decode_fused_kernel(FusedArg
   float* hsa_s = reinterpret_cast<float*>(smem + s.off_hsa);
   float* prod_s = reinterpret_cast<float*>(smem + s.off_prod);
   int* err = reinterpret_cast<int*>(a.sync + 2);
+  TRACE(0);
 
-  // ---- 1. issue every weight copy of this CTA's slice -------------------
-  if (tid == 0) {
-    sm100::mbar_init(bar_gu, 1);
-    sm100::mbar_init(bar_dn, 1);
-    sm100::fence_barrier_init();
-    uint32_t gu_bytes = (uint32_t)(np * (2 * rb + 2 * sb));
-    uint32_t dn_bytes = (uint32_t)((size_t)nr * k * rb2);
-    sm100::mbar_arrive_expect_tx(bar_gu, gu_bytes);
-    sm100::mbar_arrive_expect_tx(bar_dn, dn_bytes);
-    // gate/up rows: the pair range spans at most a few slots; copy per segment
-    int64_t p = p0;
-    int dst = 0;
-    while (p < p1) {
-      const int64_t slot = p / I, n = p - slot * I;
-      const int64_t len = min(p1 - p, I - n);
-      const int64_t e = load_index(a.ids, a.ids_dt, slot);
-      if (e >= 0 && e < s.E) {
-        const uint8_t* g = a.gu + (e * 2 * I + n) * rb;
-        const uint8_t* gs = a.gu_sf + (e * 2 * I + n) * sb;
-        bulk_g2s(gate_s + dst * rb, g, (uint32_t)(len * rb), bar_gu);
-        bulk_g2s(up_s + dst * rb, g + I * rb, (uint32_t)(len * rb), bar_gu);
-        bulk_g2s(gsf_s + dst * sb, gs, (uint32_t)(len * sb), bar_gu);
-        bulk_g2s(usf_s + dst * sb, gs + I * sb, (uint32_t)(len * sb), bar_gu);
-      } else {
-        // invalid expert id: no copy; account for the bytes so the barrier completes
-        asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(sm100::smem_u32(bar_gu)),
-                     "r"((uint32_t)(len * (2 * rb + 2 * sb)))
-                     : "memory");
-      }
-      dst += (int)len;
-      p += len;
+  // ---- 1. expert ids (one load latency), then every weight copy -----------
+  if (warp == 0) {
+    int64_t myid = -1;
+    if (lane < k) myid = load_index(a.ids, a.ids_dt, lane);
+    if (lane < k) ids_s[lane] = myid;
+    if (lane == 0) {
+      for (int b = 0; b <= kMaxGuBars; ++b) sm100::mbar_init(bars + b, 1);
+      sm100::fence_barrier_init();
     }
-    for (int j = 0; j < k && nr > 0; ++j) {
-      const int64_t e = load_index(a.ids, a.ids_dt, j);
-      if (e >= 0 && e < s.E) {
-        bulk_g2s(dn_s + (size_t)j * nr * rb2, a.dw + (e * H + r0) * rb2, (uint32_t)(nr * rb2), bar_dn);
-      } else {
-        asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(sm100::smem_u32(bar_dn)),
-                     "r"((uint32_t)(nr * rb2))
-                     : "memory");
+    __syncwarp();
+    if (lane == 0) {
+      // gate/up: kPairsPerBar pairs per barrier, split at slot boundaries
+      for (int b = 0; b < nbar; ++b) {
+        const int i0 = b * kPairsPerBar, i1 = min(np, i0 + kPairsPerBar);
+        sm100::mbar_arrive_expect_tx(bars + b, (uint32_t)((i1 - i0) * (2 * rb + 2 * sb)));
+        int64_t p = p0 + i0;
+        int dst = i0;
+        while (p < p0 + i1) {
+          const int64_t slot = p / I, n = p - slot * I;
+          const int64_t len = min(p0 + i1 - p, I - n);
+          const int64_t e = ids_s[slot];
+          if (e >= 0 && e < s.E) {
+            const uint8_t* g = a.gu + (e * 2 * I + n) * rb;
+            const uint8_t* gs = a.gu_sf + (e * 2 * I + n) * sb;
+            bulk_g2s(gate_s + dst * rb, g, (uint32_t)(len * rb), bars + b);
+            bulk_g2s(up_s + dst * rb, g + I * rb, (uint32_t)(len * rb), bars + b);
+            bulk_g2s(gsf_s + dst * sb, gs, (uint32_t)(len * sb), bars + b);
+            bulk_g2s(usf_s + dst * sb, gs + I * sb, (uint32_t)(len * sb), bars + b);
+          } else {
+            asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(sm100::smem_u32(bars + b)),
+                         "r"((uint32_t)(len * (2 * rb + 2 * sb)))
+                         : "memory");
+          }
+          dst += (int)len;
+          p += len;
+        }
+      }
+      uint64_t* bdn = bars + kMaxGuBars;
+      sm100::mbar_arrive_expect_tx(bdn, (uint32_t)((size_t)nr * k * rb2));
+      for (int j = 0; j < k && nr > 0; ++j) {
+        const int64_t e = ids_s[j];
+        if (e >= 0 && e < s.E) {
+          bulk_g2s(dn_s + (size_t)j * nr * rb2, a.dw + (e * H + r0) * rb2, (uint32_t)(nr * rb2), bdn);
+        } else {
+          asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(sm100::smem_u32(bdn)),
+                       "r"((uint32_t)(nr * rb2))
+                       : "memory");
+        }
       }
     }
   }
-  // down scale rows (44 B per row: not bulk-copy aligned) with plain loads
-  {
-    const int words = (int)(nr * sb2 / 4);   // per slot
-    for (int idx = tid; idx < k * words; idx += kFThreads) {
-      const int j = idx / words, wdx = idx - j * words;
-      const int64_t e = load_index(a.ids, a.ids_dt, j);
-      uint32_t v = 0;
-      if (e >= 0 && e < s.E)
-        v = *reinterpret_cast<const uint32_t*>(a.dw_sf + (e * H + r0) * sb2 + 4 * wdx);
-      reinterpret_cast<uint32_t*>(dsf_s + (size_t)j * nr * sb2)[wdx] = v;
-    }
-  }
-
-  // ---- 2. hidden quant: amax -> ts -> exact halves in shared memory ----
+  TRACE(1);
+  // hidden amax (independent of the ids)
   uint32_t key = 0;
   for (int64_t i = tid; i < H / 8; i += kFThreads) {
     const uint4 u = *reinterpret_cast<const uint4*>(a.hidden + 8 * i);
@@ -199,7 +215,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_decode_fused_kernel(FusedArg
   }
   key = warp_umax(key);
   if (lane == 0) red[warp] = key;
-  __syncthreads();   // also publishes the barrier init and the down scales
+  __syncthreads();   // publishes ids_s, the barrier inits and red
   key = 0;
 #pragma unroll
   for (int w = 0; w < kFWarps; ++w) key = max(key, red[w]);
@@ -207,46 +223,81 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_decode_fused_kernel(FusedArg
   const float alpha = ts * load_scalar_f(a.gu_ts, a.gu_ts_dt);
   for (int64_t b = tid; b < H / 16; b += kFThreads)
     quant_block_to_smem<false>(a.hidden + 16 * b, ts, act_s + 8 * b, asa_s + b);
-  __syncthreads();
-
-  // ---- 3. gate/up GEMV + GeGLU ------------------------------------------
-  const int nchunk = (int)(H / 32);
-  uint32_t hkey = 0;
-  const bool ok_gu = sm100::mbar_wait(bar_gu, 0, err, 1);
-  if (ok_gu) {
-    for (int i = warp; i < np; i += kFWarps) {
-      const int64_t slot = (p0 + i) / I;
-      const int64_t e = load_index(a.ids, a.ids_dt, slot);
-      const bool valid = e >= 0 && e < s.E;   // an invalid id contributes zeros
-      float ag = 0.f, au = 0.f;
-      for (int c = lane; c < nchunk && valid; c += 32) {
-        __half2 av[16];
-        const uint4* ap = reinterpret_cast<const uint4*>(act_s + 16 * c);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(&av[4 * q]) = ap[q];
-        const float sa2[2] = {asa_s[2 * c], asa_s[2 * c + 1]};
-        const uint4 gw = *reinterpret_cast<const uint4*>(gate_s + i * rb + 16 * c);
-        const uint4 uw = *reinterpret_cast<const uint4*>(up_s + i * rb + 16 * c);
-        const uint16_t gs = *reinterpret_cast<const uint16_t*>(gsf_s + i * sb + 2 * c);
-        const uint16_t us = *reinterpret_cast<const uint16_t*>(usf_s + i * sb + 2 * c);
-        ag = chunk_dot_x(av, sa2, gw, gs, ag);
-        au = chunk_dot_x(av, sa2, uw, us, au);
-      }
-      ag = warp_sum(ag);
-      au = warp_sum(au);
-      if (lane == 0) {
-        const float g = bf16r(ag * alpha), u = bf16r(au * alpha);
-        const __nv_bfloat16 hv = __float2bfloat16_rn(bf16r(gelu_tanh(g)) * u);
-        a.h[p0 + i] = hv;
-        hkey = max(hkey, In<AEOQ_BF16>::abs_key(hv));
-      }
+  // down scale rows (44 B per row: not bulk-copy aligned) with plain loads
+  {
+    const int words = (int)(nr * sb2 / 4);   // per slot
+    for (int idx = tid; idx < k * words; idx += kFThreads) {
+      const int j = idx / words, wdx = idx - j * words;
+      const int64_t e = ids_s[j];
+      uint32_t v = 0;
+      if (e >= 0 && e < s.E) v = *reinterpret_cast<const uint32_t*>(a.dw_sf + (e * H + r0) * sb2 + 4 * wdx);
+      reinterpret_cast<uint32_t*>(dsf_s + (size_t)j * nr * sb2)[wdx] = v;
     }
   }
+  __syncthreads();
+  TRACE(2);
+
+  // ---- 3. gate/up GEMV + GeGLU, pair groups consumed as they land ---------
+  constexpr int kCPL = 4;   // 16-byte chunks per lane per row (H <= 4096)
+  const int nchunk = (int)(H / 32);
+  __half2 act[kCPL][16];
+  float sa[kCPL][2];
+#pragma unroll
+  for (int q = 0; q < kCPL; ++q) {
+    const int c = lane + 32 * q;
+    if (c < nchunk) {
+      const uint4* ap = reinterpret_cast<const uint4*>(act_s + 16 * c);
+#pragma unroll
+      for (int z = 0; z < 4; ++z) *reinterpret_cast<uint4*>(&act[q][4 * z]) = ap[z];
+      sa[q][0] = asa_s[2 * c];
+      sa[q][1] = asa_s[2 * c + 1];
+    }
+  }
+  uint32_t hkey = 0;
+  bool ok = true;
+  int waited_bar = -1;
+  for (int i = warp; i < np; i += kFWarps) {
+    const int b = i / kPairsPerBar;
+    if (b > waited_bar) {
+      for (int bb = waited_bar + 1; bb <= b; ++bb) ok &= sm100::mbar_wait(bars + bb, 0, err, 1);
+      waited_bar = b;
+    }
+    const int64_t slot = (p0 + i) / I;
+    const int64_t e = ids_s[slot];
+    const bool valid = ok && e >= 0 && e < s.E;   // an invalid id contributes zeros
+    float ag = 0.f, au = 0.f;
+    if (valid) {
+#pragma unroll
+      for (int q = 0; q < kCPL; ++q) {
+        const int c = lane + 32 * q;
+        if (c < nchunk) {
+          const uint4 gw = *reinterpret_cast<const uint4*>(gate_s + i * rb + 16 * c);
+          const uint4 uw = *reinterpret_cast<const uint4*>(up_s + i * rb + 16 * c);
+          const uint16_t gs = *reinterpret_cast<const uint16_t*>(gsf_s + i * sb + 2 * c);
+          const uint16_t us = *reinterpret_cast<const uint16_t*>(usf_s + i * sb + 2 * c);
+          ag = chunk_dot(act[q], sa[q], gw, gs, ag);
+          au = chunk_dot(act[q], sa[q], uw, us, au);
+        }
+      }
+    }
+    ag = warp_sum(ag);
+    au = warp_sum(au);
+    if (lane == 0) {
+      const float g = bf16r(ag * alpha), u = bf16r(au * alpha);
+      const __nv_bfloat16 hv = __float2bfloat16_rn(bf16r(gelu_tanh(g)) * u);
+      a.h[p0 + i] = hv;
+      hkey = max(hkey, In<AEOQ_BF16>::abs_key(hv));
+    }
+  }
+  // barriers this warp never waited on still have to complete before exit
+  for (int bb = waited_bar + 1; bb < nbar; ++bb) sm100::mbar_wait(bars + bb, 0, err, 1);
+  TRACE(3);
   hkey = warp_umax(hkey);
   __threadfence();   // h stores of every writer ordered before the arrival below
   __syncthreads();
   if (lane == 0) red[warp] = hkey;
   __syncthreads();
+  TRACE(4);
 
   // ---- 4. grid barrier ----------------------------------------------------
   if (tid == 0) {
@@ -260,11 +311,12 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_decode_fused_kernel(FusedArg
       uint32_t v;
       asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync + 0) : "memory");
       if (v >= (uint32_t)s.G) { done = true; break; }
-      __nanosleep(64);
+      __nanosleep(32);
     }
     if (!done) atomicCAS(err, 0, 2);
   }
   __syncthreads();
+  TRACE(5);
 
   // shared tensor scale of h over all CTAs, then re-quantize all of h here
   uint32_t hk = 0;
@@ -280,30 +332,51 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_decode_fused_kernel(FusedArg
   for (int64_t b = tid; b < (int64_t)k * I / 16; b += kFThreads)
     quant_block_to_smem<true>(a.h + 16 * b, hts, hact_s + 8 * b, hsa_s + b);
   __syncthreads();
+  TRACE(6);
 
-  // ---- 5. down GEMV + weighted combine -----------------------------------
-  const bool ok_dn = sm100::mbar_wait(bar_dn, 0, err, 3);
+  // ---- 5. down GEMV + weighted combine: warps own one slot each ------------
+  const bool ok_dn = sm100::mbar_wait(bars + kMaxGuBars, 0, err, 3);
+  TRACE(7);
   const int nchunk2 = (int)(I / 32);
-  if (ok_dn) {
-    for (int it = warp; it < nr * k; it += kFWarps) {
-      const int j = it / nr, r = it - j * nr;
-      const int64_t e = load_index(a.ids, a.ids_dt, j);
-      const bool valid = e >= 0 && e < s.E;
-      float acc = 0.f;
-      for (int c = lane; c < nchunk2 && valid; c += 32) {
-        __half2 av[16];
-        const uint4* ap = reinterpret_cast<const uint4*>(hact_s + (j * (I / 16) + 2 * c) * 8);
+  const int wpj = kFWarps / k;   // warps per slot (k <= 16)
+  if (ok_dn && warp < wpj * k) {
+    const int j = warp / wpj;
+    const int64_t e = ids_s[j];
+    const bool valid = e >= 0 && e < s.E;
+    const float wj = __bfloat162float(a.topw[j]);
+    // the intermediate dimension is at most 2048: at most two chunks per lane
+    __half2 hv0[16], hv1[16];
+    float hs0[2] = {0.f, 0.f}, hs1[2] = {0.f, 0.f};
+    const int c0 = lane, c1 = lane + 32;
+    if (c0 < nchunk2) {
+      const int hb = (int)(j * (I / 16) + 2 * c0);
+      const uint4* ap = reinterpret_cast<const uint4*>(hact_s + hb * 8);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(&av[4 * q]) = ap[q];
-        const int hb = (int)(j * (I / 16) + 2 * c);
-        const float sa2[2] = {hsa_s[hb], hsa_s[hb + 1]};
+      for (int z = 0; z < 4; ++z) *reinterpret_cast<uint4*>(&hv0[4 * z]) = ap[z];
+      hs0[0] = hsa_s[hb];
+      hs0[1] = hsa_s[hb + 1];
+    }
+    if (c1 < nchunk2) {
+      const int hb = (int)(j * (I / 16) + 2 * c1);
+      const uint4* ap = reinterpret_cast<const uint4*>(hact_s + hb * 8);
+#pragma unroll
+      for (int z = 0; z < 4; ++z) *reinterpret_cast<uint4*>(&hv1[4 * z]) = ap[z];
+      hs1[0] = hsa_s[hb];
+      hs1[1] = hsa_s[hb + 1];
+    }
+    for (int r = warp % wpj; r < nr; r += wpj) {
+      float acc = 0.f;
+      if (valid) {
         const size_t row = (size_t)j * nr + r;
-        const uint4 wv = *reinterpret_cast<const uint4*>(dn_s + row * rb2 + 16 * c);
-        const uint16_t ws = *reinterpret_cast<const uint16_t*>(dsf_s + row * sb2 + 2 * c);
-        acc = chunk_dot_x(av, sa2, wv, ws, acc);
+        if (c0 < nchunk2)
+          acc = chunk_dot(hv0, hs0, *reinterpret_cast<const uint4*>(dn_s + row * rb2 + 16 * c0),
+                          *reinterpret_cast<const uint16_t*>(dsf_s + row * sb2 + 2 * c0), acc);
+        if (c1 < nchunk2)
+          acc = chunk_dot(hv1, hs1, *reinterpret_cast<const uint4*>(dn_s + row * rb2 + 16 * c1),
+                          *reinterpret_cast<const uint16_t*>(dsf_s + row * sb2 + 2 * c1), acc);
       }
       acc = warp_sum(acc);
-      if (lane == 0) prod_s[j * kFMaxDownRows + r] = bf16r(bf16r(acc * alpha_d) * __bfloat162float(a.topw[j]));
+      if (lane == 0) prod_s[j * kFMaxDownRows + r] = bf16r(bf16r(acc * alpha_d) * wj);
     }
   }
   __syncthreads();
@@ -312,6 +385,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_decode_fused_kernel(FusedArg
     for (int j = 0; j < k; ++j) acc += prod_s[j * kFMaxDownRows + tid];
     a.out[r0 + tid] = __float2bfloat16_rn(acc);
   }
+  TRACE(8);
 
   // ---- departure: the last CTA out resets the counters ------------------
   if (tid == 0) {
@@ -349,8 +423,10 @@ extern "C" size_t aeoq_moe_nvfp4_decode_fused_workspace_size(int64_t top_k, int6
 extern "C" int aeoq_moe_nvfp4_decode_fused_supported(int64_t top_k, int64_t hidden, int64_t inter) {
   if (top_k < 1 || top_k > kFMaxTopK) return 0;
   if (hidden % 256 != 0 || inter % 64 != 0 || hidden <= 0 || inter <= 0) return 0;
+  if (hidden > 4096 || inter > 2048) return 0;
   const FusedShape s = fused_shape(0, hidden, inter, (int)top_k, fused_grid());
   if (s.rpc > kFMaxDownRows) return 0;
+  if ((s.ppc + kPairsPerBar - 1) / kPairsPerBar > kMaxGuBars) return 0;
   return s.bytes <= (size_t)kSmemCap ? 1 : 0;
 }
 
