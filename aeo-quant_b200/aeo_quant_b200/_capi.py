@@ -42,9 +42,13 @@ _SIGS["aeoq_moe_nvfp4_decode_down"] = _SIGS["aeoq_moe_nvfp4_decode"]
 _SIGS["aeoq_moe_nvfp4_decode_fused"] = _SIGS["aeoq_moe_nvfp4_decode"]
 _SIGS["aeoq_moe_nvfp4_decode_fused_supported"] = [_L, _L, _L]
 _SIGS["aeoq_moe_nvfp4_decode_fused_workspace_size"] = [_L, _L, _L]
+_SIGS["aeoq_moe_nvfp4_decode_fused_noalloc_max_scratch"] = []
+_SIGS["aeoq_moe_nvfp4_decode_fused_noalloc"] = [_P, _P, _I, _P, _L, _P, _P, _P, _I, _P, _P, _P, _I, _L, _L, _L,
+                                                _P, _P]
 _RESTYPE = {"aeoq_last_error": C.c_char_p, "aeoq_nvfp4_quantize_workspace_size": C.c_size_t,
             "aeoq_moe_nvfp4_decode_workspace_size": C.c_size_t,
-            "aeoq_moe_nvfp4_decode_fused_workspace_size": C.c_size_t}
+            "aeoq_moe_nvfp4_decode_fused_workspace_size": C.c_size_t,
+            "aeoq_moe_nvfp4_decode_fused_noalloc_max_scratch": C.c_size_t}
 
 _lib = None
 

@@ -493,3 +493,88 @@ extern "C" int aeoq_moe_nvfp4_decode_fused(const void* hidden, const void* top_k
   }
   return check_launch("moe_decode_fused_kernel");
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// Some callers cannot allocate device memory at the point where they run the
+// expert forward: a serving runtime that reserves every byte of device memory
+// at start-up and forbids allocation on its request path, or a plugin hosted
+// by a framework whose allocator it cannot reach. For them this entry point
+// takes the same inputs and outputs as aeoq_moe_nvfp4_decode_fused but no
+// workspace: its scratch (arrival counters, per-CTA maxima, the bf16
+// intermediate) lives in the file-scope device array below, kNoAllocScratch
+// bytes per GPU, held by every GPU that loads the library until the process
+// exits.
+//
+// * Host code only names the array through a host-side stand-in, so its
+//   device address is looked up with cudaGetSymbolAddress, once per device,
+//   with that device current. The first call on a device performs this
+//   lookup; make that first call before any stream capture.
+// * All calls on a device share the array and it keeps the last call's
+//   contents. Each call clears the counters that must start at zero
+//   (cudaMemsetAsync on its stream). Calls whose kernels overlap on the GPU
+//   (different streams without ordering) race on the array.
+// * Shapes whose scratch exceeds kNoAllocScratch are rejected.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace aeoq {
+constexpr size_t kNoAllocScratch = 128 * 1024;
+constexpr int kNoAllocMaxDevices = 64;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratch];
+static void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+static std::mutex g_noalloc_mu;
+
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(AEOQ_ERR_CUDA, "moe_decode_fused_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  }
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return set_error(AEOQ_ERR_UNSUPPORTED, "moe_decode_fused_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      cudaGetLastError();
+      return set_error(AEOQ_ERR_CUDA, "moe_decode_fused_noalloc: cudaGetSymbolAddress: %s",
+                       cudaGetErrorString(e));
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return AEOQ_OK;
+}
+}  // namespace aeoq
+
+extern "C" size_t aeoq_moe_nvfp4_decode_fused_noalloc_max_scratch(void) { return aeoq::kNoAllocScratch; }
+
+extern "C" int aeoq_moe_nvfp4_decode_fused_noalloc(const void* hidden, const void* top_k_index, int idx_dtype,
+                                                   const void* top_k_weights, int64_t top_k,
+                                                   const uint8_t* gate_up, const uint8_t* gate_up_sf,
+                                                   const void* gate_up_ts, int gate_up_ts_dtype,
+                                                   const uint8_t* down, const uint8_t* down_sf,
+                                                   const void* down_ts, int down_ts_dtype, int64_t num_experts,
+                                                   int64_t hidden_dim, int64_t inter_dim, void* out,
+                                                   void* stream) {
+  const size_t need = aeoq_moe_nvfp4_decode_fused_workspace_size(top_k, hidden_dim, inter_dim);
+  AEOQ_REQUIRE(need <= kNoAllocScratch, AEOQ_ERR_INVALID,
+               "moe_decode_fused_noalloc: needs %zu bytes of scratch, the static array holds %zu "
+               "(top_k * inter too large); use aeoq_moe_nvfp4_decode_fused with a workspace",
+               need, kNoAllocScratch);
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  cudaError_t e = cudaMemsetAsync(scratch, 0, 256, (cudaStream_t)stream);   // arrival/departure counters
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(AEOQ_ERR_CUDA, "moe_decode_fused_noalloc: clearing counters: %s", cudaGetErrorString(e));
+  }
+  return aeoq_moe_nvfp4_decode_fused(hidden, top_k_index, idx_dtype, top_k_weights, top_k, gate_up, gate_up_sf,
+                                     gate_up_ts, gate_up_ts_dtype, down, down_sf, down_ts, down_ts_dtype,
+                                     num_experts, hidden_dim, inter_dim, out, scratch, kNoAllocScratch, stream);
+}

@@ -190,6 +190,30 @@ AEOQ_API int aeoq_moe_nvfp4_decode_fused(const void* hidden, const void* top_k_i
                                          int64_t num_experts, int64_t hidden_dim, int64_t inter_dim,
                                          void* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Allocation-free one-token decode. No counterpart in the reference: it
+ * exists for callers that cannot allocate device memory where they run the
+ * expert forward (a serving runtime that pre-reserves all device memory, a
+ * plugin without access to its host's allocator). Same arguments as
+ * aeoq_moe_nvfp4_decode_fused minus the workspace; the scratch is a static
+ * device array of aeoq_moe_nvfp4_decode_fused_noalloc_max_scratch() bytes
+ * (128 KiB) per GPU, kept for the life of the process. Shapes needing more
+ * are rejected with AEOQ_ERR_INVALID. The first call on a device looks the
+ * array up (cudaGetSymbolAddress) and should precede any stream capture.
+ * Calls that overlap on the device share the array and race. Allocates
+ * nothing: no cudaMalloc/cudaFree, only a 256-byte cudaMemsetAsync of the
+ * counters on the given stream.
+ * ------------------------------------------------------------------------ */
+AEOQ_API size_t aeoq_moe_nvfp4_decode_fused_noalloc_max_scratch(void);
+AEOQ_API int aeoq_moe_nvfp4_decode_fused_noalloc(const void* hidden, const void* top_k_index, int idx_dtype,
+                                                 const void* top_k_weights, int64_t top_k,
+                                                 const uint8_t* gate_up, const uint8_t* gate_up_sf,
+                                                 const void* gate_up_ts, int gate_up_ts_dtype,
+                                                 const uint8_t* down, const uint8_t* down_sf,
+                                                 const void* down_ts, int down_ts_dtype,
+                                                 int64_t num_experts, int64_t hidden_dim, int64_t inter_dim,
+                                                 void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
