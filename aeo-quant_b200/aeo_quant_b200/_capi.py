@@ -43,6 +43,7 @@ _SIGS["aeoq_moe_nvfp4_decode_fused"] = _SIGS["aeoq_moe_nvfp4_decode"]
 _SIGS["aeoq_moe_nvfp4_decode_fused_supported"] = [_L, _L, _L]
 _SIGS["aeoq_moe_nvfp4_decode_fused_workspace_size"] = [_L, _L, _L]
 _SIGS["aeoq_moe_nvfp4_decode_fused_noalloc_max_scratch"] = []
+_SIGS["aeoq_nvfp4_gemm_tc"] = [_P, _P, _P, _I, _L, _P, _P, _P, _I, _L, _P, _I, _L, _L, _L, _L, _P, _I, _P, _P]
 _SIGS["aeoq_moe_nvfp4_decode_fused_noalloc"] = [_P, _P, _I, _P, _L, _P, _P, _P, _I, _P, _P, _P, _I, _L, _L, _L,
                                                 _P, _P]
 _RESTYPE = {"aeoq_last_error": C.c_char_p, "aeoq_nvfp4_quantize_workspace_size": C.c_size_t,
@@ -114,3 +115,16 @@ def stream_ptr(device: torch.device) -> int:
 
 def ptr(t) -> int | None:
     return None if t is None else t.data_ptr()
+
+
+_ERR_WORDS: dict = {}
+
+
+def err_word(device: torch.device) -> torch.Tensor:
+    """Per-device int32 that the tensor-core kernels' bounded waits set on a stall."""
+    key = device.index
+    t = _ERR_WORDS.get(key)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _ERR_WORDS[key] = t
+    return t

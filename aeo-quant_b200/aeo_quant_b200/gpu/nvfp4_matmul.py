@@ -51,8 +51,15 @@ def _out_code(out_dtype: torch.dtype) -> int:
     return _OUT_DT[out_dtype]
 
 
+# Which kernel serves a GEMM: "auto" picks the tcgen05 kernel once M reaches
+# TC_MIN_M rows (below that the problem is a weight stream that the CUDA-core
+# gather GEMV serves), "tc" / "simt" force one (used by the tests).
+PATH = "auto"
+TC_MIN_M = 8
+
+
 def _gemm(a, a_sf, a_ts, w, w_sf, w_ts, ids, slots, M, N, K, a_shared, out_dtype):
-    """Launch aeoq_nvfp4_gemm. ``a``/``a_sf`` are (M,K/2)/(M,K/16) when
+    """Launch the block-scaled GEMM. ``a``/``a_sf`` are (M,K/2)/(M,K/16) when
     ``a_shared`` else (slots,M,...); ``w``/``w_sf`` are (E,N,...)."""
     A.require_cuda(a, a_sf, a_ts, w, w_sf, w_ts)
     lib = A.load()
@@ -61,6 +68,15 @@ def _gemm(a, a_sf, a_ts, w, w_sf, w_ts, ids, slots, M, N, K, a_shared, out_dtype
     w = w.contiguous()
     w_sf = w_sf.contiguous()
     c = torch.empty(slots, M, N, dtype=out_dtype, device=a.device)
+    use_tc = PATH == "tc" or (PATH == "auto" and M >= TC_MIN_M)
+    if use_tc:
+        ids_p, ids_dt = (None, 0) if ids is None else (ids.data_ptr(), A.dtype_code(ids.dtype))
+        A.check(lib.aeoq_nvfp4_gemm_tc(
+            a.data_ptr(), a_sf.data_ptr(), a_ts.data_ptr(), A.dtype_code(a_ts.dtype), 0 if a_shared else M,
+            w.data_ptr(), w_sf.data_ptr(), w_ts.data_ptr(), A.dtype_code(w_ts.dtype), w.shape[0],
+            ids_p, ids_dt, slots, M, N, K, c.data_ptr(), _out_code(out_dtype),
+            A.err_word(a.device).data_ptr(), A.stream_ptr(a.device)))
+        return c
     es = c.element_size()
     if a_shared:
         a_ss, a_sfss = 0, 0

@@ -1,0 +1,470 @@
+// Block-scaled NVFP4 GEMM on the 5th-generation tensor cores (tcgen05).
+//
+// Computes, for a set of (weight matrix, activation rows) problems,
+//   C[row][n] = epilogue( sum_k A[n][k] * B[row][k] )      (A = weights)
+// with A and B packed E2M1 (two per byte, high nibble = even k, the aeo_quant
+// layout: src/aeo_quant/gpu/quant.py:180-183) and one UE4M3 scale per 16
+// values along k, i.e. the contract of the reference's tl.dot_scaled kernels
+// (src/aeo_quant/gpu/nvfp4_matmul.py:51-325). Both operands share the
+// in-byte nibble order, so the hardware's (low nibble = even k) convention
+// only permutes k inside each 16-value scale block, identically for A and B:
+// the dot product is unchanged.
+//
+// Weight-stationary "swap AB" tiling: the MMA's M = 128 rows are weight
+// rows (output features), its N = BN columns are activation rows (tokens),
+// so one to a few hundred tokens per expert map onto N = 8..256 without
+// padding M. Per CTA: one 128 x BN output tile, K in steps of 256 values
+// (128 B rows, four MMAs of K = 64), a STAGES-deep shared-memory ring.
+//
+//   warp 0      TMA producer: A and B tiles (128-byte swizzle) per stage
+//   warp 1      TMEM owner + MMA issuer (one thread): tcgen05.cp of the
+//               stage's scale atoms, four tcgen05.mma, tcgen05.commit
+//   warps 2-5   scale-atom builders during the main loop (row-major global
+//               scales -> the 128-row x 4 atom layout tcgen05.cp expects),
+//               then the epilogue (tcgen05.ld -> alpha, cast, store)
+//
+// No TMA multicast anywhere: every CTA loads its own tiles.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace aeoq {
+
+constexpr int kTcThreads = 192;
+constexpr int kTcStages = 4;
+constexpr int kKT = 256;            // K values per stage
+constexpr int kKTBytes = kKT / 2;   // 128 B per row per stage
+
+enum TcEpilogue : int { kEpiStore = 0, kEpiGeglu = 1, kEpiScaleRow = 2 };
+
+struct TcParams {
+  // problem
+  int64_t n_out;        // weight rows per expert (N of the reference, multiple of 128)
+  int64_t K;            // reduction length (multiple of 64)
+  int64_t num_experts;
+  // A (weights): tensor map over (num_experts * n_out) rows; scales row-major
+  const uint8_t* sfa;
+  int64_t sfa_ld;       // bytes per scale row (K / 16)
+  // B (activations): tensor map over b_rows rows; scales row-major
+  const uint8_t* sfb;
+  int64_t sfb_ld;
+  int64_t b_rows;       // rows addressable through the tensor map
+  // tiling of B rows into problems
+  int mode;             // 0: slots (blockIdx.z = slot), 1: grouped by expert (device offsets)
+  int64_t M;            // rows per slot (mode 0)
+  int64_t b_slot_rows;  // row offset between slots' activations (0 = shared)
+  const void* ids; int ids_dt;   // mode 0: slot -> expert (null = identity)
+  const int* grp_off;   // mode 1: [E+1] row offsets of each expert's rows
+  const int* tile_off;  // mode 1: [E+1] first token tile of each expert
+  // epilogue
+  int epi;
+  const void* a_ts; int a_ts_dt;          // alpha = f32(*a_ts) * f32(*w_ts) (kEpiStore / kEpiGeglu)
+  const void* w_ts; int w_ts_dt;
+  const float* grp_alpha_ts;              // kEpiScaleRow: per-expert activation scale (f32), times w_ts
+  const __nv_bfloat16* row_w;             // kEpiScaleRow: per-row weight (bf16)
+  void* c; int c_dt;                      // output
+  int64_t ldc;                            // bytes per output row
+  int64_t c_slot_stride;                  // bytes between slots (mode 0)
+  uint32_t* grp_amax;                     // kEpiGeglu: per-expert |h| max key (atomicMax)
+  int* err;                               // device error word (bounded waits)
+};
+
+struct TcSmem {
+  uint64_t full[kTcStages];
+  uint64_t empty[kTcStages];
+  uint64_t accum;
+  uint32_t tmem_base;
+};
+
+template <int BN>
+struct TcLayout {
+  static constexpr int kSfbAtoms = (BN + 127) / 128;
+  static constexpr size_t kA = 128 * kKTBytes;             // 16 KB
+  static constexpr size_t kB = (size_t)BN * kKTBytes;
+  static constexpr size_t kSfa = 4 * 512;
+  static constexpr size_t kSfb = (size_t)4 * 512 * kSfbAtoms;
+  static constexpr size_t kStage = kA + kB + kSfa + kSfb;
+  // GeGLU exchange of the up half (64 x BN f32) reuses the stage ring, which
+  // is idle once the accumulator is complete.
+  static constexpr size_t kXchg = 64 * (size_t)BN * 4;
+  static_assert(kXchg <= kTcStages * kStage, "exchange buffer must fit in the stage ring");
+  static constexpr size_t kBytes = 1024 + kTcStages * kStage + 256;
+  static constexpr uint32_t kTmemCols = (BN + 32 * kSfbAtoms + 16 <= 256) ? 256 : 512;
+  static constexpr uint32_t kSfaCol = BN;                  // 16 columns
+  static constexpr uint32_t kSfbCol = BN + 16;             // 16 * kSfbAtoms columns
+};
+
+// Resolve this CTA's problem: expert, first activation row, valid rows.
+struct TileInfo {
+  int64_t expert, b_row0, c_row0;
+  int n_valid;
+  int64_t slot;
+  bool active;
+};
+
+template <int BN>
+__device__ __forceinline__ TileInfo resolve_tile(const TcParams& p) {
+  TileInfo t{};
+  if (p.mode == 0) {
+    const int64_t s = blockIdx.z;
+    const int64_t tb = (int64_t)blockIdx.y * BN;
+    t.slot = s;
+    t.expert = p.ids ? load_index(p.ids, p.ids_dt, s) : s;
+    t.b_row0 = s * p.b_slot_rows + tb;
+    t.c_row0 = tb;
+    t.n_valid = (int)min((int64_t)BN, p.M - tb);
+    t.active = t.n_valid > 0;
+  } else {
+    const int y = blockIdx.y;
+    const int E = (int)p.num_experts;
+    if (y >= p.tile_off[E]) {
+      t.active = false;
+      return t;
+    }
+    int lo = 0, hi = E;   // largest e with tile_off[e] <= y
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (p.tile_off[mid] <= y) lo = mid; else hi = mid;
+    }
+    while (lo < E - 1 && p.tile_off[lo + 1] <= y) ++lo;
+    t.expert = lo;
+    const int64_t tb = (int64_t)(y - p.tile_off[lo]) * BN;
+    t.b_row0 = p.grp_off[lo] + tb;
+    t.c_row0 = t.b_row0;
+    t.n_valid = (int)min((int64_t)BN, (int64_t)(p.grp_off[lo + 1] - p.grp_off[lo]) - tb);
+    t.slot = 0;
+    t.active = t.n_valid > 0;
+  }
+  if (t.expert < 0 || t.expert >= p.num_experts) t.active = false;
+  return t;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                                      const __grid_constant__ CUtensorMap tmB,
+                                                                      const TcParams p) {
+  using L = TcLayout<BN>;
+  extern __shared__ __align__(1024) uint8_t dsmem[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~uintptr_t(1023));
+  uint8_t* stage0 = base;
+  float* xchg = reinterpret_cast<float*>(base);   // epilogue only (stage ring idle by then)
+  TcSmem* sh = reinterpret_cast<TcSmem*>(base + kTcStages * L::kStage);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  const TileInfo ti = resolve_tile<BN>(p);
+  if (!ti.active) return;   // whole CTA exits together before any sync
+  const int64_t m_tile = blockIdx.x;
+  const bool geglu = (p.epi == kEpiGeglu);
+  // A rows of this tile: 128 consecutive weight rows, or for GeGLU 64 gate
+  // rows (n0..n0+63) and the matching 64 up rows (n0 + n_out/2 ...).
+  const int64_t a_row_base = ti.expert * p.n_out;
+  const int num_kt = (int)((p.K + kKT - 1) / kKT);
+  const int kb_total = (int)(p.K / 64);
+
+  auto stA = [&](int s) { return stage0 + s * L::kStage; };
+  auto stB = [&](int s) { return stage0 + s * L::kStage + L::kA; };
+  auto stSFA = [&](int s) { return stage0 + s * L::kStage + L::kA + L::kB; };
+  auto stSFB = [&](int s) { return stage0 + s * L::kStage + L::kA + L::kB + L::kSfa; };
+
+  if (tid == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      sm100::mbar_init(&sh->full[s], 1 + 4);   // TMA arrival + 4 scale-builder warps
+      sm100::mbar_init(&sh->empty[s], 1);      // tcgen05.commit
+    }
+    sm100::mbar_init(&sh->accum, 1);
+    sm100::fence_barrier_init();
+    sm100::prefetch_tmap(&tmA);
+    sm100::prefetch_tmap(&tmB);
+  }
+  if (warp == 1) sm100::tmem_alloc(&sh->tmem_base, L::kTmemCols);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = sh->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint32_t bytes = (uint32_t)(L::kA + L::kB);
+      for (int kt = 0; kt < num_kt; ++kt) {
+        const int s = kt % kTcStages;
+        const uint32_t ph = (kt / kTcStages) & 1;
+        if (!sm100::mbar_wait(&sh->empty[s], ph ^ 1, p.err, 11)) break;
+        sm100::mbar_arrive_expect_tx(&sh->full[s], bytes);
+        const int32_t x = kt * kKTBytes;
+        if (geglu) {
+          const int64_t n0 = m_tile * 64;
+          sm100::tma_load_2d(stA(s), &tmA, x, (int32_t)(a_row_base + n0), &sh->full[s]);
+          sm100::tma_load_2d(stA(s) + 64 * kKTBytes, &tmA, x, (int32_t)(a_row_base + p.n_out / 2 + n0),
+                             &sh->full[s]);
+        } else {
+          sm100::tma_load_2d(stA(s), &tmA, x, (int32_t)(a_row_base + m_tile * 128), &sh->full[s]);
+        }
+        sm100::tma_load_2d(stB(s), &tmB, x, (int32_t)ti.b_row0, &sh->full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = sm100::idesc_nvf4(BN);
+      for (int kt = 0; kt < num_kt; ++kt) {
+        const int s = kt % kTcStages;
+        const uint32_t ph = (kt / kTcStages) & 1;
+        if (!sm100::mbar_wait(&sh->full[s], ph, p.err, 12)) break;
+        sm100::tc_fence_after();
+        const int nkb = min(4, kb_total - kt * 4);
+        for (int kb = 0; kb < nkb; ++kb) {
+          sm100::tc_cp_32x128b_warpx4(tmem + L::kSfaCol + 4 * kb, sm100::sdesc_sf_atom(sm100::smem_u32(stSFA(s) + kb * 512)));
+#pragma unroll
+          for (int a = 0; a < L::kSfbAtoms; ++a)
+            sm100::tc_cp_32x128b_warpx4(tmem + L::kSfbCol + 4 * (kb * L::kSfbAtoms + a),
+                                        sm100::sdesc_sf_atom(sm100::smem_u32(stSFB(s) + (kb * L::kSfbAtoms + a) * 512)));
+        }
+        for (int kb = 0; kb < nkb; ++kb) {
+          const uint64_t ad = sm100::sdesc_k_sw128(sm100::smem_u32(stA(s)) + kb * 32);
+          const uint64_t bd = sm100::sdesc_k_sw128(sm100::smem_u32(stB(s)) + kb * 32);
+          sm100::tc_mma_nvf4(tmem, ad, bd, idesc, tmem + L::kSfaCol + 4 * kb,
+                             tmem + L::kSfbCol + 4 * kb * L::kSfbAtoms, (kt | kb) ? 1u : 0u);
+        }
+        sm100::tc_commit(&sh->empty[s]);
+      }
+      sm100::tc_commit(&sh->accum);
+    }
+  } else {
+    // ------------------------------------------------ scale-atom builders
+    const int r = tid - 64;   // 0..127: one A row and one B row per thread
+    int64_t a_row;
+    if (geglu) a_row = a_row_base + (r < 64 ? m_tile * 64 + r : p.n_out / 2 + m_tile * 64 + (r - 64));
+    else a_row = a_row_base + m_tile * 128 + r;
+    const uint8_t* sfa_row = p.sfa + a_row * p.sfa_ld;
+    for (int kt = 0; kt < num_kt; ++kt) {
+      const int s = kt % kTcStages;
+      const uint32_t ph = (kt / kTcStages) & 1;
+      uint32_t va[4], vb[4 * L::kSfbAtoms];
+#pragma unroll
+      for (int kb = 0; kb < 4; ++kb) {
+        const int kbg = kt * 4 + kb;
+        va[kb] = kbg < kb_total ? *reinterpret_cast<const uint32_t*>(sfa_row + kbg * 4) : 0u;
+#pragma unroll
+        for (int a = 0; a < L::kSfbAtoms; ++a) {
+          const int br = r + 128 * a;
+          const int64_t brow = ti.b_row0 + br;
+          vb[kb * L::kSfbAtoms + a] = (kbg < kb_total && br < BN && brow < p.b_rows)
+                                          ? *reinterpret_cast<const uint32_t*>(p.sfb + brow * p.sfb_ld + kbg * 4)
+                                          : 0u;
+        }
+      }
+      if (lane == 0) sm100::mbar_wait(&sh->empty[s], ph ^ 1, p.err, 13);
+      __syncwarp();
+      const int off = (r & 31) * 16 + (r >> 5) * 4;
+#pragma unroll
+      for (int kb = 0; kb < 4; ++kb) {
+        *reinterpret_cast<uint32_t*>(stSFA(s) + kb * 512 + off) = va[kb];
+#pragma unroll
+        for (int a = 0; a < L::kSfbAtoms; ++a)
+          *reinterpret_cast<uint32_t*>(stSFB(s) + (kb * L::kSfbAtoms + a) * 512 + off) = vb[kb * L::kSfbAtoms + a];
+      }
+      sm100::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&sh->full[s]);
+    }
+
+    // ------------------------------------------------------------ epilogue
+    const bool ok = sm100::mbar_wait(&sh->accum, 0, p.err, 14);
+    sm100::tc_fence_after();
+    const int q = warp & 3;            // TMEM lane quadrant this warp may access
+    const int row = 32 * q + lane;     // accumulator row = weight row in the tile
+    float alpha;
+    if (p.epi == kEpiScaleRow) alpha = p.grp_alpha_ts[ti.expert] * load_scalar_f(p.w_ts, p.w_ts_dt);
+    else alpha = load_scalar_f(p.a_ts, p.a_ts_dt) * load_scalar_f(p.w_ts, p.w_ts_dt);
+    char* cbase = reinterpret_cast<char*>(p.c) + ti.slot * p.c_slot_stride;
+    uint32_t hkey = 0;
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      float v[16];
+      sm100::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+      if (!ok) continue;
+      if (p.epi == kEpiStore) {
+        const int64_t n = m_tile * 128 + row;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (c0 + j < ti.n_valid) {
+            char* dst = cbase + (ti.c_row0 + c0 + j) * p.ldc;
+            if (p.c_dt == AEOQ_BF16) reinterpret_cast<__nv_bfloat16*>(dst)[n] = __float2bfloat16_rn(v[j] * alpha);
+            else reinterpret_cast<float*>(dst)[n] = v[j] * alpha;
+          }
+        }
+      } else if (p.epi == kEpiScaleRow) {
+        const int64_t n = m_tile * 128 + row;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (c0 + j < ti.n_valid) {
+            const int64_t crow = ti.c_row0 + c0 + j;
+            const float w = __bfloat162float(p.row_w[crow]);
+            reinterpret_cast<__nv_bfloat16*>(cbase + crow * p.ldc)[n] = __float2bfloat16_rn(bf16r(v[j] * alpha) * w);
+          }
+        }
+      } else {
+        // GeGLU: rows 64..127 (up) hand bf16(alpha*acc) to rows 0..63 (gate)
+        if (row >= 64) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) xchg[(row - 64) * BN + c0 + j] = bf16r(v[j] * alpha);
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (row < 64) {
+          const int64_t n = m_tile * 64 + row;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            if (c0 + j < ti.n_valid) {
+              const float g = bf16r(v[j] * alpha);
+              const float u = xchg[row * BN + c0 + j];
+              const __nv_bfloat16 hv = __float2bfloat16_rn(bf16r(gelu_tanh(g)) * u);
+              reinterpret_cast<__nv_bfloat16*>(cbase + (ti.c_row0 + c0 + j) * p.ldc)[n] = hv;
+              hkey = max(hkey, In<AEOQ_BF16>::abs_key(hv));
+            }
+          }
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
+    }
+    if (p.epi == kEpiGeglu && p.grp_amax) {
+      hkey = warp_umax(hkey);
+      if (lane == 0 && hkey) atomicMax(p.grp_amax + ti.expert, hkey);
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, L::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// 2D uint8 tensor map: rows x row_bytes (row stride ld), box 128 B x box_rows, 128-byte swizzle.
+static int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int64_t row_bytes, int64_t ld, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(AEOQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld};
+  cuuint32_t box[2] = {(cuuint32_t)kKTBytes, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(AEOQ_ERR_INVALID, "tensor map encode failed (%d)", (int)r);
+  return AEOQ_OK;
+}
+
+template <int BN>
+static int launch_tc(const uint8_t* a, int64_t a_rows, const uint8_t* b, const TcParams& p, dim3 grid,
+                     cudaStream_t st) {
+  using L = TcLayout<BN>;
+  CUtensorMap ta, tb;
+  int rc = make_tmap(&ta, a, a_rows, p.K / 2, p.K / 2, p.epi == kEpiGeglu ? 64 : 128);
+  if (rc) return rc;
+  rc = make_tmap(&tb, b, p.b_rows, p.K / 2, p.K / 2, BN);
+  if (rc) return rc;
+  static size_t set_bytes[4] = {0, 0, 0, 0};
+  const int slot = BN == 32 ? 0 : BN == 64 ? 1 : BN == 128 ? 2 : 3;
+  if (set_bytes[slot] < L::kBytes) {
+    cudaError_t e = cudaFuncSetAttribute(nvfp4_tc_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)L::kBytes);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(AEOQ_ERR_CUDA, "tc_gemm: smem attribute: %s", cudaGetErrorString(e));
+    }
+    set_bytes[slot] = L::kBytes;
+  }
+  nvfp4_tc_gemm_kernel<BN><<<grid, kTcThreads, L::kBytes, st>>>(ta, tb, p);
+  return check_launch("nvfp4_tc_gemm_kernel");
+}
+
+int tc_gemm_dispatch(int bn, const uint8_t* a, int64_t a_rows, const uint8_t* b, const TcParams& p, dim3 grid,
+                     cudaStream_t st) {
+  switch (bn) {
+    case 32: return launch_tc<32>(a, a_rows, b, p, grid, st);
+    case 64: return launch_tc<64>(a, a_rows, b, p, grid, st);
+    case 128: return launch_tc<128>(a, a_rows, b, p, grid, st);
+    case 256: return launch_tc<256>(a, a_rows, b, p, grid, st);
+  }
+  return set_error(AEOQ_ERR_INVALID, "tc_gemm: unsupported tile N %d", bn);
+}
+
+static int pick_bn(int64_t M) {
+  if (M <= 32) return 32;
+  if (M <= 64) return 64;
+  if (M <= 128) return 128;
+  return 256;
+}
+
+}  // namespace aeoq
+
+using namespace aeoq;
+
+// Tensor-core path of aeoq_nvfp4_gemm for contiguous operands: A/B packed rows
+// of K/2 bytes, scale rows of K/16 bytes (the reference tensors' layouts).
+extern "C" int aeoq_nvfp4_gemm_tc(const uint8_t* a, const uint8_t* a_sf, const void* a_ts, int a_ts_dtype,
+                                  int64_t a_slot_rows, const uint8_t* w, const uint8_t* w_sf, const void* w_ts,
+                                  int w_ts_dtype, int64_t num_experts, const void* expert_ids, int ids_dtype,
+                                  int64_t slots, int64_t M, int64_t N, int64_t K, void* c, int c_dtype,
+                                  int* err_word, void* stream) {
+  AEOQ_REQUIRE(slots >= 0 && M >= 0 && N >= 0 && K >= 0, AEOQ_ERR_INVALID, "nvfp4_gemm_tc: negative shape");
+  AEOQ_REQUIRE(N % 128 == 0, AEOQ_ERR_INVALID, "nvfp4_gemm_tc: N (%lld) must be a multiple of 128", (long long)N);
+  AEOQ_REQUIRE(K % 64 == 0 && K > 0, AEOQ_ERR_INVALID, "nvfp4_gemm_tc: K (%lld) must be a multiple of 64",
+               (long long)K);
+  AEOQ_REQUIRE((K / 2) % 16 == 0, AEOQ_ERR_INVALID, "nvfp4_gemm_tc: K/2 must be a multiple of 16");
+  AEOQ_REQUIRE(c_dtype == AEOQ_BF16 || c_dtype == AEOQ_F32, AEOQ_ERR_INVALID, "nvfp4_gemm_tc: bad output dtype");
+  if (slots * M * N == 0) return AEOQ_OK;
+  AEOQ_REQUIRE(a && a_sf && a_ts && w && w_sf && w_ts && c && err_word, AEOQ_ERR_INVALID,
+               "nvfp4_gemm_tc: null pointer");
+  AEOQ_REQUIRE((uintptr_t)a % 16 == 0 && (uintptr_t)w % 16 == 0 && (uintptr_t)a_sf % 4 == 0 &&
+                   (uintptr_t)w_sf % 4 == 0,
+               AEOQ_ERR_INVALID, "nvfp4_gemm_tc: operands must be 16-byte aligned, scales 4-byte aligned");
+  TcParams p{};
+  p.n_out = N;
+  p.K = K;
+  p.num_experts = num_experts;
+  p.sfa = w_sf;
+  p.sfa_ld = K / 16;
+  p.sfb = a_sf;
+  p.sfb_ld = K / 16;
+  p.b_rows = a_slot_rows ? slots * M : M;
+  p.mode = 0;
+  p.M = M;
+  p.b_slot_rows = a_slot_rows ? M : 0;
+  p.ids = expert_ids;
+  p.ids_dt = ids_dtype;
+  p.epi = kEpiStore;
+  p.a_ts = a_ts; p.a_ts_dt = a_ts_dtype;
+  p.w_ts = w_ts; p.w_ts_dt = w_ts_dtype;
+  p.c = c;
+  p.c_dt = c_dtype;
+  const int es = c_dtype == AEOQ_BF16 ? 2 : 4;
+  p.ldc = N * es;
+  p.c_slot_stride = M * N * es;
+  p.err = err_word;
+  const int bn = pick_bn(M);
+  dim3 grid((unsigned)(N / 128), (unsigned)((M + bn - 1) / bn), (unsigned)slots);
+  return tc_gemm_dispatch(bn, w, num_experts * N, a, p, grid, (cudaStream_t)stream);
+}

@@ -122,6 +122,19 @@ AEOQ_API int aeoq_nvfp4_gemm(const uint8_t* a, const uint8_t* a_sf, const void* 
                     void* c, int c_dtype, int64_t c_slot_stride, int64_t c_row_stride,
                     void* stream);
 
+/* Tensor-core (tcgen05, kind::mxf4nvf4) path of aeoq_nvfp4_gemm for
+ * contiguous operands: activation rows of K/2 bytes (a_slot_rows != 0: each
+ * slot has its own M rows; 0: one M-row activation shared by every slot),
+ * weights [num_experts, N, K/2], scales [.., K/16], C [slots, M, N].
+ * N % 128 == 0, K % 64 == 0. `err_word` is a device int that a bounded wait
+ * sets non-zero if the pipeline stalls (never expected). Same replaced
+ * reference functions as aeoq_nvfp4_gemm (nvfp4_matmul.py:399-864). */
+AEOQ_API int aeoq_nvfp4_gemm_tc(const uint8_t* a, const uint8_t* a_sf, const void* a_ts, int a_ts_dtype,
+                                int64_t a_slot_rows, const uint8_t* w, const uint8_t* w_sf, const void* w_ts,
+                                int w_ts_dtype, int64_t num_experts, const void* expert_ids, int ids_dtype,
+                                int64_t slots, int64_t M, int64_t N, int64_t K, void* c, int c_dtype,
+                                int* err_word, void* stream);
+
 /* ------------------------------------------------------------------------
  * One-token NVFP4 MoE expert forward, fully fused (two launches).
  * Replaces Gemma4TextExpertsNVFP4._forward_decode_3d
