@@ -43,6 +43,12 @@ _SIGS["aeoq_moe_nvfp4_decode_fused"] = _SIGS["aeoq_moe_nvfp4_decode"]
 _SIGS["aeoq_moe_nvfp4_decode_fused_supported"] = [_L, _L, _L]
 _SIGS["aeoq_moe_nvfp4_decode_fused_workspace_size"] = [_L, _L, _L]
 _SIGS["aeoq_moe_nvfp4_decode_fused_noalloc_max_scratch"] = []
+_SIGS["aeoq_nvfp4_gemm_grouped"] = [_P, _P, _L, _P, _P, _I, _P, _P, _L, _L, _L, _I, _P, _I, _P, _I, _P, _P,
+                                     _P, _P, _L, _P, _P]
+_SIGS["aeoq_moe_route"] = [_P, _I, _P, _L, _L, _L, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]
+_SIGS["aeoq_gather_rows"] = [_P, _P, _P, _P, _L, _L, _L, _P, _P, _P]
+_SIGS["aeoq_requant_rows"] = [_P, _L, _P, _P, _L, _P, _L, _I, _P, _P, _P, _P]
+_SIGS["aeoq_moe_combine"] = [_P, _P, _P, _I, _L, _L, _L, _I, _P, _P]
 _SIGS["aeoq_nvfp4_gemm_tc"] = [_P, _P, _P, _I, _L, _P, _P, _P, _I, _L, _P, _I, _L, _L, _L, _L, _P, _I, _P, _P]
 _SIGS["aeoq_moe_nvfp4_decode_fused_noalloc"] = [_P, _P, _I, _P, _L, _P, _P, _P, _I, _P, _P, _P, _I, _L, _L, _L,
                                                 _P, _P]

@@ -7,10 +7,8 @@ library.
 from __future__ import annotations
 
 import torch
-import torch.nn as nn
 
 from ... import _capi as A
-from ...gpu import nvfp4_matmul as NM
 from ...gpu.quant import quantize_2d_to_nvfp4
 
 
@@ -63,25 +61,101 @@ def nvfp4_decode(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf
     return out
 
 
+def pick_tile_n(n_pairs: int, num_experts: int) -> int:
+    """Token-tile width of the grouped GEMMs from the mean rows per expert."""
+    avg = max(1, n_pairs // max(1, min(num_experts, n_pairs)))
+    for bn in (8, 16, 32, 64, 128):
+        if avg <= bn:
+            return bn
+    return 256
+
+
+class _Route:
+    """Device buffers of one routing: expert-sorted rows of the (token, slot) pairs."""
+
+    def __init__(self, lib, top_k_index, top_k_weights, E, tile_n):
+        dev = top_k_index.device
+        T, k = top_k_index.shape
+        P = T * k
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.P, self.T, self.k, self.E, self.tile_n = P, T, k, E, tile_n
+        self.cnt = torch.empty(E, **i32)
+        self.fill = torch.empty(E, **i32)
+        self.grp_off = torch.empty(E + 1, **i32)
+        self.tile_off = torch.empty(E + 1, **i32)
+        self.pair_row = torch.empty(P, **i32)
+        self.row_tok = torch.empty(P, **i32)
+        self.row_exp = torch.empty(P, **i32)
+        self.row_w = torch.empty(P, dtype=torch.bfloat16, device=dev)
+        self.ids = top_k_index.contiguous()
+        w = top_k_weights.to(torch.bfloat16).contiguous()
+        A.check(lib.aeoq_moe_route(self.ids.data_ptr(), A.dtype_code(self.ids.dtype), w.data_ptr(), T, k, E, tile_n,
+                                   self.cnt.data_ptr(), self.fill.data_ptr(), self.grp_off.data_ptr(),
+                                   self.tile_off.data_ptr(), self.pair_row.data_ptr(), self.row_tok.data_ptr(),
+                                   self.row_w.data_ptr(), self.row_exp.data_ptr(), A.stream_ptr(dev)))
+
+    @property
+    def n_rows_ptr(self):
+        return self.grp_off.data_ptr() + 4 * self.E
+
+
+def nvfp4_experts_grouped(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf, dw_ts,
+                          one_token_semantics=False):
+    """Expert forward over any number of tokens on the device, no host sync.
+
+    Prefill semantics (modeling_nvfp4.py:188-255): one global activation
+    quant, per-expert gate_up, GeGLU, per-expert re-quantized down, weighted
+    combine folded in expert order with bf16 rounding after each add. With
+    ``one_token_semantics`` the down input shares one tensor scale and the
+    combine sums in f32 (modeling_nvfp4.py:132-186).
+    """
+    A.require_cuda(hidden, top_k_index, top_k_weights, gu, dw)
+    lib = A.load()
+    dev = hidden.device
+    E, two_i, h_half = gu.shape
+    H, I = h_half * 2, two_i // 2
+    T = hidden.shape[0]
+    k = top_k_index.shape[-1]
+    P = T * k
+    st = A.stream_ptr(dev)
+    err = A.err_word(dev)
+    tile_n = pick_tile_n(P, E)
+    r = _Route(lib, top_k_index.reshape(T, k), top_k_weights.reshape(T, k), E, tile_n)
+    hp, hs, hts = quantize_2d_to_nvfp4(hidden)                                   # (:203-206)
+    a_sorted = torch.empty(P, H // 2, dtype=torch.uint8, device=dev)
+    a_sorted_sf = torch.empty(P, H // 16, dtype=torch.uint8, device=dev)
+    A.check(lib.aeoq_gather_rows(hp.data_ptr(), hs.data_ptr(), r.row_tok.data_ptr(), r.n_rows_ptr, P, H // 2,
+                                 H // 16, a_sorted.data_ptr(), a_sorted_sf.data_ptr(), st))
+    amax = torch.zeros(E, dtype=torch.int32, device=dev)
+    h_sorted = torch.empty(P, I, dtype=torch.bfloat16, device=dev)
+    A.check(lib.aeoq_nvfp4_gemm_grouped(a_sorted.data_ptr(), a_sorted_sf.data_ptr(), P, r.grp_off.data_ptr(),
+                                        r.tile_off.data_ptr(), tile_n, gu.data_ptr(), gu_sf.data_ptr(), E, 2 * I, H,
+                                        1, hts.data_ptr(), A.dtype_code(hts.dtype), gu_ts.data_ptr(),
+                                        A.dtype_code(gu_ts.dtype), None, None, amax.data_ptr(), h_sorted.data_ptr(),
+                                        I * 2, err.data_ptr(), st))
+    hq = torch.empty(P, I // 2, dtype=torch.uint8, device=dev)
+    hq_sf = torch.empty(P, I // 16, dtype=torch.uint8, device=dev)
+    ts_e = torch.empty(E, dtype=torch.float32, device=dev)
+    A.check(lib.aeoq_requant_rows(h_sorted.data_ptr(), I, r.row_exp.data_ptr(), r.n_rows_ptr, P, amax.data_ptr(), E,
+                                  1 if one_token_semantics else 0, hq.data_ptr(), hq_sf.data_ptr(),
+                                  ts_e.data_ptr(), st))
+    c_sorted = torch.empty(P, H, dtype=torch.bfloat16, device=dev)
+    A.check(lib.aeoq_nvfp4_gemm_grouped(hq.data_ptr(), hq_sf.data_ptr(), P, r.grp_off.data_ptr(),
+                                        r.tile_off.data_ptr(), tile_n, dw.data_ptr(), dw_sf.data_ptr(), E, H, I,
+                                        2, None, 0, dw_ts.data_ptr(), A.dtype_code(dw_ts.dtype), ts_e.data_ptr(),
+                                        r.row_w.data_ptr(), None, c_sorted.data_ptr(), H * 2, err.data_ptr(), st))
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    A.check(lib.aeoq_moe_combine(c_sorted.data_ptr(), r.pair_row.data_ptr(), r.ids.data_ptr(),
+                                 A.dtype_code(r.ids.dtype), T, k, H, 1 if one_token_semantics else 0,
+                                 out.data_ptr(), st))
+    return out
+
+
 def nvfp4_prefill(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf, dw_ts, num_experts):
-    """Many-token forward (modeling_nvfp4.py:188-255)."""
-    h_packed, h_block_scale, h_tensor_scale = quantize_2d_to_nvfp4(hidden)
-    final_hidden_states = torch.zeros_like(hidden)
-    with torch.no_grad():
-        expert_mask = nn.functional.one_hot(top_k_index, num_classes=num_experts).permute(2, 1, 0)
-        expert_hit = torch.greater(expert_mask.sum(dim=(-1, -2)), 0).nonzero()
-    I = gu.shape[1] // 2
-    for expert_idx in expert_hit:
-        expert_idx = expert_idx[0]
-        if expert_idx == num_experts:
-            continue
-        top_k_pos, token_idx = torch.where(expert_mask[expert_idx])
-        gate_up = NM.nvfp4_linear_prequantized(
-            h_packed[token_idx], h_block_scale[token_idx], h_tensor_scale,
-            gu[expert_idx], gu_sf[expert_idx], gu_ts)
-        gate, up = gate_up[:, :I], gate_up[:, I:]
-        cur = nn.functional.gelu(gate, approximate="tanh") * up
-        cur = NM.nvfp4_linear(cur, dw[expert_idx], dw_sf[expert_idx], dw_ts)
-        cur *= top_k_weights[token_idx, top_k_pos, None]
-        final_hidden_states.index_add_(0, token_idx, cur.to(final_hidden_states.dtype))
-    return final_hidden_states
+    """Many-token forward (modeling_nvfp4.py:188-255), all on the device."""
+    if hidden.dtype != torch.bfloat16:
+        raise ValueError(f"hidden_states must be bfloat16, got {hidden.dtype}")
+    if gu.shape[0] != num_experts:
+        raise ValueError(f"gate_up_proj holds {gu.shape[0]} experts, config says {num_experts}")
+    return nvfp4_experts_grouped(hidden.contiguous(), top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf,
+                                 dw_ts)

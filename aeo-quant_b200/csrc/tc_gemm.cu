@@ -385,8 +385,8 @@ static int launch_tc(const uint8_t* a, int64_t a_rows, const uint8_t* b, const T
   if (rc) return rc;
   rc = make_tmap(&tb, b, p.b_rows, p.K / 2, p.K / 2, BN);
   if (rc) return rc;
-  static size_t set_bytes[4] = {0, 0, 0, 0};
-  const int slot = BN == 32 ? 0 : BN == 64 ? 1 : BN == 128 ? 2 : 3;
+  static size_t set_bytes[6] = {0, 0, 0, 0, 0, 0};
+  const int slot = BN == 8 ? 4 : BN == 16 ? 5 : BN == 32 ? 0 : BN == 64 ? 1 : BN == 128 ? 2 : 3;
   if (set_bytes[slot] < L::kBytes) {
     cudaError_t e = cudaFuncSetAttribute(nvfp4_tc_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)L::kBytes);
@@ -403,6 +403,8 @@ static int launch_tc(const uint8_t* a, int64_t a_rows, const uint8_t* b, const T
 int tc_gemm_dispatch(int bn, const uint8_t* a, int64_t a_rows, const uint8_t* b, const TcParams& p, dim3 grid,
                      cudaStream_t st) {
   switch (bn) {
+    case 8: return launch_tc<8>(a, a_rows, b, p, grid, st);
+    case 16: return launch_tc<16>(a, a_rows, b, p, grid, st);
     case 32: return launch_tc<32>(a, a_rows, b, p, grid, st);
     case 64: return launch_tc<64>(a, a_rows, b, p, grid, st);
     case 128: return launch_tc<128>(a, a_rows, b, p, grid, st);
@@ -412,6 +414,8 @@ int tc_gemm_dispatch(int bn, const uint8_t* a, int64_t a_rows, const uint8_t* b,
 }
 
 static int pick_bn(int64_t M) {
+  if (M <= 8) return 8;
+  if (M <= 16) return 16;
   if (M <= 32) return 32;
   if (M <= 64) return 64;
   if (M <= 128) return 128;
@@ -467,4 +471,54 @@ extern "C" int aeoq_nvfp4_gemm_tc(const uint8_t* a, const uint8_t* a_sf, const v
   const int bn = pick_bn(M);
   dim3 grid((unsigned)(N / 128), (unsigned)((M + bn - 1) / bn), (unsigned)slots);
   return tc_gemm_dispatch(bn, w, num_experts * N, a, p, grid, (cudaStream_t)stream);
+}
+
+// Grouped (MoE) path: B rows are sorted by expert; expert e owns rows
+// [grp_off[e], grp_off[e+1]) and token tiles [tile_off[e], tile_off[e+1]) of
+// tile_n rows. epi: 0 store alpha*acc (bf16), 1 GeGLU over the gate/up halves
+// (N = 2I weight rows, output I wide, per-expert amax keys), 2 down with
+// bf16(bf16(grp_ts[e]*w_ts*acc) * row_w[r]).
+extern "C" int aeoq_nvfp4_gemm_grouped(const uint8_t* b, const uint8_t* b_sf, int64_t max_rows, const int* grp_off,
+                                       const int* tile_off, int tile_n, const uint8_t* w, const uint8_t* w_sf,
+                                       int64_t num_experts, int64_t N, int64_t K, int epi, const void* a_ts,
+                                       int a_ts_dtype, const void* w_ts, int w_ts_dtype, const float* grp_ts,
+                                       const void* row_w, uint32_t* grp_amax, void* c, int64_t ldc, int* err_word,
+                                       void* stream) {
+  AEOQ_REQUIRE(N % 128 == 0 && K % 64 == 0 && K > 0 && (K / 2) % 16 == 0, AEOQ_ERR_INVALID,
+               "nvfp4_gemm_grouped: N %% 128 == 0 and K %% 64 == 0 required");
+  AEOQ_REQUIRE(epi >= 0 && epi <= 2, AEOQ_ERR_INVALID, "nvfp4_gemm_grouped: bad epilogue %d", epi);
+  AEOQ_REQUIRE(tile_n == 8 || tile_n == 16 || tile_n == 32 || tile_n == 64 || tile_n == 128 || tile_n == 256,
+               AEOQ_ERR_INVALID, "nvfp4_gemm_grouped: tile_n must be 8..256, a power of two");
+  AEOQ_REQUIRE(num_experts >= 1 && num_experts <= 1024, AEOQ_ERR_INVALID, "nvfp4_gemm_grouped: bad expert count");
+  if (max_rows <= 0) return AEOQ_OK;
+  AEOQ_REQUIRE(b && b_sf && grp_off && tile_off && w && w_sf && w_ts && c && err_word, AEOQ_ERR_INVALID,
+               "nvfp4_gemm_grouped: null pointer");
+  AEOQ_REQUIRE(epi != 2 || (grp_ts && row_w), AEOQ_ERR_INVALID, "nvfp4_gemm_grouped: down epilogue needs scales");
+  AEOQ_REQUIRE(epi == 2 || a_ts, AEOQ_ERR_INVALID, "nvfp4_gemm_grouped: activation scale missing");
+  TcParams p{};
+  p.n_out = N;
+  p.K = K;
+  p.num_experts = num_experts;
+  p.sfa = w_sf;
+  p.sfa_ld = K / 16;
+  p.sfb = b_sf;
+  p.sfb_ld = K / 16;
+  p.b_rows = max_rows;
+  p.mode = 1;
+  p.grp_off = grp_off;
+  p.tile_off = tile_off;
+  p.epi = epi;
+  p.a_ts = a_ts; p.a_ts_dt = a_ts_dtype;
+  p.w_ts = w_ts; p.w_ts_dt = w_ts_dtype;
+  p.grp_alpha_ts = grp_ts;
+  p.row_w = reinterpret_cast<const __nv_bfloat16*>(row_w);
+  p.c = c;
+  p.c_dt = AEOQ_BF16;
+  p.ldc = ldc;
+  p.grp_amax = grp_amax;
+  p.err = err_word;
+  const int64_t max_tiles = (max_rows + tile_n - 1) / tile_n + num_experts;
+  const unsigned gx = (unsigned)(epi == kEpiGeglu ? (N / 2) / 64 : N / 128);
+  dim3 grid(gx, (unsigned)max_tiles, 1);
+  return tc_gemm_dispatch(tile_n, w, num_experts * N, b, p, grid, (cudaStream_t)stream);
 }

@@ -135,6 +135,51 @@ AEOQ_API int aeoq_nvfp4_gemm_tc(const uint8_t* a, const uint8_t* a_sf, const voi
                                 int64_t slots, int64_t M, int64_t N, int64_t K, void* c, int c_dtype,
                                 int* err_word, void* stream);
 
+/* Grouped tensor-core GEMM over expert-sorted activation rows (the MoE
+ * prefill path). Expert e owns sorted rows [grp_off[e], grp_off[e+1]) and
+ * token tiles [tile_off[e], tile_off[e+1]) of tile_n rows (as produced by
+ * aeoq_moe_route). epi 0: C = bf16(f32(*a_ts) * f32(*w_ts) * acc);
+ * epi 1 (gate_up, N = 2I): C[r][0..I) = bf16(bf16(gelu(g)) * u), with the
+ * per-expert max |C| accumulated into grp_amax keys (zero them first);
+ * epi 2 (down): C = bf16(bf16(grp_ts[e] * f32(*w_ts) * acc) * row_w[r]).
+ * Replaces the per-expert nvfp4_linear_prequantized / nvfp4_linear calls,
+ * GeGLU and weighting of _forward_prefill (modeling_nvfp4.py:218-249). */
+AEOQ_API int aeoq_nvfp4_gemm_grouped(const uint8_t* b, const uint8_t* b_sf, int64_t max_rows, const int* grp_off,
+                                     const int* tile_off, int tile_n, const uint8_t* w, const uint8_t* w_sf,
+                                     int64_t num_experts, int64_t N, int64_t K, int epi, const void* a_ts,
+                                     int a_ts_dtype, const void* w_ts, int w_ts_dtype, const float* grp_ts,
+                                     const void* row_w, uint32_t* grp_amax, void* c, int64_t ldc, int* err_word,
+                                     void* stream);
+
+/* Device-side grouping of (token, slot) pairs by expert (replaces the
+ * one_hot / nonzero / where scaffolding, modeling_nvfp4.py:208-222, and
+ * modeling.py:111-121): counts, row offsets, token-tile offsets for tile_n,
+ * pair -> sorted row, and per sorted row its token, routing weight and
+ * expert. Arrays: cnt/fill [E] (scratch), grp_off/tile_off [E+1],
+ * pair_row [T*k] (-1 for ids outside [0,E)), row_tok/row_w(bf16)/row_exp [T*k]. */
+AEOQ_API int aeoq_moe_route(const void* top_k_index, int idx_dtype, const void* top_k_weights, int64_t T,
+                            int64_t k, int64_t num_experts, int tile_n, int* cnt, int* fill, int* grp_off,
+                            int* tile_off, int* pair_row, int* row_tok, void* row_w, int* row_exp, void* stream);
+
+/* dst[r] = src[row_tok[r]] for r < *n_rows (packed rows and scale rows). */
+AEOQ_API int aeoq_gather_rows(const uint8_t* src, const uint8_t* src_sf, const int* row_tok, const int* n_rows,
+                              int64_t max_rows, int64_t row_bytes, int64_t sf_bytes, uint8_t* dst, uint8_t* dst_sf,
+                              void* stream);
+
+/* NVFP4 re-quantization of the sorted GeGLU rows: one tensor scale per
+ * expert from amax_key[e] (shared_scale = 0; per-expert nvfp4_linear in the
+ * prefill path, nvfp4_matmul.py:386) or one for all rows (shared_scale = 1;
+ * the one-token path, modeling_nvfp4.py:164-172). ts_out[e] gets the scales. */
+AEOQ_API int aeoq_requant_rows(const void* h, int64_t I, const int* row_exp, const int* n_rows, int64_t max_rows,
+                               const uint32_t* amax_key, int64_t num_experts, int shared_scale, uint8_t* hq,
+                               uint8_t* hsf, float* ts_out, void* stream);
+
+/* out[t] = fold over token t's expert outputs in ascending expert order:
+ * mode 0 bf16 rounding after every add (index_add_, modeling_nvfp4.py:250-253);
+ * mode 1 f32 sum rounded once (modeling_nvfp4.py:181-186). */
+AEOQ_API int aeoq_moe_combine(const void* c_sorted, const int* pair_row, const void* top_k_index, int idx_dtype,
+                              int64_t T, int64_t k, int64_t H, int mode, void* out, void* stream);
+
 /* ------------------------------------------------------------------------
  * One-token NVFP4 MoE expert forward, fully fused (two launches).
  * Replaces Gemma4TextExpertsNVFP4._forward_decode_3d

@@ -76,7 +76,7 @@ def oracle_module(m, experts):
     return om, remap
 
 
-@pytest.mark.parametrize("B,seed", [(1, 0), (1, 1), (1, 2), (4, 3), (16, 4)])
+@pytest.mark.parametrize("B,seed", [(1, 0), (1, 1), (1, 2), (4, 3), (16, 4), (64, 5), (200, 6)])
 def test_full_size_vs_oracle(full_layer, B, seed):
     m = full_layer
     h = randn_bf16((B, 2816), 1.0, 200 + seed)
@@ -146,3 +146,18 @@ def test_decode_invalid_expert_contributes_zero(full_layer):
     # the dropped slot still shares the h tensor scale; compare loosely
     assert np.all(np.isfinite(bf16_to_np(y)))
     assert max_rel_err(bf16_to_np(y), ref_h) < 0.05
+
+
+def test_grouped_one_token_semantics_matches_fused(full_layer):
+    """The device-grouped pipeline run with one-token semantics (shared down
+    scale, f32 combine) agrees with the cooperative decode kernel."""
+    from aeo_quant_b200.bridges.gemma4 import moe_ops
+    m = full_layer
+    for seed in range(3):
+        h = randn_bf16((1, 2816), 1.0, 1100 + seed)
+        idx, w = routing(1, 128, 8, 1200 + seed)
+        args = (h, idx.cuda(), w.cuda(), m.gate_up_proj, m.gate_up_proj_scale, m.gate_up_proj_scale_2,
+                m.down_proj, m.down_proj_scale, m.down_proj_scale_2)
+        y1 = moe_ops.nvfp4_decode(*args)
+        y2 = moe_ops.nvfp4_experts_grouped(*args, one_token_semantics=True)
+        assert max_rel_err(bf16_to_np(y2), bf16_to_np(y1)) <= TOL
