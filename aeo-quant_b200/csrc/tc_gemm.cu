@@ -310,14 +310,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
         // GeGLU: rows 64..127 (up) hand bf16(alpha*acc) to rows 0..63 (gate)
         if (row >= 64) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) xchg[(row - 64) * BN + c0 + j] = bf16r(v[j] * alpha);
+          for (int j = 0; j < 16; ++j)
+            if (c0 + j < BN) xchg[(row - 64) * BN + c0 + j] = bf16r(v[j] * alpha);
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (row < 64) {
           const int64_t n = m_tile * 64 + row;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            if (c0 + j < ti.n_valid) {
+            if (c0 + j < ti.n_valid && c0 + j < BN) {
               const float g = bf16r(v[j] * alpha);
               const float u = xchg[row * BN + c0 + j];
               const __nv_bfloat16 hv = __float2bfloat16_rn(bf16r(gelu_tanh(g)) * u);
