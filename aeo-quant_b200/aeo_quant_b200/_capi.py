@@ -46,13 +46,19 @@ _SIGS["aeoq_moe_nvfp4_decode_fused_noalloc_max_scratch"] = []
 _SIGS["aeoq_nvfp4_gemm_grouped"] = [_P, _P, _L, _P, _P, _I, _P, _P, _L, _L, _L, _I, _P, _I, _P, _I, _P, _P,
                                      _P, _P, _L, _P, _P]
 _SIGS["aeoq_moe_route"] = [_P, _I, _P, _L, _L, _L, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]
-_SIGS["aeoq_gather_rows"] = [_P, _P, _P, _P, _L, _L, _L, _P, _P, _P]
-_SIGS["aeoq_requant_rows"] = [_P, _L, _P, _P, _L, _P, _L, _I, _P, _P, _P, _P]
+_SIGS["aeoq_gather_rows"] = [_P, _P, _P, _P, _P, _P, _I, _P, _L, _L, _L, _P, _P, _P]
+_SIGS["aeoq_requant_rows"] = [_P, _L, _P, _P, _P, _I, _P, _L, _P, _L, _I, _P, _P, _P, _P]
+_SIGS["aeoq_nvfp4_tile_n"] = [_L]
+_SIGS["aeoq_nvfp4_weight_atoms_size"] = [_L, _L]
+_SIGS["aeoq_nvfp4_act_atoms_size"] = [_L, _L, _I]
+_SIGS["aeoq_nvfp4_sf_to_atoms"] = [_P, _L, _L, _L, _L, _P, _P]
+_SIGS["aeoq_nvfp4_rows_to_tile_atoms"] = [_P, _L, _L, _L, _I, _P, _P]
 _SIGS["aeoq_moe_combine"] = [_P, _P, _P, _I, _L, _L, _L, _I, _P, _P]
-_SIGS["aeoq_nvfp4_gemm_tc"] = [_P, _P, _P, _I, _L, _P, _P, _P, _I, _L, _P, _I, _L, _L, _L, _L, _P, _I, _P, _P]
+_SIGS["aeoq_nvfp4_gemm_tc"] = [_P, _P, _P, _I, _L, _P, _P, _P, _I, _L, _P, _I, _L, _L, _L, _L, _I, _P, _I, _P, _P]
 _SIGS["aeoq_moe_nvfp4_decode_fused_noalloc"] = [_P, _P, _I, _P, _L, _P, _P, _P, _I, _P, _P, _P, _I, _L, _L, _L,
                                                 _P, _P]
-_RESTYPE = {"aeoq_last_error": C.c_char_p, "aeoq_nvfp4_quantize_workspace_size": C.c_size_t,
+_RESTYPE = {"aeoq_nvfp4_weight_atoms_size": C.c_size_t, "aeoq_nvfp4_act_atoms_size": C.c_size_t,
+            "aeoq_last_error": C.c_char_p, "aeoq_nvfp4_quantize_workspace_size": C.c_size_t,
             "aeoq_moe_nvfp4_decode_workspace_size": C.c_size_t,
             "aeoq_moe_nvfp4_decode_fused_workspace_size": C.c_size_t,
             "aeoq_moe_nvfp4_decode_fused_noalloc_max_scratch": C.c_size_t}
@@ -133,4 +139,28 @@ def err_word(device: torch.device) -> torch.Tensor:
     if t is None:
         t = torch.zeros(1, dtype=torch.int32, device=device)
         _ERR_WORDS[key] = t
+    return t
+
+
+# Weight scale atoms are derived once per weight tensor and cached here,
+# keyed on the tensor's storage, shape and version counter (an in-place
+# update of the scales invalidates the entry).
+_ATOMS: dict = {}
+_ATOMS_MAX = 256
+
+
+def weight_atoms(sf: torch.Tensor, groups: int, rows_per_group: int, K: int, geglu_inter: int = 0) -> torch.Tensor:
+    key = (sf.data_ptr(), tuple(sf.shape), sf._version, groups, rows_per_group, K, geglu_inter)
+    t = _ATOMS.get(key)
+    if t is not None:
+        return t
+    lib = load()
+    sf = sf.contiguous()
+    n = lib.aeoq_nvfp4_weight_atoms_size(groups * rows_per_group, K)
+    t = torch.empty(max(n, 16), dtype=torch.uint8, device=sf.device)
+    check(lib.aeoq_nvfp4_sf_to_atoms(sf.data_ptr(), groups, rows_per_group, K, geglu_inter, t.data_ptr(),
+                                     stream_ptr(sf.device)))
+    if len(_ATOMS) >= _ATOMS_MAX:
+        _ATOMS.pop(next(iter(_ATOMS)))
+    _ATOMS[key] = t
     return t

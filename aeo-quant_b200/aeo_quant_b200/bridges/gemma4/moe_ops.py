@@ -121,27 +121,32 @@ def nvfp4_experts_grouped(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, 
     err = A.err_word(dev)
     tile_n = pick_tile_n(P, E)
     r = _Route(lib, top_k_index.reshape(T, k), top_k_weights.reshape(T, k), E, tile_n)
+    gu_atoms = A.weight_atoms(gu_sf, E, 2 * I, H, geglu_inter=I)
+    dw_atoms = A.weight_atoms(dw_sf, E, H, I)
+    max_tiles = (P + tile_n - 1) // tile_n + E
     hp, hs, hts = quantize_2d_to_nvfp4(hidden)                                   # (:203-206)
     a_sorted = torch.empty(P, H // 2, dtype=torch.uint8, device=dev)
-    a_sorted_sf = torch.empty(P, H // 16, dtype=torch.uint8, device=dev)
-    A.check(lib.aeoq_gather_rows(hp.data_ptr(), hs.data_ptr(), r.row_tok.data_ptr(), r.n_rows_ptr, P, H // 2,
+    a_sorted_sf = torch.empty(lib.aeoq_nvfp4_act_atoms_size(max_tiles, H, tile_n), dtype=torch.uint8, device=dev)
+    A.check(lib.aeoq_gather_rows(hp.data_ptr(), hs.data_ptr(), r.row_tok.data_ptr(), r.row_exp.data_ptr(),
+                                 r.grp_off.data_ptr(), r.tile_off.data_ptr(), tile_n, r.n_rows_ptr, P, H // 2,
                                  H // 16, a_sorted.data_ptr(), a_sorted_sf.data_ptr(), st))
     amax = torch.zeros(E, dtype=torch.int32, device=dev)
     h_sorted = torch.empty(P, I, dtype=torch.bfloat16, device=dev)
     A.check(lib.aeoq_nvfp4_gemm_grouped(a_sorted.data_ptr(), a_sorted_sf.data_ptr(), P, r.grp_off.data_ptr(),
-                                        r.tile_off.data_ptr(), tile_n, gu.data_ptr(), gu_sf.data_ptr(), E, 2 * I, H,
+                                        r.tile_off.data_ptr(), tile_n, gu.data_ptr(), gu_atoms.data_ptr(), E, 2 * I, H,
                                         1, hts.data_ptr(), A.dtype_code(hts.dtype), gu_ts.data_ptr(),
                                         A.dtype_code(gu_ts.dtype), None, None, amax.data_ptr(), h_sorted.data_ptr(),
                                         I * 2, err.data_ptr(), st))
     hq = torch.empty(P, I // 2, dtype=torch.uint8, device=dev)
-    hq_sf = torch.empty(P, I // 16, dtype=torch.uint8, device=dev)
+    hq_sf = torch.empty(lib.aeoq_nvfp4_act_atoms_size(max_tiles, I, tile_n), dtype=torch.uint8, device=dev)
     ts_e = torch.empty(E, dtype=torch.float32, device=dev)
-    A.check(lib.aeoq_requant_rows(h_sorted.data_ptr(), I, r.row_exp.data_ptr(), r.n_rows_ptr, P, amax.data_ptr(), E,
+    A.check(lib.aeoq_requant_rows(h_sorted.data_ptr(), I, r.row_exp.data_ptr(), r.grp_off.data_ptr(),
+                                  r.tile_off.data_ptr(), tile_n, r.n_rows_ptr, P, amax.data_ptr(), E,
                                   1 if one_token_semantics else 0, hq.data_ptr(), hq_sf.data_ptr(),
                                   ts_e.data_ptr(), st))
     c_sorted = torch.empty(P, H, dtype=torch.bfloat16, device=dev)
     A.check(lib.aeoq_nvfp4_gemm_grouped(hq.data_ptr(), hq_sf.data_ptr(), P, r.grp_off.data_ptr(),
-                                        r.tile_off.data_ptr(), tile_n, dw.data_ptr(), dw_sf.data_ptr(), E, H, I,
+                                        r.tile_off.data_ptr(), tile_n, dw.data_ptr(), dw_atoms.data_ptr(), E, H, I,
                                         2, None, 0, dw_ts.data_ptr(), A.dtype_code(dw_ts.dtype), ts_e.data_ptr(),
                                         r.row_w.data_ptr(), None, c_sorted.data_ptr(), H * 2, err.data_ptr(), st))
     out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)

@@ -71,10 +71,18 @@ def _gemm(a, a_sf, a_ts, w, w_sf, w_ts, ids, slots, M, N, K, a_shared, out_dtype
     use_tc = PATH == "tc" or (PATH == "auto" and M >= TC_MIN_M)
     if use_tc:
         ids_p, ids_dt = (None, 0) if ids is None else (ids.data_ptr(), A.dtype_code(ids.dtype))
+        tile_n = lib.aeoq_nvfp4_tile_n(M)
+        a_rows = M if a_shared else slots * M
+        tiles = (M + tile_n - 1) // tile_n * (1 if a_shared else slots)
+        a_atoms = torch.empty(max(lib.aeoq_nvfp4_act_atoms_size(tiles, K, tile_n), 16), dtype=torch.uint8,
+                              device=a.device)
+        A.check(lib.aeoq_nvfp4_rows_to_tile_atoms(a_sf.data_ptr(), a_rows, M, K, tile_n, a_atoms.data_ptr(),
+                                                  A.stream_ptr(a.device)))
+        w_atoms = A.weight_atoms(w_sf, w.shape[0], N, K)
         A.check(lib.aeoq_nvfp4_gemm_tc(
-            a.data_ptr(), a_sf.data_ptr(), a_ts.data_ptr(), A.dtype_code(a_ts.dtype), 0 if a_shared else M,
-            w.data_ptr(), w_sf.data_ptr(), w_ts.data_ptr(), A.dtype_code(w_ts.dtype), w.shape[0],
-            ids_p, ids_dt, slots, M, N, K, c.data_ptr(), _out_code(out_dtype),
+            a.data_ptr(), a_atoms.data_ptr(), a_ts.data_ptr(), A.dtype_code(a_ts.dtype), 0 if a_shared else M,
+            w.data_ptr(), w_atoms.data_ptr(), w_ts.data_ptr(), A.dtype_code(w_ts.dtype), w.shape[0],
+            ids_p, ids_dt, slots, M, N, K, tile_n, c.data_ptr(), _out_code(out_dtype),
             A.err_word(a.device).data_ptr(), A.stream_ptr(a.device)))
         return c
     es = c.element_size()

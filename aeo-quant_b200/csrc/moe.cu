@@ -100,29 +100,47 @@ __global__ void route_scatter_kernel(const void* ids, int ids_dt, const __nv_bfl
   }
 }
 
-// Copy packed rows + scale rows of src (indexed by token) into sorted order.
+// Byte offset of (sorted row r, K-step kb) in the token-tile scale atoms of
+// the grouped GEMM (tiles of tile_n rows per expert, see sf_atoms.cu).
+__device__ __forceinline__ int64_t tile_atom_offset(int r, int64_t kb, int64_t kbc, const int* row_exp,
+                                                    const int* grp_off, const int* tile_off, int tile_n) {
+  const int e = row_exp[r];
+  const int q = r - grp_off[e];
+  const int64_t tile = tile_off[e] + q / tile_n;
+  const int rit = q % tile_n;
+  const int natoms = (tile_n + 127) / 128;
+  const int rr = rit & 127;
+  return ((tile * kbc + kb) * natoms + (rit >> 7)) * 512 + (rr & 31) * 16 + (rr >> 5) * 4;
+}
+
+// Copy packed rows of src (indexed by token) into sorted order; their scales
+// go straight into the grouped GEMM's token-tile atoms.
 __global__ void gather_rows_kernel(const uint8_t* __restrict__ src, const uint8_t* __restrict__ src_sf,
-                                   const int* __restrict__ row_tok, const int* __restrict__ n_rows_ptr,
-                                   int64_t row_bytes, int64_t sf_bytes, uint8_t* __restrict__ dst,
-                                   uint8_t* __restrict__ dst_sf) {
+                                   const int* __restrict__ row_tok, const int* __restrict__ row_exp,
+                                   const int* __restrict__ grp_off, const int* __restrict__ tile_off, int tile_n,
+                                   const int* __restrict__ n_rows_ptr, int64_t row_bytes, int64_t sf_bytes,
+                                   uint8_t* __restrict__ dst, uint8_t* __restrict__ dst_atoms) {
   const int n_rows = *n_rows_ptr;
   const int64_t v_row = row_bytes / 16;
+  const int64_t kbc = sf_bytes / 4;
   for (int64_t r = blockIdx.x; r < n_rows; r += gridDim.x) {
     const int t = row_tok[r];
     const uint4* s = reinterpret_cast<const uint4*>(src + (int64_t)t * row_bytes);
     uint4* d = reinterpret_cast<uint4*>(dst + r * row_bytes);
     for (int64_t i = threadIdx.x; i < v_row; i += blockDim.x) d[i] = s[i];
     const uint32_t* ss = reinterpret_cast<const uint32_t*>(src_sf + (int64_t)t * sf_bytes);
-    uint32_t* ds = reinterpret_cast<uint32_t*>(dst_sf + r * sf_bytes);
-    for (int64_t i = threadIdx.x; i < sf_bytes / 4; i += blockDim.x) ds[i] = ss[i];
+    for (int64_t kb = threadIdx.x; kb < kbc; kb += blockDim.x)
+      *reinterpret_cast<uint32_t*>(dst_atoms + tile_atom_offset((int)r, kb, kbc, row_exp, grp_off, tile_off, tile_n)) =
+          ss[kb];
   }
 }
 
 // Per-expert (or one shared) tensor scale from amax keys, then one 16-value
 // block per thread. amax_key[e] holds the max |h| key of expert e's rows.
 __global__ void requant_rows_kernel(const __nv_bfloat16* __restrict__ h, int64_t I, const int* __restrict__ row_exp,
+                                    const int* __restrict__ grp_off, const int* __restrict__ tile_off, int tile_n,
                                     const int* __restrict__ n_rows_ptr, const uint32_t* __restrict__ amax_key, int E,
-                                    int shared_scale, uint8_t* __restrict__ hq, uint8_t* __restrict__ hsf,
+                                    int shared_scale, uint8_t* __restrict__ hq, uint8_t* __restrict__ hsf_atoms,
                                     float* __restrict__ ts_out) {
   const int n_rows = *n_rows_ptr;
   const int64_t bpr = I / 16;
@@ -146,8 +164,11 @@ __global__ void requant_rows_kernel(const __nv_bfloat16* __restrict__ h, int64_t
       for (int j = 0; j < 8; ++j) v[8 * q + j] = __bfloat162float(x[j]);
     }
     uint32_t w0, w1;
-    hsf[b] = (uint8_t)nvfp4_quant_block(v, ts, w0, w1);
+    const uint32_t sf = nvfp4_quant_block(v, ts, w0, w1);
     *reinterpret_cast<uint2*>(hq + 8 * b) = make_uint2(w0, w1);
+    // block b of row r is scale column c = b % bpr: byte c % 4 of K-step c / 4
+    const int64_t c = b - r * bpr;
+    hsf_atoms[tile_atom_offset((int)r, c >> 2, bpr / 4, row_exp, grp_off, tile_off, tile_n) + (c & 3)] = (uint8_t)sf;
   }
 }
 
@@ -223,27 +244,29 @@ extern "C" int aeoq_moe_route(const void* top_k_index, int idx_dtype, const void
   return check_launch("route_scatter_kernel");
 }
 
-extern "C" int aeoq_gather_rows(const uint8_t* src, const uint8_t* src_sf, const int* row_tok, const int* n_rows,
-                                int64_t max_rows, int64_t row_bytes, int64_t sf_bytes, uint8_t* dst, uint8_t* dst_sf,
-                                void* stream) {
+extern "C" int aeoq_gather_rows(const uint8_t* src, const uint8_t* src_sf, const int* row_tok, const int* row_exp,
+                                const int* grp_off, const int* tile_off, int tile_n, const int* n_rows,
+                                int64_t max_rows, int64_t row_bytes, int64_t sf_bytes, uint8_t* dst,
+                                uint8_t* dst_atoms, void* stream) {
   AEOQ_REQUIRE(row_bytes % 16 == 0 && sf_bytes % 4 == 0, AEOQ_ERR_INVALID,
                "gather_rows: row bytes must be a multiple of 16, scale bytes of 4");
   if (max_rows <= 0) return AEOQ_OK;
   const int blocks = (int)std::min<int64_t>(max_rows, 148 * 8);
-  gather_rows_kernel<<<blocks, 128, 0, (cudaStream_t)stream>>>(src, src_sf, row_tok, n_rows, row_bytes, sf_bytes, dst,
-                                                                dst_sf);
+  gather_rows_kernel<<<blocks, 128, 0, (cudaStream_t)stream>>>(src, src_sf, row_tok, row_exp, grp_off, tile_off,
+                                                                tile_n, n_rows, row_bytes, sf_bytes, dst, dst_atoms);
   return check_launch("gather_rows_kernel");
 }
 
-extern "C" int aeoq_requant_rows(const void* h, int64_t I, const int* row_exp, const int* n_rows, int64_t max_rows,
-                                 const uint32_t* amax_key, int64_t num_experts, int shared_scale, uint8_t* hq,
-                                 uint8_t* hsf, float* ts_out, void* stream) {
-  AEOQ_REQUIRE(I % 16 == 0, AEOQ_ERR_INVALID, "requant_rows: I must be a multiple of 16");
+extern "C" int aeoq_requant_rows(const void* h, int64_t I, const int* row_exp, const int* grp_off, const int* tile_off,
+                                 int tile_n, const int* n_rows, int64_t max_rows, const uint32_t* amax_key,
+                                 int64_t num_experts, int shared_scale, uint8_t* hq, uint8_t* hsf_atoms,
+                                 float* ts_out, void* stream) {
+  AEOQ_REQUIRE(I % 64 == 0, AEOQ_ERR_INVALID, "requant_rows: I must be a multiple of 64");
   const int64_t nb = std::max<int64_t>(max_rows * (I / 16), 1);
   const int blocks = (int)std::min<int64_t>((nb + 255) / 256, 148 * 8);
   requant_rows_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(reinterpret_cast<const __nv_bfloat16*>(h), I, row_exp,
-                                                                 n_rows, amax_key, (int)num_experts, shared_scale, hq,
-                                                                 hsf, ts_out);
+                                                                 grp_off, tile_off, tile_n, n_rows, amax_key,
+                                                                 (int)num_experts, shared_scale, hq, hsf_atoms, ts_out);
   return check_launch("requant_rows_kernel");
 }
 

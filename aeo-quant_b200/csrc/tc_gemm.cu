@@ -16,12 +16,17 @@
 // padding M. Per CTA: one 128 x BN output tile, K in steps of 256 values
 // (128 B rows, four MMAs of K = 64), a STAGES-deep shared-memory ring.
 //
-//   warp 0      TMA producer: A and B tiles (128-byte swizzle) per stage
+//   warp 0      producer: per stage one TMA tile of A and of B (128-byte
+//               swizzle) and one bulk copy of each operand's scale atoms
 //   warp 1      TMEM owner + MMA issuer (one thread): tcgen05.cp of the
 //               stage's scale atoms, four tcgen05.mma, tcgen05.commit
-//   warps 2-5   scale-atom builders during the main loop (row-major global
-//               scales -> the 128-row x 4 atom layout tcgen05.cp expects),
-//               then the epilogue (tcgen05.ld -> alpha, cast, store)
+//   warps 2-5   epilogue (tcgen05.ld -> alpha, GeGLU / weighting, cast, store)
+//
+// Scale factors travel pre-arranged in "atoms": 128 rows x 4 scales (one
+// K = 64 step) = 512 B, row r at byte (r % 32) * 16 + (r / 32) * 4, the
+// layout tcgen05.cp .32x128b.warpx4 broadcasts into TMEM. Weights' atoms are
+// derived once per weight tensor (aeoq_nvfp4_sf_to_atoms); activations'
+// atoms are written by the kernels that produce them, tile by tile.
 //
 // No TMA multicast anywhere: every CTA loads its own tiles.
 #include <cuda.h>
@@ -45,13 +50,14 @@ struct TcParams {
   int64_t n_out;        // weight rows per expert (N of the reference, multiple of 128)
   int64_t K;            // reduction length (multiple of 64)
   int64_t num_experts;
-  // A (weights): tensor map over (num_experts * n_out) rows; scales row-major
+  // A (weights): tensor map over (num_experts * n_out) rows; scale atoms
+  // [expert][n_out / 128][K / 64][512 B]
   const uint8_t* sfa;
-  int64_t sfa_ld;       // bytes per scale row (K / 16)
-  // B (activations): tensor map over b_rows rows; scales row-major
+  // B (activations): tensor map over b_rows rows; scale atoms
+  // [token tile][K / 64][ceil(BN / 128)][512 B]
   const uint8_t* sfb;
-  int64_t sfb_ld;
   int64_t b_rows;       // rows addressable through the tensor map
+  int64_t tiles_per_slot;   // mode 0 with per-slot activations
   // tiling of B rows into problems
   int mode;             // 0: slots (blockIdx.z = slot), 1: grouped by expert (device offsets)
   int64_t M;            // rows per slot (mode 0)
@@ -99,7 +105,7 @@ struct TcLayout {
 
 // Resolve this CTA's problem: expert, first activation row, valid rows.
 struct TileInfo {
-  int64_t expert, b_row0, c_row0;
+  int64_t expert, b_row0, c_row0, tile;
   int n_valid;
   int64_t slot;
   bool active;
@@ -115,6 +121,7 @@ __device__ __forceinline__ TileInfo resolve_tile(const TcParams& p) {
     t.expert = p.ids ? load_index(p.ids, p.ids_dt, s) : s;
     t.b_row0 = s * p.b_slot_rows + tb;
     t.c_row0 = tb;
+    t.tile = (p.b_slot_rows ? s * p.tiles_per_slot : 0) + blockIdx.y;
     t.n_valid = (int)min((int64_t)BN, p.M - tb);
     t.active = t.n_valid > 0;
   } else {
@@ -131,6 +138,7 @@ __device__ __forceinline__ TileInfo resolve_tile(const TcParams& p) {
     }
     while (lo < E - 1 && p.tile_off[lo + 1] <= y) ++lo;
     t.expert = lo;
+    t.tile = y;
     const int64_t tb = (int64_t)(y - p.tile_off[lo]) * BN;
     t.b_row0 = p.grp_off[lo] + tb;
     t.c_row0 = t.b_row0;
@@ -171,7 +179,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
 
   if (tid == 0) {
     for (int s = 0; s < kTcStages; ++s) {
-      sm100::mbar_init(&sh->full[s], 1 + 4);   // TMA arrival + 4 scale-builder warps
+      sm100::mbar_init(&sh->full[s], 1);       // producer arrival + transaction bytes
       sm100::mbar_init(&sh->empty[s], 1);      // tcgen05.commit
     }
     sm100::mbar_init(&sh->accum, 1);
@@ -188,12 +196,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const uint32_t bytes = (uint32_t)(L::kA + L::kB);
+      const int64_t m_tiles = p.n_out / 128;
+      const uint8_t* sfa_base = p.sfa + ((ti.expert * m_tiles + m_tile) * kb_total) * 512;
+      const uint8_t* sfb_base = p.sfb + (ti.tile * kb_total) * (size_t)L::kSfbAtoms * 512;
       for (int kt = 0; kt < num_kt; ++kt) {
         const int s = kt % kTcStages;
         const uint32_t ph = (kt / kTcStages) & 1;
         if (!sm100::mbar_wait(&sh->empty[s], ph ^ 1, p.err, 11)) break;
-        sm100::mbar_arrive_expect_tx(&sh->full[s], bytes);
+        const int nkb = min(4, kb_total - kt * 4);
+        const uint32_t sfa_bytes = (uint32_t)nkb * 512, sfb_bytes = (uint32_t)nkb * L::kSfbAtoms * 512;
+        sm100::mbar_arrive_expect_tx(&sh->full[s], (uint32_t)(L::kA + L::kB) + sfa_bytes + sfb_bytes);
+        bulk_g2s(stSFA(s), sfa_base + (size_t)kt * 4 * 512, sfa_bytes, &sh->full[s]);
+        bulk_g2s(stSFB(s), sfb_base + (size_t)kt * 4 * L::kSfbAtoms * 512, sfb_bytes, &sh->full[s]);
         const int32_t x = kt * kKTBytes;
         if (geglu) {
           const int64_t n0 = m_tile * 64;
@@ -234,44 +248,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
       sm100::tc_commit(&sh->accum);
     }
   } else {
-    // ------------------------------------------------ scale-atom builders
-    const int r = tid - 64;   // 0..127: one A row and one B row per thread
-    int64_t a_row;
-    if (geglu) a_row = a_row_base + (r < 64 ? m_tile * 64 + r : p.n_out / 2 + m_tile * 64 + (r - 64));
-    else a_row = a_row_base + m_tile * 128 + r;
-    const uint8_t* sfa_row = p.sfa + a_row * p.sfa_ld;
-    for (int kt = 0; kt < num_kt; ++kt) {
-      const int s = kt % kTcStages;
-      const uint32_t ph = (kt / kTcStages) & 1;
-      uint32_t va[4], vb[4 * L::kSfbAtoms];
-#pragma unroll
-      for (int kb = 0; kb < 4; ++kb) {
-        const int kbg = kt * 4 + kb;
-        va[kb] = kbg < kb_total ? *reinterpret_cast<const uint32_t*>(sfa_row + kbg * 4) : 0u;
-#pragma unroll
-        for (int a = 0; a < L::kSfbAtoms; ++a) {
-          const int br = r + 128 * a;
-          const int64_t brow = ti.b_row0 + br;
-          vb[kb * L::kSfbAtoms + a] = (kbg < kb_total && br < BN && brow < p.b_rows)
-                                          ? *reinterpret_cast<const uint32_t*>(p.sfb + brow * p.sfb_ld + kbg * 4)
-                                          : 0u;
-        }
-      }
-      if (lane == 0) sm100::mbar_wait(&sh->empty[s], ph ^ 1, p.err, 13);
-      __syncwarp();
-      const int off = (r & 31) * 16 + (r >> 5) * 4;
-#pragma unroll
-      for (int kb = 0; kb < 4; ++kb) {
-        *reinterpret_cast<uint32_t*>(stSFA(s) + kb * 512 + off) = va[kb];
-#pragma unroll
-        for (int a = 0; a < L::kSfbAtoms; ++a)
-          *reinterpret_cast<uint32_t*>(stSFB(s) + (kb * L::kSfbAtoms + a) * 512 + off) = vb[kb * L::kSfbAtoms + a];
-      }
-      sm100::fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(&sh->full[s]);
-    }
-
     // ------------------------------------------------------------ epilogue
     const bool ok = sm100::mbar_wait(&sh->accum, 0, p.err, 14);
     sm100::tc_fence_after();
@@ -414,7 +390,7 @@ int tc_gemm_dispatch(int bn, const uint8_t* a, int64_t a_rows, const uint8_t* b,
   return set_error(AEOQ_ERR_INVALID, "tc_gemm: unsupported tile N %d", bn);
 }
 
-static int pick_bn(int64_t M) {
+int pick_bn(int64_t M) {
   if (M <= 8) return 8;
   if (M <= 16) return 16;
   if (M <= 32) return 32;
@@ -427,12 +403,14 @@ static int pick_bn(int64_t M) {
 
 using namespace aeoq;
 
+extern "C" int aeoq_nvfp4_tile_n(int64_t M) { return pick_bn(M); }
+
 // Tensor-core path of aeoq_nvfp4_gemm for contiguous operands: A/B packed rows
 // of K/2 bytes, scale rows of K/16 bytes (the reference tensors' layouts).
-extern "C" int aeoq_nvfp4_gemm_tc(const uint8_t* a, const uint8_t* a_sf, const void* a_ts, int a_ts_dtype,
-                                  int64_t a_slot_rows, const uint8_t* w, const uint8_t* w_sf, const void* w_ts,
+extern "C" int aeoq_nvfp4_gemm_tc(const uint8_t* a, const uint8_t* a_sf_atoms, const void* a_ts, int a_ts_dtype,
+                                  int64_t a_slot_rows, const uint8_t* w, const uint8_t* w_sf_atoms, const void* w_ts,
                                   int w_ts_dtype, int64_t num_experts, const void* expert_ids, int ids_dtype,
-                                  int64_t slots, int64_t M, int64_t N, int64_t K, void* c, int c_dtype,
+                                  int64_t slots, int64_t M, int64_t N, int64_t K, int tile_n, void* c, int c_dtype,
                                   int* err_word, void* stream) {
   AEOQ_REQUIRE(slots >= 0 && M >= 0 && N >= 0 && K >= 0, AEOQ_ERR_INVALID, "nvfp4_gemm_tc: negative shape");
   AEOQ_REQUIRE(N % 128 == 0, AEOQ_ERR_INVALID, "nvfp4_gemm_tc: N (%lld) must be a multiple of 128", (long long)N);
@@ -440,21 +418,23 @@ extern "C" int aeoq_nvfp4_gemm_tc(const uint8_t* a, const uint8_t* a_sf, const v
                (long long)K);
   AEOQ_REQUIRE((K / 2) % 16 == 0, AEOQ_ERR_INVALID, "nvfp4_gemm_tc: K/2 must be a multiple of 16");
   AEOQ_REQUIRE(c_dtype == AEOQ_BF16 || c_dtype == AEOQ_F32, AEOQ_ERR_INVALID, "nvfp4_gemm_tc: bad output dtype");
+  AEOQ_REQUIRE(tile_n == aeoq_nvfp4_tile_n(M), AEOQ_ERR_INVALID,
+               "nvfp4_gemm_tc: activation atoms were built for tile %d, expected %d", tile_n,
+               aeoq_nvfp4_tile_n(M));
   if (slots * M * N == 0) return AEOQ_OK;
-  AEOQ_REQUIRE(a && a_sf && a_ts && w && w_sf && w_ts && c && err_word, AEOQ_ERR_INVALID,
+  AEOQ_REQUIRE(a && a_sf_atoms && a_ts && w && w_sf_atoms && w_ts && c && err_word, AEOQ_ERR_INVALID,
                "nvfp4_gemm_tc: null pointer");
-  AEOQ_REQUIRE((uintptr_t)a % 16 == 0 && (uintptr_t)w % 16 == 0 && (uintptr_t)a_sf % 4 == 0 &&
-                   (uintptr_t)w_sf % 4 == 0,
-               AEOQ_ERR_INVALID, "nvfp4_gemm_tc: operands must be 16-byte aligned, scales 4-byte aligned");
+  AEOQ_REQUIRE((uintptr_t)a % 16 == 0 && (uintptr_t)w % 16 == 0 && (uintptr_t)a_sf_atoms % 16 == 0 &&
+                   (uintptr_t)w_sf_atoms % 16 == 0,
+               AEOQ_ERR_INVALID, "nvfp4_gemm_tc: operands and scale atoms must be 16-byte aligned");
   TcParams p{};
   p.n_out = N;
   p.K = K;
   p.num_experts = num_experts;
-  p.sfa = w_sf;
-  p.sfa_ld = K / 16;
-  p.sfb = a_sf;
-  p.sfb_ld = K / 16;
+  p.sfa = w_sf_atoms;
+  p.sfb = a_sf_atoms;
   p.b_rows = a_slot_rows ? slots * M : M;
+  p.tiles_per_slot = (M + tile_n - 1) / tile_n;
   p.mode = 0;
   p.M = M;
   p.b_slot_rows = a_slot_rows ? M : 0;
@@ -469,9 +449,8 @@ extern "C" int aeoq_nvfp4_gemm_tc(const uint8_t* a, const uint8_t* a_sf, const v
   p.ldc = N * es;
   p.c_slot_stride = M * N * es;
   p.err = err_word;
-  const int bn = pick_bn(M);
-  dim3 grid((unsigned)(N / 128), (unsigned)((M + bn - 1) / bn), (unsigned)slots);
-  return tc_gemm_dispatch(bn, w, num_experts * N, a, p, grid, (cudaStream_t)stream);
+  dim3 grid((unsigned)(N / 128), (unsigned)((M + tile_n - 1) / tile_n), (unsigned)slots);
+  return tc_gemm_dispatch(tile_n, w, num_experts * N, a, p, grid, (cudaStream_t)stream);
 }
 
 // Grouped (MoE) path: B rows are sorted by expert; expert e owns rows
@@ -501,9 +480,7 @@ extern "C" int aeoq_nvfp4_gemm_grouped(const uint8_t* b, const uint8_t* b_sf, in
   p.K = K;
   p.num_experts = num_experts;
   p.sfa = w_sf;
-  p.sfa_ld = K / 16;
   p.sfb = b_sf;
-  p.sfb_ld = K / 16;
   p.b_rows = max_rows;
   p.mode = 1;
   p.grp_off = grp_off;

@@ -129,11 +129,27 @@ AEOQ_API int aeoq_nvfp4_gemm(const uint8_t* a, const uint8_t* a_sf, const void* 
  * N % 128 == 0, K % 64 == 0. `err_word` is a device int that a bounded wait
  * sets non-zero if the pipeline stalls (never expected). Same replaced
  * reference functions as aeoq_nvfp4_gemm (nvfp4_matmul.py:399-864). */
-AEOQ_API int aeoq_nvfp4_gemm_tc(const uint8_t* a, const uint8_t* a_sf, const void* a_ts, int a_ts_dtype,
-                                int64_t a_slot_rows, const uint8_t* w, const uint8_t* w_sf, const void* w_ts,
+AEOQ_API int aeoq_nvfp4_gemm_tc(const uint8_t* a, const uint8_t* a_sf_atoms, const void* a_ts, int a_ts_dtype,
+                                int64_t a_slot_rows, const uint8_t* w, const uint8_t* w_sf_atoms, const void* w_ts,
                                 int w_ts_dtype, int64_t num_experts, const void* expert_ids, int ids_dtype,
-                                int64_t slots, int64_t M, int64_t N, int64_t K, void* c, int c_dtype,
+                                int64_t slots, int64_t M, int64_t N, int64_t K, int tile_n, void* c, int c_dtype,
                                 int* err_word, void* stream);
+
+/* Token-tile width the tensor-core GEMM uses for M activation rows. */
+AEOQ_API int aeoq_nvfp4_tile_n(int64_t M);
+
+/* Scale-factor atoms (the order tcgen05.cp loads into tensor memory: 128
+ * rows x 4 scales per 512 B, row r at byte (r%32)*16 + (r/32)*4).
+ * Weights: [groups][rows_per_group/128][K/64][512 B]; with geglu_inter = I
+ * each 128-row tile holds gate rows 64t.. and up rows I+64t.. of a group.
+ * Activations: [tile][K/64][ceil(tile_n/128)][512 B], rows r of slot r/M in
+ * tiles of tile_n. Sizes in bytes from the *_size functions. */
+AEOQ_API size_t aeoq_nvfp4_weight_atoms_size(int64_t rows, int64_t K);
+AEOQ_API size_t aeoq_nvfp4_act_atoms_size(int64_t tiles, int64_t K, int tile_n);
+AEOQ_API int aeoq_nvfp4_sf_to_atoms(const uint8_t* sf, int64_t groups, int64_t rows_per_group, int64_t K,
+                                    int64_t geglu_inter, uint8_t* out, void* stream);
+AEOQ_API int aeoq_nvfp4_rows_to_tile_atoms(const uint8_t* sf, int64_t rows, int64_t M, int64_t K, int tile_n,
+                                           uint8_t* out, void* stream);
 
 /* Grouped tensor-core GEMM over expert-sorted activation rows (the MoE
  * prefill path). Expert e owns sorted rows [grp_off[e], grp_off[e+1]) and
@@ -142,9 +158,11 @@ AEOQ_API int aeoq_nvfp4_gemm_tc(const uint8_t* a, const uint8_t* a_sf, const voi
  * epi 1 (gate_up, N = 2I): C[r][0..I) = bf16(bf16(gelu(g)) * u), with the
  * per-expert max |C| accumulated into grp_amax keys (zero them first);
  * epi 2 (down): C = bf16(bf16(grp_ts[e] * f32(*w_ts) * acc) * row_w[r]).
+ * Scales as atoms: b_sf_atoms token-tile atoms, w_sf weight atoms (GeGLU
+ * layout for epi 1, plain otherwise).
  * Replaces the per-expert nvfp4_linear_prequantized / nvfp4_linear calls,
  * GeGLU and weighting of _forward_prefill (modeling_nvfp4.py:218-249). */
-AEOQ_API int aeoq_nvfp4_gemm_grouped(const uint8_t* b, const uint8_t* b_sf, int64_t max_rows, const int* grp_off,
+AEOQ_API int aeoq_nvfp4_gemm_grouped(const uint8_t* b, const uint8_t* b_sf_atoms, int64_t max_rows, const int* grp_off,
                                      const int* tile_off, int tile_n, const uint8_t* w, const uint8_t* w_sf,
                                      int64_t num_experts, int64_t N, int64_t K, int epi, const void* a_ts,
                                      int a_ts_dtype, const void* w_ts, int w_ts_dtype, const float* grp_ts,
@@ -161,18 +179,21 @@ AEOQ_API int aeoq_moe_route(const void* top_k_index, int idx_dtype, const void* 
                             int64_t k, int64_t num_experts, int tile_n, int* cnt, int* fill, int* grp_off,
                             int* tile_off, int* pair_row, int* row_tok, void* row_w, int* row_exp, void* stream);
 
-/* dst[r] = src[row_tok[r]] for r < *n_rows (packed rows and scale rows). */
-AEOQ_API int aeoq_gather_rows(const uint8_t* src, const uint8_t* src_sf, const int* row_tok, const int* n_rows,
-                              int64_t max_rows, int64_t row_bytes, int64_t sf_bytes, uint8_t* dst, uint8_t* dst_sf,
-                              void* stream);
+/* dst[r] = src[row_tok[r]] for r < *n_rows; the scale rows go to the
+ * grouped GEMM's token-tile atoms (expert of row r: row_exp[r]). */
+AEOQ_API int aeoq_gather_rows(const uint8_t* src, const uint8_t* src_sf, const int* row_tok, const int* row_exp,
+                              const int* grp_off, const int* tile_off, int tile_n, const int* n_rows,
+                              int64_t max_rows, int64_t row_bytes, int64_t sf_bytes, uint8_t* dst,
+                              uint8_t* dst_atoms, void* stream);
 
 /* NVFP4 re-quantization of the sorted GeGLU rows: one tensor scale per
  * expert from amax_key[e] (shared_scale = 0; per-expert nvfp4_linear in the
  * prefill path, nvfp4_matmul.py:386) or one for all rows (shared_scale = 1;
  * the one-token path, modeling_nvfp4.py:164-172). ts_out[e] gets the scales. */
-AEOQ_API int aeoq_requant_rows(const void* h, int64_t I, const int* row_exp, const int* n_rows, int64_t max_rows,
-                               const uint32_t* amax_key, int64_t num_experts, int shared_scale, uint8_t* hq,
-                               uint8_t* hsf, float* ts_out, void* stream);
+AEOQ_API int aeoq_requant_rows(const void* h, int64_t I, const int* row_exp, const int* grp_off, const int* tile_off,
+                               int tile_n, const int* n_rows, int64_t max_rows, const uint32_t* amax_key,
+                               int64_t num_experts, int shared_scale, uint8_t* hq, uint8_t* hsf_atoms,
+                               float* ts_out, void* stream);
 
 /* out[t] = fold over token t's expert outputs in ascending expert order:
  * mode 0 bf16 rounding after every add (index_add_, modeling_nvfp4.py:250-253);
