@@ -48,7 +48,7 @@ _SIGS["aeoq_nvfp4_gemm_grouped"] = [_P, _P, _L, _P, _P, _I, _P, _P, _L, _L, _L, 
 _SIGS["aeoq_moe_route"] = [_P, _I, _P, _L, _L, _L, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]
 _SIGS["aeoq_gather_rows"] = [_P, _P, _P, _P, _P, _P, _I, _P, _L, _L, _L, _P, _P, _P]
 _SIGS["aeoq_requant_rows"] = [_P, _L, _P, _P, _P, _I, _P, _L, _P, _L, _I, _P, _P, _P, _P]
-_SIGS["aeoq_nvfp4_tile_n"] = [_L]
+_SIGS["aeoq_nvfp4_tile_n"] = [_L, _L, _L]
 _SIGS["aeoq_nvfp4_weight_atoms_size"] = [_L, _L]
 _SIGS["aeoq_nvfp4_act_atoms_size"] = [_L, _L, _I]
 _SIGS["aeoq_nvfp4_sf_to_atoms"] = [_P, _L, _L, _L, _L, _P, _P]
@@ -144,16 +144,23 @@ def err_word(device: torch.device) -> torch.Tensor:
 
 # Weight scale atoms are derived once per weight tensor and cached here,
 # keyed on the tensor's storage, shape and version counter (an in-place
-# update of the scales invalidates the entry).
+# update of the scales invalidates the entry). Each entry also holds a weak
+# reference to the tensor it was built from: memory freed and reused by a
+# new tensor at the same address finds a dead reference and rebuilds.
 _ATOMS: dict = {}
 _ATOMS_MAX = 256
 
 
 def weight_atoms(sf: torch.Tensor, groups: int, rows_per_group: int, K: int, geglu_inter: int = 0) -> torch.Tensor:
-    key = (sf.data_ptr(), tuple(sf.shape), sf._version, groups, rows_per_group, K, geglu_inter)
-    t = _ATOMS.get(key)
-    if t is not None:
-        return t
+    import weakref
+    key = (sf.data_ptr(), tuple(sf.shape), tuple(sf.stride()), sf._version, groups, rows_per_group, K, geglu_inter)
+    hit = _ATOMS.get(key)
+    if hit is not None:
+        ref, t = hit
+        if ref() is sf:
+            return t
+        del _ATOMS[key]
+    src = sf
     lib = load()
     sf = sf.contiguous()
     n = lib.aeoq_nvfp4_weight_atoms_size(groups * rows_per_group, K)
@@ -162,5 +169,5 @@ def weight_atoms(sf: torch.Tensor, groups: int, rows_per_group: int, K: int, geg
                                      stream_ptr(sf.device)))
     if len(_ATOMS) >= _ATOMS_MAX:
         _ATOMS.pop(next(iter(_ATOMS)))
-    _ATOMS[key] = t
+    _ATOMS[key] = (weakref.ref(src), t)
     return t

@@ -56,6 +56,7 @@ def _out_code(out_dtype: torch.dtype) -> int:
 # gather GEMV serves), "tc" / "simt" force one (used by the tests).
 PATH = "auto"
 TC_MIN_M = 8
+FORCE_TILE_N = 0   # tests: force the token-tile width of the tensor-core GEMM
 
 
 def _gemm(a, a_sf, a_ts, w, w_sf, w_ts, ids, slots, M, N, K, a_shared, out_dtype):
@@ -71,7 +72,7 @@ def _gemm(a, a_sf, a_ts, w, w_sf, w_ts, ids, slots, M, N, K, a_shared, out_dtype
     use_tc = PATH == "tc" or (PATH == "auto" and M >= TC_MIN_M)
     if use_tc:
         ids_p, ids_dt = (None, 0) if ids is None else (ids.data_ptr(), A.dtype_code(ids.dtype))
-        tile_n = lib.aeoq_nvfp4_tile_n(M)
+        tile_n = FORCE_TILE_N or lib.aeoq_nvfp4_tile_n(M, N, slots)
         a_rows = M if a_shared else slots * M
         tiles = (M + tile_n - 1) // tile_n * (1 if a_shared else slots)
         a_atoms = torch.empty(max(lib.aeoq_nvfp4_act_atoms_size(tiles, K, tile_n), 16), dtype=torch.uint8,

@@ -31,6 +31,7 @@
 // No TMA multicast anywhere: every CTA loads its own tiles.
 #include <cuda.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -76,11 +77,28 @@ struct TcParams {
   int64_t c_slot_stride;                  // bytes between slots (mode 0)
   uint32_t* grp_amax;                     // kEpiGeglu: per-expert |h| max key (atomicMax)
   int* err;                               // device error word (bounded waits)
+  uint64_t* trace;                        // development builds only: per-CTA phase stamps
+  int dbg;                                // development builds only: experiment switches
 };
 
+#ifdef AEOQ_TC_TRACE
+#define TC_TRACE(i)                                                                                      \
+  do {                                                                                                   \
+    if (p.trace) {                                                                                       \
+      uint64_t t_;                                                                                       \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                             \
+      const uint64_t cta_ = blockIdx.x + (uint64_t)gridDim.x * (blockIdx.y + (uint64_t)gridDim.y * blockIdx.z); \
+      if (cta_ < 8192) p.trace[cta_ * 8 + (i)] = t_;                                                     \
+    }                                                                                                    \
+  } while (0)
+#else
+#define TC_TRACE(i) do {} while (0)
+#endif
+
+constexpr int kTcMaxStages = 8;
 struct TcSmem {
-  uint64_t full[kTcStages];
-  uint64_t empty[kTcStages];
+  uint64_t full[kTcMaxStages];
+  uint64_t empty[kTcMaxStages];
   uint64_t accum;
   uint32_t tmem_base;
 };
@@ -93,11 +111,16 @@ struct TcLayout {
   static constexpr size_t kSfa = 4 * 512;
   static constexpr size_t kSfb = (size_t)4 * 512 * kSfbAtoms;
   static constexpr size_t kStage = kA + kB + kSfa + kSfb;
-  // GeGLU exchange of the up half (64 x BN f32) reuses the stage ring, which
-  // is idle once the accumulator is complete.
+  // as many stages as the shared-memory budget holds (at most 8)
+  static constexpr int kStages =
+      (int)((220 * 1024 - 1280) / kStage) < kTcMaxStages ? (int)((220 * 1024 - 1280) / kStage) : kTcMaxStages;
+  // The epilogue reuses the stage ring, idle once the accumulator is
+  // complete: the GeGLU exchange of the up half (64 x BN f32) and the
+  // output tile staged for coalesced row stores (BN x 128 x 4 B at most).
   static constexpr size_t kXchg = 64 * (size_t)BN * 4;
-  static_assert(kXchg <= kTcStages * kStage, "exchange buffer must fit in the stage ring");
-  static constexpr size_t kBytes = 1024 + kTcStages * kStage + 256;
+  static constexpr size_t kOut = (size_t)BN * 128 * 4;
+  static_assert(kXchg + kOut <= kStages * kStage, "epilogue buffers must fit in the stage ring");
+  static constexpr size_t kBytes = 1024 + kStages * kStage + 256;
   static constexpr uint32_t kTmemCols = (BN + 32 * kSfbAtoms + 16 <= 256) ? 256 : 512;
   static constexpr uint32_t kSfaCol = BN;                  // 16 columns
   static constexpr uint32_t kSfbCol = BN + 16;             // 16 * kSfbAtoms columns
@@ -150,6 +173,23 @@ __device__ __forceinline__ TileInfo resolve_tile(const TcParams& p) {
   return t;
 }
 
+// min(BN, 32) accumulator columns of this thread's TMEM lane, one wait.
+template <int BN>
+__device__ __forceinline__ void tmem_cols(uint32_t taddr, float (&v)[32]) {
+  if constexpr (BN >= 32) {
+    uint32_t r[32];
+    sm100::tmem_ld32_nowait(taddr, r);
+    sm100::tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  } else {
+    float w[16];
+    sm100::tmem_ld16(taddr, w);   // reads 16 columns; only BN of them are used
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = w[i];
+  }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                                                                       const __grid_constant__ CUtensorMap tmB,
@@ -159,9 +199,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~uintptr_t(1023));
   uint8_t* stage0 = base;
   float* xchg = reinterpret_cast<float*>(base);   // epilogue only (stage ring idle by then)
-  TcSmem* sh = reinterpret_cast<TcSmem*>(base + kTcStages * L::kStage);
+  TcSmem* sh = reinterpret_cast<TcSmem*>(base + L::kStages * L::kStage);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
+  if (tid == 0) TC_TRACE(0);
   const TileInfo ti = resolve_tile<BN>(p);
   if (!ti.active) return;   // whole CTA exits together before any sync
   const int64_t m_tile = blockIdx.x;
@@ -178,7 +219,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
   auto stSFB = [&](int s) { return stage0 + s * L::kStage + L::kA + L::kB + L::kSfa; };
 
   if (tid == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < L::kStages; ++s) {
       sm100::mbar_init(&sh->full[s], 1);       // producer arrival + transaction bytes
       sm100::mbar_init(&sh->empty[s], 1);      // tcgen05.commit
     }
@@ -192,23 +233,35 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
+  if (tid == 0) TC_TRACE(1);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    {
+      const bool leader = sm100::elect_one();
+#ifdef AEOQ_TC_TRACE
+      uint64_t pwait_ = 0;
+#endif
       const int64_t m_tiles = p.n_out / 128;
       const uint8_t* sfa_base = p.sfa + ((ti.expert * m_tiles + m_tile) * kb_total) * 512;
       const uint8_t* sfb_base = p.sfb + (ti.tile * kb_total) * (size_t)L::kSfbAtoms * 512;
       for (int kt = 0; kt < num_kt; ++kt) {
-        const int s = kt % kTcStages;
-        const uint32_t ph = (kt / kTcStages) & 1;
+        const int s = kt % L::kStages;
+        const uint32_t ph = (kt / L::kStages) & 1;
+#ifdef AEOQ_TC_TRACE
+        uint64_t w0_; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(w0_));
+#endif
         if (!sm100::mbar_wait(&sh->empty[s], ph ^ 1, p.err, 11)) break;
+#ifdef AEOQ_TC_TRACE
+        { uint64_t w1_; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(w1_)); pwait_ += w1_ - w0_; }
+#endif
         const int nkb = min(4, kb_total - kt * 4);
         const uint32_t sfa_bytes = (uint32_t)nkb * 512, sfb_bytes = (uint32_t)nkb * L::kSfbAtoms * 512;
+        const int32_t x = kt * kKTBytes;
+        if (!leader) continue;
         sm100::mbar_arrive_expect_tx(&sh->full[s], (uint32_t)(L::kA + L::kB) + sfa_bytes + sfb_bytes);
         bulk_g2s(stSFA(s), sfa_base + (size_t)kt * 4 * 512, sfa_bytes, &sh->full[s]);
         bulk_g2s(stSFB(s), sfb_base + (size_t)kt * 4 * L::kSfbAtoms * 512, sfb_bytes, &sh->full[s]);
-        const int32_t x = kt * kKTBytes;
         if (geglu) {
           const int64_t n0 = m_tile * 64;
           sm100::tma_load_2d(stA(s), &tmA, x, (int32_t)(a_row_base + n0), &sh->full[s]);
@@ -219,17 +272,35 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
         }
         sm100::tma_load_2d(stB(s), &tmB, x, (int32_t)ti.b_row0, &sh->full[s]);
       }
+#ifdef AEOQ_TC_TRACE
+      (void)pwait_;
+#endif
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    {
+      const bool leader = sm100::elect_one();
+#ifdef AEOQ_TC_TRACE
+      uint64_t mwait_ = 0, mcp_ = 0, mmma_ = 0;
+#endif
       const uint32_t idesc = sm100::idesc_nvf4(BN);
       for (int kt = 0; kt < num_kt; ++kt) {
-        const int s = kt % kTcStages;
-        const uint32_t ph = (kt / kTcStages) & 1;
+        const int s = kt % L::kStages;
+        const uint32_t ph = (kt / L::kStages) & 1;
+#ifdef AEOQ_TC_TRACE
+        const long long w0_ = clock64();
+#endif
         if (!sm100::mbar_wait(&sh->full[s], ph, p.err, 12)) break;
+#ifdef AEOQ_TC_TRACE
+        const long long w1_ = clock64();
+        mwait_ += w1_ - w0_;
+#endif
         sm100::tc_fence_after();
         const int nkb = min(4, kb_total - kt * 4);
+#ifdef AEOQ_TC_TRACE
+        if (!((p.dbg & 1) && kt > 0))
+#endif
+        if (leader)
         for (int kb = 0; kb < nkb; ++kb) {
           sm100::tc_cp_32x128b_warpx4(tmem + L::kSfaCol + 4 * kb, sm100::sdesc_sf_atom(sm100::smem_u32(stSFA(s) + kb * 512)));
 #pragma unroll
@@ -237,75 +308,123 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
             sm100::tc_cp_32x128b_warpx4(tmem + L::kSfbCol + 4 * (kb * L::kSfbAtoms + a),
                                         sm100::sdesc_sf_atom(sm100::smem_u32(stSFB(s) + (kb * L::kSfbAtoms + a) * 512)));
         }
+#ifdef AEOQ_TC_TRACE
+        const long long w2_ = clock64();
+        mcp_ += w2_ - w1_;
+        if (!(p.dbg & 2))
+#endif
+        if (leader)
         for (int kb = 0; kb < nkb; ++kb) {
           const uint64_t ad = sm100::sdesc_k_sw128(sm100::smem_u32(stA(s)) + kb * 32);
           const uint64_t bd = sm100::sdesc_k_sw128(sm100::smem_u32(stB(s)) + kb * 32);
           sm100::tc_mma_nvf4(tmem, ad, bd, idesc, tmem + L::kSfaCol + 4 * kb,
                              tmem + L::kSfbCol + 4 * kb * L::kSfbAtoms, (kt | kb) ? 1u : 0u);
         }
-        sm100::tc_commit(&sh->empty[s]);
+#ifdef AEOQ_TC_TRACE
+        mmma_ += clock64() - w2_;
+#endif
+        if (leader) sm100::tc_commit(&sh->empty[s]);
+        __syncwarp();
       }
-      sm100::tc_commit(&sh->accum);
+      if (leader) sm100::tc_commit(&sh->accum);
+      TC_TRACE(5);
+#ifdef AEOQ_TC_TRACE
+      if (p.trace) { const uint64_t c_ = blockIdx.x + (uint64_t)gridDim.x * (blockIdx.y + (uint64_t)gridDim.y * blockIdx.z); if (c_ < 8192) { p.trace[c_ * 8 + 4] = mwait_; p.trace[c_ * 8 + 2] = mcp_; p.trace[c_ * 8 + 3] = mmma_; } }
+#endif
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const bool ok = sm100::mbar_wait(&sh->accum, 0, p.err, 14);
-    sm100::tc_fence_after();
     const int q = warp & 3;            // TMEM lane quadrant this warp may access
     const int row = 32 * q + lane;     // accumulator row = weight row in the tile
-    float alpha;
+    float alpha;                       // read while the main loop runs
     if (p.epi == kEpiScaleRow) alpha = p.grp_alpha_ts[ti.expert] * load_scalar_f(p.w_ts, p.w_ts_dt);
     else alpha = load_scalar_f(p.a_ts, p.a_ts_dt) * load_scalar_f(p.w_ts, p.w_ts_dt);
+    const bool ok = sm100::mbar_wait(&sh->accum, 0, p.err, 14);
+    if (tid == 64) TC_TRACE(6);
+    sm100::tc_fence_after();
     char* cbase = reinterpret_cast<char*>(p.c) + ti.slot * p.c_slot_stride;
     uint32_t hkey = 0;
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-      float v[16];
-      sm100::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
-      if (!ok) continue;
-      if (p.epi == kEpiStore) {
-        const int64_t n = m_tile * 128 + row;
+    // Output tile staged in shared memory as [token][column] so the global
+    // stores are whole 16-byte pieces of output rows.
+    uint8_t* outs = base + L::kXchg;
+    const int ncol = geglu ? 64 : 128;
+    const int es = (p.epi == kEpiStore && p.c_dt == AEOQ_F32) ? 4 : 2;
+    constexpr int kChunk = BN < 32 ? BN : 32;   // columns per tcgen05.ld batch
+#ifdef AEOQ_TC_TRACE
+    long long e_ld = 0, e_st = 0, e0_ = clock64();
+#endif
+    if (p.epi != kEpiGeglu) {
+      for (int c0 = 0; c0 < BN; c0 += kChunk) {
+        float v[32];
+#ifdef AEOQ_TC_TRACE
+        const long long a_ = clock64();
+#endif
+        tmem_cols<BN>(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+#ifdef AEOQ_TC_TRACE
+        e_ld += clock64() - a_;
+#endif
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (c0 + j < ti.n_valid) {
-            char* dst = cbase + (ti.c_row0 + c0 + j) * p.ldc;
-            if (p.c_dt == AEOQ_BF16) reinterpret_cast<__nv_bfloat16*>(dst)[n] = __float2bfloat16_rn(v[j] * alpha);
-            else reinterpret_cast<float*>(dst)[n] = v[j] * alpha;
+        for (int j = 0; j < kChunk; ++j) {
+          const int t = c0 + j;
+          if (t < BN) {
+            float y = v[j] * alpha;
+            if (p.epi == kEpiScaleRow)
+              y = (t < ti.n_valid) ? bf16r(y) * __bfloat162float(p.row_w[ti.c_row0 + t]) : 0.f;
+            if (es == 4) reinterpret_cast<float*>(outs)[t * ncol + row] = y;
+            else reinterpret_cast<__nv_bfloat16*>(outs)[t * ncol + row] = __float2bfloat16_rn(y);
           }
         }
-      } else if (p.epi == kEpiScaleRow) {
-        const int64_t n = m_tile * 128 + row;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (c0 + j < ti.n_valid) {
-            const int64_t crow = ti.c_row0 + c0 + j;
-            const float w = __bfloat162float(p.row_w[crow]);
-            reinterpret_cast<__nv_bfloat16*>(cbase + crow * p.ldc)[n] = __float2bfloat16_rn(bf16r(v[j] * alpha) * w);
-          }
-        }
-      } else {
-        // GeGLU: rows 64..127 (up) hand bf16(alpha*acc) to rows 0..63 (gate)
+      }
+    } else {
+      // GeGLU: rows 64..127 (up) hand bf16(alpha*acc) to rows 0..63 (gate)
+      for (int c0 = 0; c0 < BN; c0 += kChunk) {
+        float v[32];
+        tmem_cols<BN>(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
         if (row >= 64) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
+          for (int j = 0; j < kChunk; ++j)
             if (c0 + j < BN) xchg[(row - 64) * BN + c0 + j] = bf16r(v[j] * alpha);
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (row < 64) {
-          const int64_t n = m_tile * 64 + row;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (q < 2) {
+        for (int c0 = 0; c0 < BN; c0 += kChunk) {
+          float v[32];
+          tmem_cols<BN>(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            if (c0 + j < ti.n_valid && c0 + j < BN) {
+          for (int j = 0; j < kChunk; ++j) {
+            const int t = c0 + j;
+            if (t < BN) {
               const float g = bf16r(v[j] * alpha);
-              const float u = xchg[row * BN + c0 + j];
+              const float u = xchg[row * BN + t];
               const __nv_bfloat16 hv = __float2bfloat16_rn(bf16r(gelu_tanh(g)) * u);
-              reinterpret_cast<__nv_bfloat16*>(cbase + (ti.c_row0 + c0 + j) * p.ldc)[n] = hv;
-              hkey = max(hkey, In<AEOQ_BF16>::abs_key(hv));
+              reinterpret_cast<__nv_bfloat16*>(outs)[t * ncol + row] = hv;
+              if (t < ti.n_valid) hkey = max(hkey, In<AEOQ_BF16>::abs_key(hv));
             }
           }
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
       }
     }
+#ifdef AEOQ_TC_TRACE
+    const long long e1_ = clock64();
+#endif
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (ok) {
+      const int chunks = ncol * es / 16;             // 16-byte pieces per output row
+      const int64_t col0 = (int64_t)m_tile * ncol * es;
+      for (int idx = tid - 64; idx < ti.n_valid * chunks; idx += 128) {
+        const int t = idx / chunks, c = idx - t * chunks;
+        *reinterpret_cast<uint4*>(cbase + (ti.c_row0 + t) * p.ldc + col0 + 16 * c) =
+            *reinterpret_cast<const uint4*>(outs + (size_t)t * ncol * es + 16 * c);
+      }
+    }
+#ifdef AEOQ_TC_TRACE
+    e_st = clock64() - e1_;
+    if (tid == 64 && p.trace) {
+      const uint64_t c_ = blockIdx.x + (uint64_t)gridDim.x * (blockIdx.y + (uint64_t)gridDim.y * blockIdx.z);
+      if (c_ < 8192) { p.trace[c_ * 8 + 5] = e_ld; p.trace[c_ * 8 + 6] = e1_ - e0_; p.trace[c_ * 8 + 1] = e_st; }
+    }
+#endif
     if (p.epi == kEpiGeglu && p.grp_amax) {
       hkey = warp_umax(hkey);
       if (lane == 0 && hkey) atomicMax(p.grp_amax + ti.expert, hkey);
@@ -313,6 +432,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
   }
   sm100::tc_fence_before();
   __syncthreads();
+  if (tid == 0) TC_TRACE(7);
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, L::kTmemCols);
@@ -373,7 +493,14 @@ static int launch_tc(const uint8_t* a, int64_t a_rows, const uint8_t* b, const T
     }
     set_bytes[slot] = L::kBytes;
   }
+#ifdef AEOQ_TC_TRACE
+  TcParams pt = p;
+  if (const char* tp = getenv("AEOQ_TC_TRACE_PTR")) pt.trace = reinterpret_cast<uint64_t*>(strtoull(tp, nullptr, 10));
+  if (const char* dp = getenv("AEOQ_TC_DBG")) pt.dbg = atoi(dp);
+  nvfp4_tc_gemm_kernel<BN><<<grid, kTcThreads, L::kBytes, st>>>(ta, tb, pt);
+#else
   nvfp4_tc_gemm_kernel<BN><<<grid, kTcThreads, L::kBytes, st>>>(ta, tb, p);
+#endif
   return check_launch("nvfp4_tc_gemm_kernel");
 }
 
@@ -403,7 +530,15 @@ int pick_bn(int64_t M) {
 
 using namespace aeoq;
 
-extern "C" int aeoq_nvfp4_tile_n(int64_t M) { return pick_bn(M); }
+// Token-tile width: the smallest tile covering M, halved while the grid
+// would leave SMs idle (each halving adds CTAs that re-read the weight tile
+// from L2, which is cheaper than idle HBM bandwidth).
+extern "C" int aeoq_nvfp4_tile_n(int64_t M, int64_t N, int64_t slots) {
+  int bn = pick_bn(M);
+  const int64_t base = (N / 128) * (slots > 0 ? slots : 1);
+  while (bn > 8 && base * ((M + bn - 1) / bn) < 148) bn >>= 1;
+  return bn;
+}
 
 // Tensor-core path of aeoq_nvfp4_gemm for contiguous operands: A/B packed rows
 // of K/2 bytes, scale rows of K/16 bytes (the reference tensors' layouts).
@@ -418,9 +553,8 @@ extern "C" int aeoq_nvfp4_gemm_tc(const uint8_t* a, const uint8_t* a_sf_atoms, c
                (long long)K);
   AEOQ_REQUIRE((K / 2) % 16 == 0, AEOQ_ERR_INVALID, "nvfp4_gemm_tc: K/2 must be a multiple of 16");
   AEOQ_REQUIRE(c_dtype == AEOQ_BF16 || c_dtype == AEOQ_F32, AEOQ_ERR_INVALID, "nvfp4_gemm_tc: bad output dtype");
-  AEOQ_REQUIRE(tile_n == aeoq_nvfp4_tile_n(M), AEOQ_ERR_INVALID,
-               "nvfp4_gemm_tc: activation atoms were built for tile %d, expected %d", tile_n,
-               aeoq_nvfp4_tile_n(M));
+  AEOQ_REQUIRE(tile_n == 8 || tile_n == 16 || tile_n == 32 || tile_n == 64 || tile_n == 128 || tile_n == 256,
+               AEOQ_ERR_INVALID, "nvfp4_gemm_tc: tile_n %d must be a power of two in [8, 256]", tile_n);
   if (slots * M * N == 0) return AEOQ_OK;
   AEOQ_REQUIRE(a && a_sf_atoms && a_ts && w && w_sf_atoms && w_ts && c && err_word, AEOQ_ERR_INVALID,
                "nvfp4_gemm_tc: null pointer");

@@ -135,8 +135,9 @@ AEOQ_API int aeoq_nvfp4_gemm_tc(const uint8_t* a, const uint8_t* a_sf_atoms, con
                                 int64_t slots, int64_t M, int64_t N, int64_t K, int tile_n, void* c, int c_dtype,
                                 int* err_word, void* stream);
 
-/* Token-tile width the tensor-core GEMM uses for M activation rows. */
-AEOQ_API int aeoq_nvfp4_tile_n(int64_t M);
+/* Token-tile width for M activation rows against N weight rows in `slots`
+ * problems (the activation atoms must be built for the same width). */
+AEOQ_API int aeoq_nvfp4_tile_n(int64_t M, int64_t N, int64_t slots);
 
 /* Scale-factor atoms (the order tcgen05.cp loads into tensor memory: 128
  * rows x 4 scales per 512 B, row r at byte (r%32)*16 + (r/32)*4).

@@ -66,3 +66,16 @@ def test_tc_matches_simt_bitwise_mostly(NM):
     NM.PATH = "tc"
     same = (y_tc == y_simt).float().mean().item()
     assert same > 0.97, same
+
+
+def test_weight_atom_cache_follows_the_tensor(NM):
+    """A weight allocated where a freed one lived must not reuse its atoms."""
+    from aeo_quant_b200.gpu import quant as Q
+    x = randn_bf16((16, 512), 1.0, 5000)
+    ap, asf, ats = _q(x)
+    for seed in (5001, 5002, 5003):
+        wp, wsf, wts = _q(randn_bf16((256, 512), 0.02 * (seed - 5000), seed))
+        y = NM.nvfp4_linear_prequantized(ap, asf, ats, wp, wsf, wts.float())
+        ref = OG.nvfp4_gemm(u8(ap), u8(asf), float(ats), u8(wp), u8(wsf), float(wts))
+        assert max_rel_err(bf16_to_np(y), ref) == 0.0
+        del wp, wsf, wts, y
