@@ -48,6 +48,10 @@ _SIGS["aeoq_nvfp4_gemm_grouped"] = [_P, _P, _L, _P, _P, _I, _P, _P, _L, _L, _L, 
 _SIGS["aeoq_moe_route"] = [_P, _I, _P, _L, _L, _L, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]
 _SIGS["aeoq_gather_rows"] = [_P, _P, _P, _P, _P, _P, _I, _P, _L, _L, _L, _P, _P, _P]
 _SIGS["aeoq_requant_rows"] = [_P, _L, _P, _P, _P, _I, _P, _L, _P, _L, _I, _P, _P, _P, _P]
+_SIGS["aeoq_selftest_div_rn"] = [_I, _P, _P, _P]
+_SIGS["aeoq_moe_nvfp4_decode_tc_supported"] = [_L, _L, _L]
+_SIGS["aeoq_moe_nvfp4_decode_tc_workspace_size"] = [_L, _L, _L]
+_SIGS["aeoq_moe_nvfp4_decode_tc"] = [_P, _P, _I, _P, _L, _P, _P, _P, _I, _P, _P, _P, _I, _L, _L, _L, _P, _P, _Z, _P, _P]
 _SIGS["aeoq_nvfp4_tile_n"] = [_L, _L, _L]
 _SIGS["aeoq_nvfp4_weight_atoms_size"] = [_L, _L]
 _SIGS["aeoq_nvfp4_act_atoms_size"] = [_L, _L, _I]
@@ -57,7 +61,8 @@ _SIGS["aeoq_moe_combine"] = [_P, _P, _P, _I, _L, _L, _L, _I, _P, _P]
 _SIGS["aeoq_nvfp4_gemm_tc"] = [_P, _P, _P, _I, _L, _P, _P, _P, _I, _L, _P, _I, _L, _L, _L, _L, _I, _P, _I, _P, _P]
 _SIGS["aeoq_moe_nvfp4_decode_fused_noalloc"] = [_P, _P, _I, _P, _L, _P, _P, _P, _I, _P, _P, _P, _I, _L, _L, _L,
                                                 _P, _P]
-_RESTYPE = {"aeoq_nvfp4_weight_atoms_size": C.c_size_t, "aeoq_nvfp4_act_atoms_size": C.c_size_t,
+_RESTYPE = {"aeoq_moe_nvfp4_decode_tc_workspace_size": C.c_size_t,
+            "aeoq_nvfp4_weight_atoms_size": C.c_size_t, "aeoq_nvfp4_act_atoms_size": C.c_size_t,
             "aeoq_last_error": C.c_char_p, "aeoq_nvfp4_quantize_workspace_size": C.c_size_t,
             "aeoq_moe_nvfp4_decode_workspace_size": C.c_size_t,
             "aeoq_moe_nvfp4_decode_fused_workspace_size": C.c_size_t,

@@ -28,9 +28,16 @@ def _fused_workspace(lib, device, k, H, I):
     return ws
 
 
-def nvfp4_decode(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf, dw_ts, fused=None):
-    """One-token forward (modeling_nvfp4.py:132-186): one cooperative kernel
-    when the shape fits its shared-memory plan, else three chained launches."""
+_TC_WS: dict = {}
+
+# One-token kernel choice: "tc" (tensor cores, two launches), "fused" (one
+# cooperative CUDA-core kernel), "chained" (three CUDA-core launches); "auto"
+# takes the first that supports the shape.
+DECODE_PATH = "auto"
+
+
+def nvfp4_decode(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf, dw_ts, fused=None, path=None):
+    """One-token forward (modeling_nvfp4.py:132-186)."""
     A.require_cuda(hidden, top_k_index, top_k_weights, gu, dw)
     lib = A.load()
     if hidden.dtype != torch.bfloat16:
@@ -44,7 +51,27 @@ def nvfp4_decode(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf
     idx = top_k_index.reshape(-1)[:k].contiguous()
     w = top_k_weights.reshape(-1)[:k].to(torch.bfloat16).contiguous()
     out = torch.empty(1, H, dtype=torch.bfloat16, device=hidden.device)
-    if fused is None:
+    path = path or ("fused" if fused else "chained" if fused is False else DECODE_PATH)
+    if path in ("auto", "tc") and lib.aeoq_moe_nvfp4_decode_tc_supported(k, H, I):
+        key = (hidden.device.index, k, H, I)
+        ws = _TC_WS.get(key)
+        if ws is None:
+            ws = torch.zeros(lib.aeoq_moe_nvfp4_decode_tc_workspace_size(k, H, I), dtype=torch.uint8,
+                             device=hidden.device)
+            _TC_WS[key] = ws
+        gu_atoms = A.weight_atoms(gu_sf, E, 2 * I, H, geglu_inter=I)
+        dw_atoms = A.weight_atoms(dw_sf, E, H, I)
+        A.check(lib.aeoq_moe_nvfp4_decode_tc(
+            hidden.data_ptr(), idx.data_ptr(), A.dtype_code(idx.dtype), w.data_ptr(), k,
+            gu.data_ptr(), gu_atoms.data_ptr(), gu_ts.data_ptr(), A.dtype_code(gu_ts.dtype),
+            dw.data_ptr(), dw_atoms.data_ptr(), dw_ts.data_ptr(), A.dtype_code(dw_ts.dtype),
+            E, H, I, out.data_ptr(), ws.data_ptr(), ws.numel(), A.err_word(hidden.device).data_ptr(),
+            A.stream_ptr(hidden.device)))
+        return out
+    if path == "tc":
+        raise ValueError(f"tensor-core decode does not support top_k={k}, hidden={H}, inter={I}")
+    fused = path in ("auto", "fused")
+    if fused:
         fused = bool(lib.aeoq_moe_nvfp4_decode_fused_supported(k, H, I))
     if fused:
         ws = _fused_workspace(lib, hidden.device, k, H, I)

@@ -6,7 +6,8 @@
 //   * e4m3fn block scale per 16 elements along K.
 //   * per-tensor scale in the input dtype (bf16 for activations).
 // All arithmetic that decides a quantized bit is IEEE round-to-nearest: the
-// library is built without fast-math, and divisions use __fdiv_rn explicitly.
+// library is built without fast-math, and divisions are correctly rounded
+// (div_rn below).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -129,70 +130,144 @@ __device__ __forceinline__ float fp4_value(uint32_t nib) {
   return (nib & 8u) ? -v : v;
 }
 
+// ---------------------------------------------------------------------------
+// Correctly rounded float division (IEEE round-to-nearest-even), the rounding
+// every quantized bit of the reference depends on.
+//
+// div_rn_core: one Newton-Raphson step on an approximate reciprocal
+// (q = a*y, r = a - q*b, q += r*y; Markstein, IBM J. Res. Dev. 34(1), 1990)
+// leaves q within about half an ulp of a/b, so the rounded quotient is q or
+// its neighbour toward a/b. Both remainders a - q*b are exact in one fma
+// (each candidate is within an ulp of a/b and nothing underflows in the
+// operand range below), and |a - q*b| = |b| * |a/b - q| orders the candidates
+// by distance: the smaller remainder wins, equal remainders are a tie and go
+// to the even significand. Valid for a == 0 or 2^-80 <= |a| <= 2^80, and
+// 2^-40 <= |b| <= 2^40; div_rn checks that and otherwise calls the
+// compiler's __fdiv_rn (out of line, so the common path carries no trace of
+// it). Tested bit for bit against __fdiv_rn over every significand pair of
+// the quantizers' operand domains.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float div_rn_core(float a, float b) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(b));
+  float q = a * y;
+  float r = fmaf(-q, b, a);
+  q = (r != 0.0f) ? fmaf(r, y, q) : q;   // keeps the sign of a zero quotient
+  r = fmaf(-q, b, a);
+  const uint32_t qb = __float_as_uint(q);
+  const bool up = (r > 0.0f) == (b > 0.0f);              // a/b lies above q
+  const uint32_t nb = (up == (q > 0.0f)) ? qb + 1u : qb - 1u;
+  const float q2 = __uint_as_float(nb);
+  const float d1 = fabsf(r), d2 = fabsf(fmaf(-q2, b, a));
+  const bool take = (r != 0.0f) && (d2 < d1 || (d2 == d1 && (nb & 1u) == 0u));
+  return take ? q2 : q;
+}
+
+static __device__ __noinline__ float div_rn_slow(float a, float b) { return __fdiv_rn(a, b); }
+
+__device__ __forceinline__ float div_rn(float a, float b) {
+  const float aa = fabsf(a), ab = fabsf(b);
+  const bool in_range = (aa == 0.0f || (aa >= 0x1p-80f && aa <= 0x1p80f)) && ab >= 0x1p-40f && ab <= 0x1p40f;
+  if (__builtin_expect(in_range, 1)) return div_rn_core(a, b);
+  return div_rn_slow(a, b);
+}
+
 // Tensor scale from the (abs) amax, in the input dtype: quant.py:167-168.
 template <int DT>
 __device__ __forceinline__ float nvfp4_tensor_scale(float amax) {
-  float t = In<DT>::round(__fdiv_rn(amax, kNvfp4Denom));
+  float t = In<DT>::round(div_rn(amax, kNvfp4Denom));
   float floor_v = In<DT>::round(1e-12f);
   return nan_max(t, floor_v);
+}
+
+// Elements of a block whose operands leave div_rn_core's range: the same
+// steps with the compiler's division, out of line.
+static __device__ __noinline__ void nvfp4_block_nibbles_slow(float4 a, float4 b, float4 c, float4 d, float ts,
+                                                             float bs, uint32_t& w0, uint32_t& w1) {
+  const float v[16] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+  uint32_t words[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    words[i >> 3] |= fp4_nibble(__fdiv_rn(__fdiv_rn(v[i], ts), bs)) << (4 * ((i & 7) ^ 1));
+  w0 = words[0];
+  w1 = words[1];
+}
+
+// E2M1 bin thresholds of one block, in the input's own float domain.
+//
+// The nibble magnitude of x is the number of midpoints m in
+// {.25, .75, 1.25, 1.75, 2.5, 3.5, 5} with q = RN(RN(|x|/ts)/bs) > m. Both
+// roundings are monotone, so each test is |x| > W for one float W per
+// midpoint and block:
+//  * q > m  <=>  q1 = RN(|x|/ts) > m' * bs, m' the midpoint between m and
+//    its float successor (a tie at m' rounds to m, whose significand is
+//    even). m' * bs is exact in double; q1 is a float, so q1 > m' * bs
+//    <=> q1 > Tf = RD_float(m' * bs).
+//  * q1 > Tf  <=>  q1 >= S = succ(Tf)  <=>  |x|/ts > M, or = M when S is
+//    even (M the midpoint of Tf and S). M * ts is exact in double (M has 25
+//    significant bits, ts at most 24), so |x| > M*ts <=> |x| > RD_float(M*ts)
+//    and |x| >= M*ts <=> |x| > pred(RU_float(M*ts)).
+// Valid when ts, bs, every nonzero |x| and the quotients are finite normal
+// floats (the fast-path range of nvfp4_quant_block).
+__device__ __forceinline__ void nvfp4_block_thresholds(float ts, float bs, float (&w)[7]) {
+  const float mids[7] = {0.25f, 0.75f, 1.25f, 1.75f, 2.5f, 3.5f, 5.0f};
+#pragma unroll
+  for (int j = 0; j < 7; ++j) {
+    const double mp = (double)mids[j] + 0.5 * ((double)__uint_as_float(__float_as_uint(mids[j]) + 1u) - mids[j]);
+    const float tf = __double2float_rd(mp * (double)bs);
+    const uint32_t sb = __float_as_uint(tf) + 1u;
+    const double M = 0.5 * ((double)tf + (double)__uint_as_float(sb));
+    const double U = M * (double)ts;
+    w[j] = (sb & 1u) ? __double2float_rd(U) : __uint_as_float(__float_as_uint(__double2float_ru(U)) - 1u);
+  }
 }
 
 // Quantize one 16-element block given the tensor scale (quant.py:169-183).
 // v[16] holds the input values as float. Returns the e4m3 code and the 8
 // packed bytes (high nibble = even k) in w0 (elements 0-7) / w1 (8-15).
-//
-// The reference computes q = RN(RN(x/ts)/bs) with two IEEE divisions per
-// element. Here:
-//  * the block maximum of RN(|x|/ts) is RN(max|x| / ts) (division by a
-//    positive scale is monotone), so the block needs one division for it and
-//    one for the e4m3 scale;
-//  * each element's bin is taken from qa = x * RN(1/RN(ts*bs)), whose
-//    relative distance to the exact q is below 5 * 2^-24; whenever qa lies
-//    within 2^-16 (relative) of a bin boundary, is tiny, or the scales are
-//    not finite positive normals, the element falls back to the exact two
-//    divisions. Every nibble therefore equals the reference's.
+// The reference's steps: bmax = RN(max|x| / ts) (division by a positive
+// scale is monotone, so the block maximum of RN(|x|/ts) is this one
+// quotient), the e4m3 scale bs of RN(max(bmax, 1e-8) / 6), and per element
+// q = RN(RN(x / ts) / bs) binned to E2M1 (ties toward the smaller
+// magnitude). The per-element bins come from nvfp4_block_thresholds when
+// every nonzero |x| is in [2^-30, 2^30], ts in [2^-40, 2^40] and bs in
+// [2^-9, 448] (all quotients then stay finite normal floats); any other
+// block runs the two divisions per element.
 __device__ __forceinline__ uint32_t nvfp4_quant_block(const float (&v)[16], float ts,
                                                       uint32_t& w0, uint32_t& w1) {
-  float amax = 0.0f;
+  float amax = 0.0f, amin = 0x1p30f;
   bool anynan = false;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const float a = fabsf(v[i]);
     anynan |= (a != a);
     amax = fmaxf(amax, a);
+    amin = fminf(amin, a == 0.0f ? 0x1p30f : a);
   }
-  float bmax = anynan ? __int_as_float(0x7FC00000) : __fdiv_rn(amax, ts);
+  const float bmax = anynan ? __int_as_float(0x7FC00000) : div_rn(amax, ts);
   const float bm = (bmax != bmax) ? bmax : fmaxf(bmax, 1e-8f);
-  const uint32_t sf = e4m3_encode(__fdiv_rn(bm, kFp4Max));
+  const uint32_t sf = e4m3_encode(div_rn(bm, kFp4Max));
   const float bs = e4m3_decode(sf);
-  const float prod = ts * bs;
-  const bool fast = (prod > 1e-30f) && (prod < 1e30f) && (ts < 3.0e38f) && (bs < 3.0e38f);
-  const float inv = fast ? __frcp_rn(prod) : 0.0f;
-  uint32_t words[2] = {0u, 0u};
+  const bool fast = !anynan && amax <= 0x1p30f && amin >= 0x1p-30f && ts >= 0x1p-40f && ts <= 0x1p40f &&
+                    bs >= 0x1p-9f && bs <= 448.0f;
+  if (__builtin_expect(fast, 1)) {
+    float w[7];
+    nvfp4_block_thresholds(ts, bs, w);
+    uint32_t words[2] = {0u, 0u};
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const float qa = v[i] * inv;
-    const float m = fabsf(qa);
-    const float e = 1.52587890625e-05f;   // 2^-16
-    bool near = !fast || (m < 1e-30f && v[i] != 0.0f);
-    near |= fabsf(m - 0.25f) <= 0.25f * e;
-    near |= fabsf(m - 0.75f) <= 0.75f * e;
-    near |= fabsf(m - 1.25f) <= 1.25f * e;
-    near |= fabsf(m - 1.75f) <= 1.75f * e;
-    near |= fabsf(m - 2.5f) <= 2.5f * e;
-    near |= fabsf(m - 3.5f) <= 3.5f * e;
-    near |= fabsf(m - 5.0f) <= 5.0f * e;
-    uint32_t nib;
-    if (near) {
-      nib = fp4_nibble(__fdiv_rn(__fdiv_rn(v[i], ts), bs));
-    } else {
-      nib = ((qa < 0.0f) ? 8u : 0u) | (uint32_t)((m > 0.25f) + (m > 0.75f) + (m > 1.25f) + (m > 1.75f) +
-                                                  (m > 2.5f) + (m > 3.5f) + (m > 5.0f));
+    for (int i = 0; i < 16; ++i) {
+      const float a = fabsf(v[i]);
+      const uint32_t nib = (v[i] < 0.0f ? 8u : 0u) | (uint32_t)((a > w[0]) + (a > w[1]) + (a > w[2]) + (a > w[3]) +
+                                                                (a > w[4]) + (a > w[5]) + (a > w[6]));
+      words[i >> 3] |= nib << (4 * ((i & 7) ^ 1));
     }
-    words[i >> 3] |= nib << (4 * ((i & 7) ^ 1));
+    w0 = words[0];
+    w1 = words[1];
+  } else {
+    nvfp4_block_nibbles_slow(make_float4(v[0], v[1], v[2], v[3]), make_float4(v[4], v[5], v[6], v[7]),
+                             make_float4(v[8], v[9], v[10], v[11]), make_float4(v[12], v[13], v[14], v[15]), ts,
+                             bs, w0, w1);
   }
-  w0 = words[0];
-  w1 = words[1];
   return sf;
 }
 

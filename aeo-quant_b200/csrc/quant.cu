@@ -252,18 +252,18 @@ __global__ void __launch_bounds__(256) fp8_rows_kernel(const typename In<DT>::T*
   float s;
   if (mode == AEOQ_FP8_WEIGHT) {
     // (max_abs / 448).clamp(min=1e-8) in the input dtype, then to bf16 (quant.py:101-102)
-    float t = In<DT>::round(__fdiv_rn(amax, kFp8Max));
+    float t = In<DT>::round(div_rn(amax, kFp8Max));
     t = nan_max(t, In<DT>::round(1e-8f));
     s = bf16r(t);
     if (lane == 0) reinterpret_cast<__nv_bfloat16*>(scale_out)[row] = __float2bfloat16_rn(s);
   } else {
     // amax.clamp(min=1e-4) in the input dtype -> f32, / 448 (modeling.py:102-103)
     float a = nan_max(amax, In<DT>::round(1e-4f));
-    s = __fdiv_rn(a, kFp8Max);
+    s = div_rn(a, kFp8Max);
     if (lane == 0) reinterpret_cast<float*>(scale_out)[row] = s;
   }
   uint8_t* qr = q + row * q_ld;
-  for (int64_t i = lane; i < K; i += 32) qr[i] = (uint8_t)e4m3_encode(__fdiv_rn(In<DT>::load(xr + i), s));
+  for (int64_t i = lane; i < K; i += 32) qr[i] = (uint8_t)e4m3_encode(div_rn(In<DT>::load(xr + i), s));
 }
 
 }  // namespace aeoq

@@ -459,7 +459,7 @@ static EncodeTiledFn encode_fn() {
 }
 
 // 2D uint8 tensor map: rows x row_bytes (row stride ld), box 128 B x box_rows, 128-byte swizzle.
-static int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int64_t row_bytes, int64_t ld, int box_rows) {
+int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int64_t row_bytes, int64_t ld, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error(AEOQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};

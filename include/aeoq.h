@@ -271,6 +271,26 @@ AEOQ_API int aeoq_moe_nvfp4_decode_fused(const void* hidden, const void* top_k_i
                                          void* out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * One-token NVFP4 MoE expert forward on the tensor cores (two launches,
+ * the second programmatically dependent on the first). Same math and
+ * rounding points as aeoq_moe_nvfp4_decode (modeling_nvfp4.py:132-186); the
+ * weight scales come as atoms (aeoq_nvfp4_sf_to_atoms): gate_up with
+ * geglu_inter = I, down plain. Workspace: *_tc_workspace_size() bytes,
+ * 256-aligned, first 256 bytes zero before the first call (each call leaves
+ * them zero; calls that overlap on the device must not share it).
+ * hidden % 128 == 0 (<= 4096), inter % 64 == 0 (<= 2048), top_k <= 16.
+ * ------------------------------------------------------------------------ */
+AEOQ_API int aeoq_moe_nvfp4_decode_tc_supported(int64_t top_k, int64_t hidden, int64_t inter);
+AEOQ_API size_t aeoq_moe_nvfp4_decode_tc_workspace_size(int64_t top_k, int64_t hidden, int64_t inter);
+AEOQ_API int aeoq_moe_nvfp4_decode_tc(const void* hidden, const void* top_k_index, int idx_dtype,
+                                      const void* top_k_weights, int64_t top_k, const uint8_t* gate_up,
+                                      const uint8_t* gate_up_atoms, const void* gate_up_ts, int gate_up_ts_dtype,
+                                      const uint8_t* down, const uint8_t* down_atoms, const void* down_ts,
+                                      int down_ts_dtype, int64_t num_experts, int64_t hidden_dim, int64_t inter_dim,
+                                      void* out, void* workspace, size_t workspace_bytes, int* err_word,
+                                      void* stream);
+
+/* ------------------------------------------------------------------------
  * Allocation-free one-token decode. No counterpart in the reference: it
  * exists for callers that cannot allocate device memory where they run the
  * expert forward (a serving runtime that pre-reserves all device memory, a
@@ -293,6 +313,22 @@ AEOQ_API int aeoq_moe_nvfp4_decode_fused_noalloc(const void* hidden, const void*
                                                  const void* down_ts, int down_ts_dtype,
                                                  int64_t num_experts, int64_t hidden_dim, int64_t inter_dim,
                                                  void* out, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Self-test of the device division every quantized bit depends on: counts
+ * (into *mismatches, device memory, accumulated) the operand pairs of a
+ * domain where the library's correctly rounded division differs from the
+ * compiler's __fdiv_rn, and stores the first such (a, b, got, want) in
+ * example[0..3] (device memory). Domains: 0 = every float dividend
+ * significand x every bf16 divisor significand; 1 = every bf16 dividend
+ * significand x every float divisor significand; 2 = 2^28 random pairs over
+ * the full exponent range of the fast path; 3 = the NVFP4 block quantizer
+ * (threshold form) against the reference's division-by-division formula on
+ * 2^22 random and boundary-probing blocks (example holds ts and the 16
+ * inputs of the first mismatching block, 17 floats). No counterpart in the
+ * reference.
+ * ------------------------------------------------------------------------ */
+AEOQ_API int aeoq_selftest_div_rn(int domain, unsigned long long* mismatches, float* example, void* stream);
 
 #ifdef __cplusplus
 }

@@ -161,3 +161,18 @@ def test_grouped_one_token_semantics_matches_fused(full_layer):
         y1 = moe_ops.nvfp4_decode(*args)
         y2 = moe_ops.nvfp4_experts_grouped(*args, one_token_semantics=True)
         assert max_rel_err(bf16_to_np(y2), bf16_to_np(y1)) <= TOL
+
+
+def test_decode_tensor_core_path_matches_cuda_core(full_layer):
+    """Tensor-core one-token decode vs the cooperative CUDA-core kernel: both
+    round once from f32 sums of exact block products."""
+    from aeo_quant_b200.bridges.gemma4 import moe_ops
+    m = full_layer
+    for seed in range(4):
+        h = randn_bf16((1, 2816), 1.0, 1300 + seed)
+        idx, w = routing(1, 128, 8, 1400 + seed)
+        args = (h, idx.cuda(), w.cuda(), m.gate_up_proj, m.gate_up_proj_scale, m.gate_up_proj_scale_2,
+                m.down_proj, m.down_proj_scale, m.down_proj_scale_2)
+        y_tc = moe_ops.nvfp4_decode(*args, path="tc")
+        y_cc = moe_ops.nvfp4_decode(*args, path="fused")
+        assert max_rel_err(bf16_to_np(y_tc), bf16_to_np(y_cc)) <= TOL
