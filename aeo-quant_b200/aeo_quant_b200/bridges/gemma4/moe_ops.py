@@ -59,12 +59,10 @@ def nvfp4_decode(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf
             ws = torch.zeros(lib.aeoq_moe_nvfp4_decode_tc_workspace_size(k, H, I), dtype=torch.uint8,
                              device=hidden.device)
             _TC_WS[key] = ws
-        gu_atoms = A.weight_atoms(gu_sf, E, 2 * I, H, geglu_inter=I)
-        dw_atoms = A.weight_atoms(dw_sf, E, H, I)
         A.check(lib.aeoq_moe_nvfp4_decode_tc(
             hidden.data_ptr(), idx.data_ptr(), A.dtype_code(idx.dtype), w.data_ptr(), k,
-            gu.data_ptr(), gu_atoms.data_ptr(), gu_ts.data_ptr(), A.dtype_code(gu_ts.dtype),
-            dw.data_ptr(), dw_atoms.data_ptr(), dw_ts.data_ptr(), A.dtype_code(dw_ts.dtype),
+            gu.data_ptr(), gu_sf.data_ptr(), gu_ts.data_ptr(), A.dtype_code(gu_ts.dtype),
+            dw.data_ptr(), dw_sf.data_ptr(), dw_ts.data_ptr(), A.dtype_code(dw_ts.dtype),
             E, H, I, out.data_ptr(), ws.data_ptr(), ws.numel(), A.err_word(hidden.device).data_ptr(),
             A.stream_ptr(hidden.device)))
         return out

@@ -2,39 +2,60 @@
 //
 // Restates Gemma4TextExpertsNVFP4._forward_decode_3d (aeo_quant
 // src/aeo_quant/bridges/gemma4/modeling_nvfp4.py:132-186). At one token the
-// work is a stream of the k selected experts' packed weights; the FP4 x FP4
-// products, their e4m3 scaling and the f32 sums are left to tcgen05.mma
-// (kind::mxf4nvf4, M = 128 weight rows, N = 8 with the token in column 0),
-// so the SMs only move bytes and run the small quantizations.
+// work is a stream of the k selected experts' packed weights through
+// tcgen05.mma (kind::mxf4nvf4, block16 e4m3 scales, f32 accumulate in TMEM).
 //
-//  launch 1  gate_up + GeGLU. CTA (m, j): 64 gate rows 64m.. and the 64
-//            matching up rows of expert ids[j], K streamed through an 8-deep
-//            TMA ring. Meanwhile four warps quantize the hidden vector
-//            (quantize_2d_to_nvfp4 semantics, :150-153) straight into the
-//            MMA's B tile and scale atoms. Epilogue: h = bf16(bf16(gelu(g))*u)
-//            (:155-162) to global memory, the CTA's max |h| to a slot.
+// Orientation: the weights are the MMA's N side (B operand, up to 256 rows
+// per instruction) and the token is the M = 128 side (A operand) with the
+// token in row 0. Only accumulator row 0 is read, so A rows 1-127 may hold
+// anything: each 1 KB token tile (8 swizzled rows of 128 B) is followed in
+// shared memory by other buffers that serve as those rows. One instruction
+// thus covers 64 K-values of up to 256 weight rows.
+//
+// Scale factors are taken in the reference's own row layout ([rows][K/16]
+// e4m3 bytes) and written into TMEM by the four epilogue warps with
+// tcgen05.st, in the arrangement tcgen05.cp.32x128b.warpx4 would produce
+// from a 512-byte atom (matrix row r of a 128-row group at lane r % 32 of
+// every lane quadrant, column (r / 32) % 4, byte k of the 64-value step).
+// No precomputed weight layout is needed.
+//
+//  launch 1  gate_up + GeGLU. CTA (m, p, j): T gate rows T*m.. and the T
+//            matching up rows of expert ids[j] (N = 2T), K range p of the
+//            hidden size. TMA streams the weight tiles through a ring while
+//            the epilogue warps quantize the hidden vector
+//            (quantize_2d_to_nvfp4 semantics, :150-153) into the token tile
+//            and both scale sets into TMEM. The K parts of a tile form a
+//            thread-block cluster: rank 0 adds the parts' f32 accumulator
+//            rows in part order from their shared memory (distributed shared
+//            memory), then computes h = bf16(bf16(gelu(bf16(g*a))) *
+//            bf16(u*a)) (:155-162) and the tile's max |h|.
 //  launch 2  down + combine, launched early (programmatic dependent launch):
-//            CTA (m, j) copies its 128 x I down rows of expert ids[j] into
-//            shared memory while launch 1 still runs, then waits, reduces
-//            the maxima to the shared tensor scale (:164-172), quantizes its
-//            slot's h row into the B tile, runs the MMAs, and writes
-//            bf16(bf16(a*d) * w_j) (:183). The last of the k CTAs of a row
-//            tile (arrival counter) sums the k rows in f32 and rounds once
-//            (:184-186). Counters reset themselves.
-//
+//            CTA (t, j) prefetches its N2 down rows of expert ids[j] and
+//            their scales and writes the weight scales into TMEM while
+//            launch 1 still runs; then waits, reduces the maxima to the
+//            shared tensor scale (:164-172), quantizes h[j] into its token
+//            tile, runs the MMAs and writes bf16(bf16(a*d) * w_j) (:183).
+//            The k CTAs of a row tile form a cluster; each sums a slice of
+//            the rows over the k CTAs' shared memory in f32 in expert order
+//            and rounds once (:184-186).
 // Every wait is bounded (sm100::mbar_wait); TMEM is freed on every path.
 #include <cuda.h>
 
-#include <cstdlib>
+#include <algorithm>
 
 #include "common.cuh"
 #include "sm100.cuh"
 
 namespace aeoq {
 
-int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int64_t row_bytes, int64_t ld, int box_rows);
+int make_tmap_bytes(CUtensorMap* m, const void* ptr, int64_t rows, int64_t row_bytes, int64_t ld, int box_bytes,
+                    int box_rows, bool swizzle128);
 
 namespace dtc {
+
+__device__ __forceinline__ int cta_linear() {
+  return (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+}
 
 #ifdef AEOQ_TC_TRACE
 __device__ uint64_t* g_dtrace = nullptr;
@@ -43,76 +64,189 @@ __device__ uint64_t* g_dtrace = nullptr;
     if (g_dtrace) {                                                                                  \
       uint64_t t_;                                                                                   \
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                         \
-      g_dtrace[(kTraceBase + blockIdx.y * gridDim.x + blockIdx.x) * 32 + (slot)] = t_;                \
+      g_dtrace[(kTraceBase + cta_linear()) * 32 + (slot)] = t_;                                       \
     }                                                                                                \
   } while (0)
-#define DC(slot, v) do { if (g_dtrace) g_dtrace[(kTraceBase + blockIdx.y * gridDim.x + blockIdx.x) * 32 + (slot)] = (v); } while (0)
+#define TRACE_BASE(v) constexpr int kTraceBase = (v)
 #else
 #define DT(slot) do {} while (0)
-#define DC(slot, v) do {} while (0)
+#define TRACE_BASE(v)
 #endif
 
 constexpr int kThreads = 192;
-constexpr int kRing = 8;            // launch-1 ring depth (16 KB A tiles)
-constexpr int kN = 8;               // MMA N: the token plus 7 zero columns
-constexpr uint32_t kAccCol = 0, kSfaCol = 8, kSfbCol = 24;   // launch-1 TMEM columns
-constexpr int kMaxKB = 64;          // K / 64 for the hidden size (H <= 4096)
-constexpr int kMaxKB2 = 32;         // K / 64 for the intermediate size (I <= 2048)
+constexpr int kRing = 3;      // launch-1 weight ring depth
+
+__host__ __device__ constexpr int rup(int v, int m) { return (v + m - 1) / m * m; }
+
+// Shape plan, computed once on the host (plan_for) and passed by value.
+struct Plan {
+  int H, I, k;
+  int64_t E;
+  int T;                // launch 1: gate rows (= up rows) per tile, N1 = 2T
+  int tiles;            // I / T
+  int parts;            // K parts of launch 1
+  int Q;                // 64-value K steps per part (multiple of 4)
+  int sfa1, sfb1, cols1;
+  int N2;               // launch 2: down rows per tile
+  int sfa2, sfb2, cols2;
+};
 
 struct Args {
   const __nv_bfloat16* hidden;
   const void* ids; int ids_dt;
   const __nv_bfloat16* topw;
-  const uint8_t* gu_atoms;  const void* gu_ts; int gu_ts_dt;
-  const uint8_t* dw_atoms;  const void* d_ts;  int d_ts_dt;
-  int64_t E, H, I;
-  int k;
-  __nv_bfloat16* h;        // [k][I]
-  uint32_t* parts;          // [k * I / 64] maxima of launch 1
-  __nv_bfloat16* c;         // [k][H] weighted expert outputs
-  uint32_t* counters;       // [H / 128] arrival counters (self-resetting)
-  __nv_bfloat16* out;       // [H]
+  const void* gu_ts; int gu_ts_dt;
+  const uint8_t* d_sf;  const void* d_ts; int d_ts_dt;
+  uint32_t* hmax;        // [k * tiles]   max |h| key per tile
+  __nv_bfloat16* h;      // [k][I]
+  __nv_bfloat16* out;    // [H]
   int* err;
 };
 
-struct Smem1 {
-  uint64_t full[kRing], empty[kRing], bready, accum;
-  uint32_t tmem;
-  uint32_t red[4];
-  float xchg[64];
+// ---- shared-memory layouts (offsets from a 1024-aligned base)
+struct L1 {
+  int a, ring, stage, hid, sf, sfchunk, tok, dv, bars, bytes;
+  __host__ __device__ explicit L1(const Plan& p) {
+    const int nt = p.Q / 4;
+    a = 0;                                   // nt token tiles of 1 KB
+    ring = 1024 * nt;
+    stage = 2 * p.T * 128;
+    hid = ring + kRing * stage;
+    sfchunk = 2 * p.T * 16;                  // per 4 K steps: gate rows, then up rows, 16 B each
+    sf = rup(hid + 2 * p.H, 128);
+    tok = rup(sf + nt * sfchunk, 16);        // token scale bytes, 4 per K step
+    dv = rup(tok + 4 * p.Q, 16);             // 2T f32 accumulator row
+    bars = rup(dv + 8 * p.T, 16);
+    bytes = bars + 256;
+    if (bytes < ring + 16384) bytes = ring + 16384;   // token tiles' rows 8-127 stay inside
+  }
+};
+struct L2 {
+  int a, b, sf, sfrow, tok, dv, bars, bytes;
+  __host__ __device__ explicit L2(const Plan& p) {
+    const int nt = (p.I / 64 + 3) / 4;
+    a = 0;
+    b = 1024 * nt;                           // nt weight tiles of N2 x 128 B
+    sfrow = p.I / 16;
+    sf = b + nt * p.N2 * 128;
+    tok = rup(sf + p.N2 * sfrow, 16);
+    dv = rup(tok + p.I / 16, 16);
+    bars = rup(dv + 4 * p.N2, 16);
+    bytes = bars + 256;
+    if (bytes < b + 16384) bytes = b + 16384;
+  }
 };
 
-// Quantize one 16-value block of bf16 (src) into row 0 of a B tile set:
-// packed bytes at btile + (b / 16) * 1024 + (b % 16) * 8 (row 0 of a
-// 128-byte-swizzled 8-row tile is unpermuted) and its scale at byte b % 4 of
-// row 0 in atom b / 4.
-template <bool kCoherent>
-__device__ __forceinline__ void quant_to_btile(const __nv_bfloat16* src, float ts, int64_t b, uint8_t* btile,
-                                               uint8_t* sfb) {
-  float v[16];
-#pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    const uint4 u = kCoherent ? __ldcg(reinterpret_cast<const uint4*>(src + 8 * q))
-                              : *reinterpret_cast<const uint4*>(src + 8 * q);
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[8 * q + j] = __bfloat162float(e[j]);
-  }
+struct Bars1 {
+  uint64_t full[kRing], empty[kRing], hid, sf, bready, accum;
+  uint32_t tmem;
+  uint32_t red[4];
+};
+struct Bars2 {
+  uint64_t full, bready, accum;
+  uint32_t tmem;
+  uint32_t red[4];
+};
+
+// One 16-value block quantized into row 0 of a token tile set (packed bytes
+// at (bl / 16) * 1024 + (bl % 16) * 8; row 0 of a 128-byte-swizzled tile is
+// unpermuted) with its scale byte at tok[bl].
+__device__ __forceinline__ void quant_block_row0(const float (&v)[16], float ts, int bl, uint8_t* tiles,
+                                                 uint8_t* tok) {
   uint32_t w0, w1;
   const uint32_t sf = nvfp4_quant_block(v, ts, w0, w1);
-  *reinterpret_cast<uint2*>(btile + (b >> 4) * 1024 + (b & 15) * 8) = make_uint2(w0, w1);
-  sfb[(b >> 2) * 512 + (b & 3)] = (uint8_t)sf;
+  *reinterpret_cast<uint2*>(tiles + (bl >> 4) * 1024 + (bl & 15) * 8) = make_uint2(w0, w1);
+  tok[bl] = (uint8_t)sf;
 }
 
-// Max |x| key over n bf16 values by the 128 threads of warps 2-5.
-__device__ __forceinline__ uint32_t amax_key128(const __nv_bfloat16* x, int64_t n, int t, uint32_t* red) {
-  uint32_t key = 0;
-  for (int64_t i = t; i < n / 8; i += 128) {
-    const uint4 u = *reinterpret_cast<const uint4*>(x + 8 * i);
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+__device__ __forceinline__ void unpack16(uint4 u0, uint4 u1, float (&v)[16]) {
+  const __nv_bfloat16* e0 = reinterpret_cast<const __nv_bfloat16*>(&u0);
+  const __nv_bfloat16* e1 = reinterpret_cast<const __nv_bfloat16*>(&u1);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) key = max(key, In<AEOQ_BF16>::abs_key(e[j]));
+  for (int i = 0; i < 8; ++i) {
+    v[i] = __bfloat162float(e0[i]);
+    v[8 + i] = __bfloat162float(e1[i]);
   }
+}
+
+// Token scales into TMEM, column 4 * kb of the warp's quadrant (lane 0 holds
+// row 0's four bytes; the other lanes' values belong to rows whose results
+// are never read).
+__device__ __forceinline__ void st_token_scales(uint32_t taddr, const uint8_t* tok, int nkb, int lane) {
+  for (int kb = 0; kb < nkb; ++kb)
+    sm100::tmem_st1(taddr + 4 * kb, lane == 0 ? *reinterpret_cast<const uint32_t*>(tok + 4 * kb) : 0u);
+}
+
+// Weight scales into TMEM for the N-row B operand: 8 columns per K step,
+// column 4a + i of lane l = matrix row 128a + 32i + l (rows >= n_rows zero).
+// Launch-1 layout: chunk c (4 K steps) holds each of the N rows' 16 scale
+// bytes contiguously (row r at c * chunk_bytes + 16 r), so every lane reads a
+// row's four steps with one conflict-free 16-byte load.
+__device__ __forceinline__ void st_weight_scales_chunked(uint32_t taddr, const uint8_t* sf, int chunk_bytes,
+                                                         int n_rows, int nkb, int lane) {
+  for (int c = 0; c < (nkb + 3) / 4; ++c) {
+    uint4 v[2][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int row = 128 * a + 32 * i + lane;
+        v[a][i] = *reinterpret_cast<const uint4*>(sf + c * chunk_bytes + 16 * (row < n_rows ? row : 0));
+        if (row >= n_rows) v[a][i] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    uint32_t r[32];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        r[0 * 8 + 4 * a + i] = v[a][i].x;
+        r[1 * 8 + 4 * a + i] = v[a][i].y;
+        r[2 * 8 + 4 * a + i] = v[a][i].z;
+        r[3 * 8 + 4 * a + i] = v[a][i].w;
+      }
+    sm100::tmem_st32(taddr + 32 * c, r);
+  }
+}
+
+// Same, from row-major scale rows of sfrow bytes (a multiple of 4; words
+// past a row's last K step are read but not used by any MMA).
+__device__ __forceinline__ void st_weight_scales_rows(uint32_t taddr, const uint8_t* sf, int sfrow, int n_rows,
+                                                      int nkb, int lane) {
+  for (int c = 0; c < (nkb + 3) / 4; ++c) {
+    uint32_t r[32];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int row = 128 * a + 32 * i + lane;
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(sf + (row < n_rows ? row : 0) * sfrow) + 4 * c;
+#pragma unroll
+        for (int kbi = 0; kbi < 4; ++kbi) r[8 * kbi + 4 * a + i] = row < n_rows ? src[kbi] : 0u;
+      }
+    sm100::tmem_st32(taddr + 32 * c, r);
+  }
+}
+
+// Accumulator row 0 (lane 0 of quadrant 0) -> dv[0..n) in shared memory;
+// run by the warp whose lane quadrant is 0.
+__device__ __forceinline__ void read_row0(uint32_t tmem, int n, bool keep, float* dv, int lane) {
+  for (int c = 0; c < (n + 63) / 64; ++c) {
+    uint32_t r0[32], r1[32];
+    sm100::tmem_ld32_nowait(tmem + 64 * c, r0);
+    sm100::tmem_ld32_nowait(tmem + 64 * c + 32, r1);
+    sm100::tmem_ld_wait();
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (64 * c + i < n) dv[64 * c + i] = keep ? __uint_as_float(r0[i]) : 0.0f;
+        if (64 * c + 32 + i < n) dv[64 * c + 32 + i] = keep ? __uint_as_float(r1[i]) : 0.0f;
+      }
+    }
+  }
+  __syncwarp();
+}
+
+__device__ __forceinline__ uint32_t block_max128(uint32_t key, int t, uint32_t* red) {
   key = warp_umax(key);
   if ((t & 31) == 0) red[t >> 5] = key;
   asm volatile("bar.sync 2, 128;" ::: "memory");
@@ -121,303 +255,377 @@ __device__ __forceinline__ uint32_t amax_key128(const __nv_bfloat16* x, int64_t 
   return key;
 }
 
-__device__ __forceinline__ void zero_smem128(uint8_t* p, int bytes, int t) {
-  for (int i = t; i < bytes / 16; i += 128) reinterpret_cast<uint4*>(p)[i] = make_uint4(0, 0, 0, 0);
-}
-
 // ------------------------------------------------------------------ launch 1
-__global__ void __launch_bounds__(kThreads, 1) decode_gateup_tc_kernel(const __grid_constant__ CUtensorMap tmA,
-                                                                       const Args a) {
-  constexpr int kTraceBase = 0;
-  if (threadIdx.x == 0) DT(0);
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_gateup_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmS,
+                            const Args a, const Plan pl) {
+  TRACE_BASE(0);
   extern __shared__ __align__(1024) uint8_t dsm[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
-  const int H = (int)a.H, I = (int)a.I;
-  const int kb_total = H / 64, num_kt = (H + 255) / 256;
-  uint8_t* ringA = base;                                   // kRing x 16 KB
-  uint8_t* ringSFA = ringA + kRing * 16384;                // kRing x 2 KB
-  uint8_t* btile = ringSFA + kRing * 2048;                 // num_kt x 1 KB
-  uint8_t* sfb = btile + num_kt * 1024;                    // kb_total x 512 B
-  Smem1* sh = reinterpret_cast<Smem1*>(sfb + kb_total * 512);
+  const L1 L(pl);
+  uint8_t* tokA = base + L.a;
+  uint8_t* ring = base + L.ring;
+  const __nv_bfloat16* hid = reinterpret_cast<const __nv_bfloat16*>(base + L.hid);
+  uint8_t* sfs = base + L.sf;
+  uint8_t* tok = base + L.tok;
+  float* dv = reinterpret_cast<float*>(base + L.dv);
+  Bars1* sh = reinterpret_cast<Bars1*>(base + L.bars);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int m = blockIdx.x, j = blockIdx.y;
+  const int m = blockIdx.x, p = blockIdx.y, j = blockIdx.z;
+  const int T = pl.T, N1 = 2 * T, H = pl.H, I = pl.I;
+  const int kb0 = p * pl.Q, nkb = min(pl.Q, H / 64 - kb0), nt = (nkb + 3) / 4;
+  if (tid == 0) DT(0);
 
   if (tid == 0) {
     for (int s = 0; s < kRing; ++s) {
       sm100::mbar_init(&sh->full[s], 1);
       sm100::mbar_init(&sh->empty[s], 1);
     }
-    sm100::mbar_init(&sh->bready, 4);
+    sm100::mbar_init(&sh->hid, 1);
+    sm100::mbar_init(&sh->sf, 1);
+    sm100::mbar_init(&sh->bready, 5);
     sm100::mbar_init(&sh->accum, 1);
     sm100::fence_barrier_init();
-    sm100::prefetch_tmap(&tmA);
+    sm100::prefetch_tmap(&tmW);
+    sm100::prefetch_tmap(&tmS);
   }
-  if (warp == 1) sm100::tmem_alloc(&sh->tmem, 64);
+  if (warp == 1) sm100::tmem_alloc(&sh->tmem, (uint32_t)pl.cols1);
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = sh->tmem;
   pdl_wait();        // inputs may come from the preceding kernel
-  pdl_trigger();     // the down launch may start its weight prefetch
   const int64_t e = load_index(a.ids, a.ids_dt, j);
-  const bool valid = e >= 0 && e < a.E;
+  const bool valid = e >= 0 && e < pl.E;
+  const int32_t row_g = (int32_t)((valid ? e : 0) * 2 * I + (int64_t)T * m);
+  float alpha = 0.0f;
 
   if (warp == 0) {
     const bool leader = sm100::elect_one();
-    const uint8_t* sfa_src = a.gu_atoms + ((valid ? e : 0) * (I / 64) + m) * (int64_t)kb_total * 512;
-    const int32_t row_g = (int32_t)((valid ? e : 0) * 2 * I + 64 * m);
-    for (int kt = 0; kt < num_kt && valid; ++kt) {
+    if (leader) {
+      // the hidden vector first: the quantization waits on it, the MMAs on that
+      sm100::mbar_arrive_expect_tx(&sh->hid, (uint32_t)(2 * H));
+      bulk_g2s(base + L.hid, a.hidden, (uint32_t)(2 * H), &sh->hid);
+      if (valid) {
+        sm100::mbar_arrive_expect_tx(&sh->sf, (uint32_t)(nt * L.sfchunk));
+        for (int c = 0; c < nt; ++c) {
+          sm100::tma_load_2d(sfs + c * L.sfchunk, &tmS, 4 * kb0 + 16 * c, row_g, &sh->sf);
+          sm100::tma_load_2d(sfs + c * L.sfchunk + 16 * T, &tmS, 4 * kb0 + 16 * c, row_g + I, &sh->sf);
+        }
+      }
+    }
+    __syncwarp();
+    // The weight stream starts once the hidden vector and the scales have
+    // landed: issued together, the small copies would queue behind it, and
+    // the MMAs cannot start before the quantization they feed.
+    bool go = sm100::mbar_wait(&sh->hid, 0, a.err, 47);
+    if (valid) go = go && sm100::mbar_wait(&sh->sf, 0, a.err, 48);
+    bool triggered = false;
+    for (int kt = 0; kt < nt && valid && go; ++kt) {
       const int s = kt % kRing;
       const uint32_t ph = (kt / kRing) & 1;
-      if (!sm100::mbar_wait(&sh->empty[s], ph ^ 1, a.err, 21)) break;
-      const int nkb = min(4, kb_total - kt * 4);
+      if (!sm100::mbar_wait(&sh->empty[s], ph ^ 1, a.err, 41)) break;
       if (leader) {
-        sm100::mbar_arrive_expect_tx(&sh->full[s], 16384u + (uint32_t)nkb * 512u);
-        bulk_g2s(ringSFA + s * 2048, sfa_src + (size_t)kt * 4 * 512, (uint32_t)nkb * 512, &sh->full[s]);
-        sm100::tma_load_2d(ringA + s * 16384, &tmA, kt * 128, row_g, &sh->full[s]);
-        sm100::tma_load_2d(ringA + s * 16384 + 8192, &tmA, kt * 128, row_g + I, &sh->full[s]);
+        const int32_t x = 32 * kb0 + 128 * kt;
+        sm100::mbar_arrive_expect_tx(&sh->full[s], (uint32_t)L.stage);
+        sm100::tma_load_2d(ring + s * L.stage, &tmW, x, row_g, &sh->full[s]);
+        sm100::tma_load_2d(ring + s * L.stage + T * 128, &tmW, x, row_g + I, &sh->full[s]);
       }
       __syncwarp();
+      if (!triggered && kt + 1 >= min(kRing, nt)) {
+        pdl_trigger();   // the down launch may start its prefetch now
+        triggered = true;
+        // Until the MMAs free a stage this warp is idle: it writes the
+        // weight scales (lane quadrant 0, the only one accumulator row 0
+        // reads), in parallel with the quantization of the hidden vector.
+        st_weight_scales_chunked(tmem + pl.sfb1, sfs, L.sfchunk, N1, nkb, lane);
+        sm100::tmem_st_wait();
+        sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&sh->bready);
+      }
+    }
+    if (!triggered) {
+      pdl_trigger();
+      if (lane == 0) sm100::mbar_arrive(&sh->bready);
     }
   } else if (warp == 1) {
     const bool leader = sm100::elect_one();
-    const uint32_t idesc = sm100::idesc_nvf4(kN);
-    bool ok = sm100::mbar_wait(&sh->bready, 0, a.err, 22);
-    if (sm100::elect_one()) DT(5);
-    for (int kt = 0; kt < num_kt && ok && valid; ++kt) {
+    const uint32_t idesc = sm100::idesc_nvf4((uint32_t)N1);
+    bool ok = sm100::mbar_wait(&sh->bready, 0, a.err, 42);
+    sm100::tc_fence_after();
+    if (tid == 32) DT(2);
+    for (int kt = 0; kt < nt && ok && valid; ++kt) {
       const int s = kt % kRing;
       const uint32_t ph = (kt / kRing) & 1;
-      if (!sm100::mbar_wait(&sh->full[s], ph, a.err, 23)) { ok = false; break; }
-      if (kt < 11 && sm100::elect_one()) DT(6 + kt);
-      const long long c0_ = clock64();
+      if (!sm100::mbar_wait(&sh->full[s], ph, a.err, 43)) { ok = false; break; }
       sm100::tc_fence_after();
-      const int nkb = min(4, kb_total - kt * 4);
+      const int n4 = min(4, nkb - 4 * kt);
       if (leader) {
-        for (int kb = 0; kb < nkb; ++kb) {
-          sm100::tc_cp_32x128b_warpx4(tmem + kSfaCol + 4 * kb,
-                                      sm100::sdesc_sf_atom(sm100::smem_u32(ringSFA + s * 2048 + kb * 512)));
-          sm100::tc_cp_32x128b_warpx4(tmem + kSfbCol + 4 * kb,
-                                      sm100::sdesc_sf_atom(sm100::smem_u32(sfb + (kt * 4 + kb) * 512)));
-        }
-        for (int kb = 0; kb < nkb; ++kb) {
-          const uint64_t ad = sm100::sdesc_k_sw128(sm100::smem_u32(ringA + s * 16384) + kb * 32);
-          const uint64_t bd = sm100::sdesc_k_sw128(sm100::smem_u32(btile + kt * 1024) + kb * 32);
-          sm100::tc_mma_nvf4(tmem + kAccCol, ad, bd, idesc, tmem + kSfaCol + 4 * kb, tmem + kSfbCol + 4 * kb,
-                             (kt | kb) ? 1u : 0u);
+        for (int kb = 0; kb < n4; ++kb) {
+          const int kk = 4 * kt + kb;
+          const uint64_t ad = sm100::sdesc_k_sw128(sm100::smem_u32(tokA + kt * 1024) + kb * 32);
+          const uint64_t bd = sm100::sdesc_k_sw128(sm100::smem_u32(ring + s * L.stage) + kb * 32);
+          sm100::tc_mma_nvf4(tmem, ad, bd, idesc, tmem + pl.sfa1 + 4 * kk, tmem + pl.sfb1 + 8 * kk, kk ? 1u : 0u);
         }
         sm100::tc_commit(&sh->empty[s]);
-        if (kt < 11) DC(17 + kt, clock64() - c0_);
       }
       __syncwarp();
     }
     if (leader) sm100::tc_commit(&sh->accum);
     __syncwarp();
   } else {
-    // ---- warps 2-5: hidden quant into the B tile, then the epilogue
+    // ---- warps 2-5: quantize, scales into TMEM, then the epilogue
     const int t = tid - 64;
-    zero_smem128(btile, num_kt * 1024, t);
-    zero_smem128(sfb, kb_total * 512, t);
-    const uint32_t key = amax_key128(a.hidden, H, t, sh->red);   // (its barriers order the zeroing too)
-    if (t == 0) DT(4);
+    const uint32_t qaddr = (uint32_t)(32 * (warp & 3)) << 16;
+    const bool hid_ok = sm100::mbar_wait(&sh->hid, 0, a.err, 44);
+    uint32_t key = 0;
+    if (hid_ok) {
+      for (int i = t; i < H / 8; i += 128) {
+        const uint4 u = reinterpret_cast<const uint4*>(hid)[i];
+        const __nv_bfloat16* v8 = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) key = max(key, In<AEOQ_BF16>::abs_key(v8[q]));
+      }
+    }
+    key = block_max128(key, t, sh->red);
     const float ts = nvfp4_tensor_scale<AEOQ_BF16>(In<AEOQ_BF16>::key_to_f(key));
-    for (int64_t b = t; b < H / 16; b += 128) quant_to_btile<false>(a.hidden + 16 * b, ts, b, btile, sfb);
-    sm100::fence_proxy_async_smem();
+    for (int bl = t; bl < 4 * nkb; bl += 128) {
+      const uint4* src = reinterpret_cast<const uint4*>(hid + 16 * (4 * kb0 + bl));
+      float v[16];
+      unpack16(src[0], src[1], v);
+      quant_block_row0(v, ts, bl, tokA, tok);
+    }
+    sm100::fence_proxy_async_smem();   // token tiles: generic writes -> MMA reads
+    asm volatile("bar.sync 2, 128;" ::: "memory");
+    if (t == 0) DT(1);
+    if (warp == 4) st_token_scales(tmem + qaddr + pl.sfa1, tok, nkb, lane);
+    if (t == 0) DT(5);
+    if (t == 0) DT(7);
+    sm100::tmem_st_wait();
+    if (t == 0) DT(8);
+    sm100::tc_fence_before();
     __syncwarp();
     if (lane == 0) sm100::mbar_arrive(&sh->bready);
-    if (t == 0) DT(1);
-    const float alpha = ts * load_scalar_f(a.gu_ts, a.gu_ts_dt);
-    const bool ok = sm100::mbar_wait(&sh->accum, 0, a.err, 24);
-    if (t == 0) DT(2);
+    alpha = ts * load_scalar_f(a.gu_ts, a.gu_ts_dt);
+    const bool ok = sm100::mbar_wait(&sh->accum, 0, a.err, 46);
     sm100::tc_fence_after();
-    const int q = warp & 3, row = 32 * q + lane;
-    float v[16];
-    sm100::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + kAccCol, v);
-    const float y = (ok && valid) ? bf16r(v[0] * alpha) : 0.0f;
-    if (row >= 64) sh->xchg[row - 64] = y;
-    asm volatile("bar.sync 2, 128;" ::: "memory");
+    if (t == 0) DT(3);
+    if (warp == 4) read_row0(tmem, N1, ok && valid, dv, lane);
+  }
+  // The K parts of a tile form one cluster: rank 0 adds the parts' rows (in
+  // part order, from each CTA's shared memory) and finishes the tile.
+  sm100::tc_fence_before();
+  sm100::cluster_sync();
+  if (warp >= 2 && sm100::cluster_ctarank() == 0) {
+    const int t = tid - 64;
+    if (t == 0) DT(9);
     uint32_t hkey = 0;
-    if (row < 64) {
-      const __nv_bfloat16 hv = __float2bfloat16_rn(bf16r(gelu_tanh(y)) * sh->xchg[row]);
-      a.h[(int64_t)j * I + 64 * m + row] = hv;
+    if (t < T) {
+      float g = 0.0f, u = 0.0f;
+      for (int pp = 0; pp < pl.parts; ++pp) {
+        const float gp = sm100::ld_dsmem_f32(sm100::dsmem_addr(dv + t, (uint32_t)pp));
+        const float up = sm100::ld_dsmem_f32(sm100::dsmem_addr(dv + T + t, (uint32_t)pp));
+        g = pp ? g + gp : gp;
+        u = pp ? u + up : up;
+      }
+      const float yg = bf16r(g * alpha), yu = bf16r(u * alpha);
+      const __nv_bfloat16 hv = __float2bfloat16_rn(bf16r(gelu_tanh(yg)) * yu);
+      a.h[(int64_t)j * I + (int64_t)T * m + t] = hv;
       hkey = In<AEOQ_BF16>::abs_key(hv);
     }
-    hkey = warp_umax(hkey);
-    if (lane == 0) sh->red[warp & 3] = hkey;
-    asm volatile("bar.sync 2, 128;" ::: "memory");
+    hkey = block_max128(hkey, t, sh->red);
     if (t == 0) {
-      a.parts[(int64_t)j * gridDim.x + m] = max(max(sh->red[0], sh->red[1]), max(sh->red[2], sh->red[3]));
-      DT(3);
+      a.hmax[(int64_t)j * pl.tiles + m] = hkey;
+      DT(4);
     }
   }
-  sm100::tc_fence_before();
+  sm100::cluster_sync();   // every part's row has been read
   __syncthreads();
   if (warp == 1) {
     sm100::tc_fence_after();
-    sm100::tmem_dealloc(tmem, 64);
+    sm100::tmem_dealloc(tmem, (uint32_t)pl.cols1);
   }
 }
 
 // ------------------------------------------------------------------ launch 2
-struct Smem2 {
-  uint64_t full, bready, accum;
-  uint32_t tmem;
-  uint32_t red[4];
-  int last;
-};
-
-__global__ void __launch_bounds__(kThreads, 1) decode_down_tc_kernel(const __grid_constant__ CUtensorMap tmD,
-                                                                     const Args a, int n_parts) {
-  constexpr int kTraceBase = 4096;
-  if (threadIdx.x == 0) DT(0);
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_down_tc_kernel(const __grid_constant__ CUtensorMap tmD, const Args a, const Plan pl) {
+  TRACE_BASE(4096);
   extern __shared__ __align__(1024) uint8_t dsm[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
-  const int H = (int)a.H, I = (int)a.I;
-  const int kb_total = I / 64, num_kt = (I + 255) / 256;
-  // swizzled tiles first: both must start on 1024-byte boundaries
-  uint8_t* tileA = base;                         // num_kt x 16 KB
-  uint8_t* btile = tileA + num_kt * 16384;       // num_kt x 1 KB
-  uint8_t* sfa = btile + num_kt * 1024;          // kb_total x 512 B
-  uint8_t* sfb = sfa + kb_total * 512;           // kb_total x 512 B
-  Smem2* sh = reinterpret_cast<Smem2*>(sfb + kb_total * 512);
+  const L2 L(pl);
+  uint8_t* tokA = base + L.a;
+  uint8_t* btile = base + L.b;
+  uint8_t* sfs = base + L.sf;
+  uint8_t* tok = base + L.tok;
+  float* dv = reinterpret_cast<float*>(base + L.dv);
+  Bars2* sh = reinterpret_cast<Bars2*>(base + L.bars);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int m = blockIdx.x, j = blockIdx.y;
-  // TMEM: accumulator (8 columns) + all K steps' scale atoms of A and B;
-  // sized to the shape so several CTAs of this kernel share an SM.
-  const uint32_t acc_col = 0, sfa_col = 8, sfb_col = 8 + 4 * kb_total;
-  uint32_t tcols = 32;
-  while (tcols < 8u + 8u * kb_total) tcols <<= 1;
+  const int t2 = blockIdx.x, j = blockIdx.y;
+  const int H = pl.H, I = pl.I, N2 = pl.N2, kb2 = I / 64, nt = (kb2 + 3) / 4;
+  if (tid == 0) DT(0);
 
   if (tid == 0) {
     sm100::mbar_init(&sh->full, 1);
-    sm100::mbar_init(&sh->bready, 4);
+    sm100::mbar_init(&sh->bready, 4);   // the four epilogue warps
     sm100::mbar_init(&sh->accum, 1);
     sm100::fence_barrier_init();
     sm100::prefetch_tmap(&tmD);
   }
-  if (warp == 1) sm100::tmem_alloc(&sh->tmem, tcols);
+  __syncthreads();
+  // The ids, the down weights and their scales do not depend on launch 1.
+  const int64_t e = load_index(a.ids, a.ids_dt, j);
+  const bool valid = e >= 0 && e < pl.E;
+  if (warp == 0 && valid && sm100::elect_one()) {
+    const int32_t row0 = (int32_t)(e * H + (int64_t)N2 * t2);
+    sm100::mbar_arrive_expect_tx(&sh->full, (uint32_t)(nt * N2 * 128 + N2 * L.sfrow));
+    bulk_g2s(sfs, a.d_sf + (int64_t)row0 * L.sfrow, (uint32_t)(N2 * L.sfrow), &sh->full);
+    for (int kt = 0; kt < nt; ++kt) sm100::tma_load_2d(btile + kt * N2 * 128, &tmD, 128 * kt, row0, &sh->full);
+  }
+  // May wait until a launch-1 CTA on this SM releases its columns.
+  if (warp == 1) sm100::tmem_alloc(&sh->tmem, (uint32_t)pl.cols2);
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = sh->tmem;
-  // The ids and the down weights do not depend on launch 1: fetch them now.
-  const int64_t e = load_index(a.ids, a.ids_dt, j);
-  const bool valid = e >= 0 && e < a.E;
+  if (tid == 0) DT(8);
 
-  if (warp == 0) {
-    if (sm100::elect_one() && valid) {
-#ifdef AEOQ_TC_TRACE
-      DT(5);
-#endif
-      sm100::mbar_arrive_expect_tx(&sh->full, (uint32_t)(num_kt * 16384 + kb_total * 512));
-      bulk_g2s(sfa, a.dw_atoms + (e * (H / 128) + m) * (int64_t)kb_total * 512, (uint32_t)kb_total * 512,
-               &sh->full);
-      for (int kt = 0; kt < num_kt; ++kt)
-        sm100::tma_load_2d(tileA + kt * 16384, &tmD, kt * 128, (int32_t)(e * H + 128 * m), &sh->full);
-    }
-    __syncwarp();
-  } else if (warp == 1) {
+  if (warp == 1) {
     const bool leader = sm100::elect_one();
-    bool ok = valid && sm100::mbar_wait(&sh->full, 0, a.err, 31);
-    if (sm100::elect_one()) DT(8);
-    ok = ok && sm100::mbar_wait(&sh->bready, 0, a.err, 32);
-    if (sm100::elect_one()) DT(6);
-    const long long c0_ = clock64();
+    bool ok = sm100::mbar_wait(&sh->bready, 0, a.err, 51);
+    if (valid) ok = ok && sm100::mbar_wait(&sh->full, 0, a.err, 52);
     sm100::tc_fence_after();
-    if (ok && leader) {
-      const uint32_t idesc = sm100::idesc_nvf4(kN);
-      for (int kb = 0; kb < kb_total; ++kb) {
-        sm100::tc_cp_32x128b_warpx4(tmem + sfa_col + 4 * kb, sm100::sdesc_sf_atom(sm100::smem_u32(sfa + kb * 512)));
-        sm100::tc_cp_32x128b_warpx4(tmem + sfb_col + 4 * kb, sm100::sdesc_sf_atom(sm100::smem_u32(sfb + kb * 512)));
+    if (tid == 32) DT(2);
+    if (ok && valid && leader) {
+      const uint32_t idesc = sm100::idesc_nvf4((uint32_t)N2);
+      for (int kb = 0; kb < kb2; ++kb) {
+        const uint64_t ad = sm100::sdesc_k_sw128(sm100::smem_u32(tokA + (kb >> 2) * 1024) + (kb & 3) * 32);
+        const uint64_t bd = sm100::sdesc_k_sw128(sm100::smem_u32(btile + (kb >> 2) * N2 * 128) + (kb & 3) * 32);
+        sm100::tc_mma_nvf4(tmem, ad, bd, idesc, tmem + pl.sfa2 + 4 * kb, tmem + pl.sfb2 + 8 * kb, kb ? 1u : 0u);
       }
-      for (int kb = 0; kb < kb_total; ++kb) {
-        const int kt = kb >> 2, r = kb & 3;
-        const uint64_t ad = sm100::sdesc_k_sw128(sm100::smem_u32(tileA + kt * 16384) + r * 32);
-        const uint64_t bd = sm100::sdesc_k_sw128(sm100::smem_u32(btile + kt * 1024) + r * 32);
-        sm100::tc_mma_nvf4(tmem + acc_col, ad, bd, idesc, tmem + sfa_col + 4 * kb, tmem + sfb_col + 4 * kb,
-                           kb ? 1u : 0u);
-      }
-      DC(9, clock64() - c0_);
     }
     if (leader) sm100::tc_commit(&sh->accum);
     __syncwarp();
-  } else {
+  } else if (warp >= 2) {
     const int t = tid - 64;
-    zero_smem128(btile, num_kt * 1024, t);
-    zero_smem128(sfb, kb_total * 512, t);
+    const uint32_t qaddr = (uint32_t)(32 * (warp & 3)) << 16;
+    if (valid && sm100::mbar_wait(&sh->full, 0, a.err, 53)) {
+      if (t == 0) DT(5);
+      if (warp == 4) st_weight_scales_rows(tmem + qaddr + pl.sfb2, sfs, L.sfrow, N2, kb2, lane);
+    }
     pdl_wait();   // launch 1 complete: h and the maxima are visible
     if (t == 0) DT(1);
+    // this thread's first h block is loaded alongside the maxima (one round trip)
+    uint4 h0 = make_uint4(0u, 0u, 0u, 0u), h1 = h0;
+    if (t < I / 16) {
+      const uint4* src = reinterpret_cast<const uint4*>(a.h + (int64_t)j * I + 16 * t);
+      h0 = __ldcg(src);
+      h1 = __ldcg(src + 1);
+    }
     uint32_t key = 0;
-    for (int i = t; i < n_parts; i += 128) key = max(key, __ldcg(a.parts + i));
-    key = warp_umax(key);
-    if (lane == 0) sh->red[t >> 5] = key;
-    asm volatile("bar.sync 2, 128;" ::: "memory");
-    key = max(max(sh->red[0], sh->red[1]), max(sh->red[2], sh->red[3]));
-    if (t == 0) DT(7);
+    const int n_parts = pl.k * pl.tiles;
+    for (int i = t; i < n_parts; i += 128) key = max(key, __ldcg(a.hmax + i));
+    key = block_max128(key, t, sh->red);
+    if (t == 0) DT(6);
     const float ts = nvfp4_tensor_scale<AEOQ_BF16>(In<AEOQ_BF16>::key_to_f(key));
-    for (int64_t b = t; b < I / 16; b += 128)
-      quant_to_btile<true>(a.h + (int64_t)j * I + 16 * b, ts, b, btile, sfb);
+    for (int bl = t; bl < I / 16; bl += 128) {
+      if (bl != t) {
+        const uint4* src = reinterpret_cast<const uint4*>(a.h + (int64_t)j * I + 16 * bl);
+        h0 = __ldcg(src);
+        h1 = __ldcg(src + 1);
+      }
+      float v[16];
+      unpack16(h0, h1, v);
+      quant_block_row0(v, ts, bl, tokA, tok);
+    }
     sm100::fence_proxy_async_smem();
+    asm volatile("bar.sync 2, 128;" ::: "memory");
+    if (warp == 4) st_token_scales(tmem + qaddr + pl.sfa2, tok, kb2, lane);
+    sm100::tmem_st_wait();
+    sm100::tc_fence_before();
     __syncwarp();
     if (lane == 0) sm100::mbar_arrive(&sh->bready);
     const float alpha = ts * load_scalar_f(a.d_ts, a.d_ts_dt);
     const float wj = __bfloat162float(a.topw[j]);
-    if (t == 0) DT(2);
-    const bool ok = sm100::mbar_wait(&sh->accum, 0, a.err, 33);
-    if (t == 0) DT(3);
+    const bool ok = sm100::mbar_wait(&sh->accum, 0, a.err, 54);
     sm100::tc_fence_after();
-    const int q = warp & 3, row = 32 * q + lane;
-    float v[16];
-    sm100::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + acc_col, v);
-    const float y = (ok && valid) ? bf16r(bf16r(v[0] * alpha) * wj) : 0.0f;
-    a.c[(int64_t)j * H + 128 * m + row] = __float2bfloat16_rn(y);
-    __threadfence();
+    if (t == 0) DT(3);
+    if (warp == 4) read_row0(tmem, N2, ok && valid, dv, lane);
     asm volatile("bar.sync 2, 128;" ::: "memory");
-    if (t == 0) {
-      sh->last = (atomicAdd(a.counters + m, 1u) == (uint32_t)a.k - 1) ? 1 : 0;
-      __threadfence();
-    }
-    asm volatile("bar.sync 2, 128;" ::: "memory");
-    if (sh->last) {
-      // the last expert of this row tile: f32 sum over the k slots, one rounding
-      float s = 0.f;
-      for (int jj = 0; jj < a.k; ++jj) s += __bfloat162float(__ldcg(a.c + (int64_t)jj * H + 128 * m + row));
-      a.out[128 * m + row] = __float2bfloat16_rn(s);
-      if (t == 0) a.counters[m] = 0;
+    for (int i = t; i < N2; i += 128) dv[i] = bf16r(bf16r(dv[i] * alpha) * wj);
+  }
+  // The k experts of a row tile form one cluster: CTA rank r sums rows
+  // [r*R, r*R + R) over the k CTAs' shared memory in expert order (f32, one
+  // rounding) and writes them.
+  sm100::tc_fence_before();
+  sm100::cluster_sync();
+  if (warp >= 2) {
+    const int t = tid - 64;
+    if (t == 0) DT(7);
+    const int R = (N2 + pl.k - 1) / pl.k, r0 = (int)sm100::cluster_ctarank() * R;
+    for (int i = r0 + t; i < min(N2, r0 + R); i += 128) {
+      float s = 0.0f;
+      for (int jj = 0; jj < pl.k; ++jj) s += sm100::ld_dsmem_f32(sm100::dsmem_addr(dv + i, (uint32_t)jj));
+      a.out[(int64_t)N2 * t2 + i] = __float2bfloat16_rn(s);
     }
     if (t == 0) DT(4);
   }
-  sm100::tc_fence_before();
+  sm100::cluster_sync();   // every CTA's rows have been read
   __syncthreads();
   if (warp == 1) {
     sm100::tc_fence_after();
-    sm100::tmem_dealloc(tmem, tcols);
+    sm100::tmem_dealloc(tmem, (uint32_t)pl.cols2);
   }
 }
 
-size_t smem1_bytes(int64_t H) {
-  return 1024 + kRing * (16384 + 2048) + (size_t)((H + 255) / 256) * 1024 + (size_t)(H / 64) * 512 + sizeof(Smem1);
-}
-size_t smem2_bytes(int64_t I) {
-  return 1024 + (size_t)((I + 255) / 256) * (16384 + 1024) + (size_t)(I / 64) * 1024 + sizeof(Smem2);
+constexpr int kSmemLimit = 232448 - 1024;
+
+bool plan_for(int64_t k, int64_t H, int64_t I, Plan& p) {
+  // H % 256: the gate_up scale rows (H/16 bytes) are a TMA pitch, a multiple of 16
+  // k <= 8 and parts <= 8: both are cluster extents (portable cluster size)
+  if (k < 1 || k > 8 || H <= 0 || I <= 0 || H % 256 || I % 64 || H > 8192 || I > 4096) return false;
+  p = Plan{};
+  p.H = (int)H; p.I = (int)I; p.k = (int)k;
+  for (int t = 128; t >= 8; t -= 8)
+    if (I % t == 0) { p.T = t; break; }
+  p.tiles = (int)(I / p.T);
+  const int kbt = (int)(H / 64);
+  // K parts: enough CTAs to cover the SMs once, each part a multiple of 4 steps
+  int parts = (int)std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(148 / (k * p.tiles), kbt / 4), 8));
+  for (;; ++parts) {
+    p.Q = rup((kbt + parts - 1) / parts, 4);
+    p.parts = (kbt + p.Q - 1) / p.Q;
+    p.sfa1 = rup(2 * p.T, 32);
+    p.sfb1 = p.sfa1 + rup(4 * p.Q, 32);
+    if (p.sfb1 + 8 * p.Q <= 512) break;
+    if (p.Q <= 4 || parts >= 8) return false;
+  }
+  p.cols1 = (p.sfb1 + 8 * p.Q <= 256) ? 256 : 512;
+  const int kb2 = (int)(I / 64);
+  p.N2 = (H % 256 == 0) ? 256 : 128;
+  auto need2 = [&](int n2) { return n2 + rup(4 * kb2, 32) + 8 * rup(kb2, 4); };
+  if (need2(p.N2) > 512) p.N2 = 128;
+  if (need2(p.N2) > 512) return false;
+  p.sfa2 = p.N2;
+  p.sfb2 = p.sfa2 + rup(4 * kb2, 32);
+  p.cols2 = need2(p.N2) <= 256 ? 256 : 512;
+  return L1(p).bytes + 1024 <= kSmemLimit && L2(p).bytes + 1024 <= kSmemLimit;
 }
 
 struct Ws {
-  uint32_t* counters;
-  uint32_t* parts;
+  uint32_t* hmax;
   __nv_bfloat16* h;
-  __nv_bfloat16* c;
   size_t bytes;
 };
 
-Ws layout(void* base, int64_t k, int64_t H, int64_t I) {
-  char* p = reinterpret_cast<char*>(base);
+Ws layout(void* base, const Plan& p) {
+  char* b = reinterpret_cast<char*>(base);
   auto al = [](size_t v) { return (v + 255) / 256 * 256; };
   Ws w{};
   size_t o = 0;
-  w.counters = reinterpret_cast<uint32_t*>(p + o); o += al((size_t)(H / 128) * 4);
-  w.parts = reinterpret_cast<uint32_t*>(p + o);    o += al((size_t)(k * I / 64) * 4);
-  w.h = reinterpret_cast<__nv_bfloat16*>(p + o);   o += al((size_t)(k * I) * 2);
-  w.c = reinterpret_cast<__nv_bfloat16*>(p + o);   o += al((size_t)(k * H) * 2);
+  w.hmax = reinterpret_cast<uint32_t*>(b + o); o += al((size_t)p.k * p.tiles * 4);
+  w.h = reinterpret_cast<__nv_bfloat16*>(b + o); o += al((size_t)p.k * p.I * 2);
   w.bytes = o;
   return w;
 }
@@ -434,59 +642,67 @@ extern "C" int aeoq_debug_set_decode_trace(void* p) {
 #endif
 
 extern "C" int aeoq_moe_nvfp4_decode_tc_supported(int64_t top_k, int64_t hidden, int64_t inter) {
-  if (top_k < 1 || top_k > 16 || hidden <= 0 || inter <= 0) return 0;
-  if (hidden % 128 != 0 || hidden > 64 * dtc::kMaxKB || inter % 64 != 0 || inter > 64 * dtc::kMaxKB2) return 0;
-  return (dtc::smem1_bytes(hidden) <= 232448 - 1024 && dtc::smem2_bytes(inter) <= 232448 - 1024) ? 1 : 0;
+  dtc::Plan p;
+  return dtc::plan_for(top_k, hidden, inter, p) ? 1 : 0;
 }
 
 extern "C" size_t aeoq_moe_nvfp4_decode_tc_workspace_size(int64_t top_k, int64_t hidden, int64_t inter) {
-  return dtc::layout(nullptr, top_k, hidden, inter).bytes;
+  dtc::Plan p;
+  if (!dtc::plan_for(top_k, hidden, inter, p)) return 0;
+  return dtc::layout(nullptr, p).bytes;
 }
 
 extern "C" int aeoq_moe_nvfp4_decode_tc(const void* hidden, const void* top_k_index, int idx_dtype,
                                         const void* top_k_weights, int64_t top_k, const uint8_t* gate_up,
-                                        const uint8_t* gate_up_atoms, const void* gate_up_ts, int gate_up_ts_dtype,
-                                        const uint8_t* down, const uint8_t* down_atoms, const void* down_ts,
+                                        const uint8_t* gate_up_sf, const void* gate_up_ts, int gate_up_ts_dtype,
+                                        const uint8_t* down, const uint8_t* down_sf, const void* down_ts,
                                         int down_ts_dtype, int64_t num_experts, int64_t hidden_dim, int64_t inter_dim,
                                         void* out, void* workspace, size_t workspace_bytes, int* err_word,
                                         void* stream) {
-  AEOQ_REQUIRE(aeoq_moe_nvfp4_decode_tc_supported(top_k, hidden_dim, inter_dim), AEOQ_ERR_INVALID,
+  dtc::Plan pl;
+  AEOQ_REQUIRE(dtc::plan_for(top_k, hidden_dim, inter_dim, pl), AEOQ_ERR_INVALID,
                "moe_decode_tc: unsupported shape (top_k=%lld hidden=%lld inter=%lld)", (long long)top_k,
                (long long)hidden_dim, (long long)inter_dim);
+  AEOQ_REQUIRE(num_experts > 0, AEOQ_ERR_INVALID, "moe_decode_tc: num_experts must be positive");
   AEOQ_REQUIRE(idx_dtype == AEOQ_I32 || idx_dtype == AEOQ_I64, AEOQ_ERR_INVALID, "moe_decode_tc: int32/int64 ids");
-  AEOQ_REQUIRE(hidden && top_k_index && top_k_weights && gate_up && gate_up_atoms && gate_up_ts && down &&
-                   down_atoms && down_ts && out && err_word,
+  AEOQ_REQUIRE(hidden && top_k_index && top_k_weights && gate_up && gate_up_sf && gate_up_ts && down && down_sf &&
+                   down_ts && out && err_word,
                AEOQ_ERR_INVALID, "moe_decode_tc: null pointer");
   AEOQ_REQUIRE((uintptr_t)hidden % 16 == 0 && (uintptr_t)gate_up % 16 == 0 && (uintptr_t)down % 16 == 0 &&
-                   (uintptr_t)gate_up_atoms % 16 == 0 && (uintptr_t)down_atoms % 16 == 0,
+                   (uintptr_t)gate_up_sf % 16 == 0 && (uintptr_t)down_sf % 16 == 0,
                AEOQ_ERR_INVALID, "moe_decode_tc: operands must be 16-byte aligned");
-  const size_t need = aeoq_moe_nvfp4_decode_tc_workspace_size(top_k, hidden_dim, inter_dim);
+  pl.E = num_experts;
+  const size_t need = dtc::layout(nullptr, pl).bytes;
   AEOQ_REQUIRE(workspace && workspace_bytes >= need && (uintptr_t)workspace % 256 == 0, AEOQ_ERR_WORKSPACE,
-               "moe_decode_tc: workspace of %zu bytes (256-aligned, counters zero) needed, %zu given", need,
-               workspace_bytes);
+               "moe_decode_tc: workspace of %zu bytes (256-aligned) needed, %zu given",
+               need, workspace_bytes);
   const int64_t E = num_experts, H = hidden_dim, I = inter_dim;
   cudaStream_t st = (cudaStream_t)stream;
-  CUtensorMap tg, td;
-  int rc = make_tmap(&tg, gate_up, E * 2 * I, H / 2, H / 2, 64);
+  CUtensorMap tw, ts, td;
+  int rc = make_tmap_bytes(&tw, gate_up, E * 2 * I, H / 2, H / 2, 128, pl.T, true);
   if (rc) return rc;
-  rc = make_tmap(&td, down, E * H, I / 2, I / 2, 128);
+  rc = make_tmap_bytes(&ts, gate_up_sf, E * 2 * I, H / 16, H / 16, 16, pl.T, false);
   if (rc) return rc;
-  dtc::Ws w = dtc::layout(workspace, top_k, H, I);
+  rc = make_tmap_bytes(&td, down, E * H, I / 2, I / 2, 128, pl.N2, true);
+  if (rc) return rc;
+  dtc::Ws w = dtc::layout(workspace, pl);
   dtc::Args a{};
   a.hidden = reinterpret_cast<const __nv_bfloat16*>(hidden);
   a.ids = top_k_index; a.ids_dt = idx_dtype;
   a.topw = reinterpret_cast<const __nv_bfloat16*>(top_k_weights);
-  a.gu_atoms = gate_up_atoms; a.gu_ts = gate_up_ts; a.gu_ts_dt = gate_up_ts_dtype;
-  a.dw_atoms = down_atoms; a.d_ts = down_ts; a.d_ts_dt = down_ts_dtype;
-  a.E = E; a.H = H; a.I = I; a.k = (int)top_k;
-  a.h = w.h; a.parts = w.parts; a.c = w.c; a.counters = w.counters;
+  a.gu_ts = gate_up_ts; a.gu_ts_dt = gate_up_ts_dtype;
+  a.d_sf = down_sf; a.d_ts = down_ts; a.d_ts_dt = down_ts_dtype;
+  a.hmax = w.hmax; a.h = w.h;
   a.out = reinterpret_cast<__nv_bfloat16*>(out);
   a.err = err_word;
-  const size_t s1 = dtc::smem1_bytes(H), s2 = dtc::smem2_bytes(I);
+  const size_t s1 = dtc::L1(pl).bytes + 1024, s2 = dtc::L2(pl).bytes + 1024;
   static size_t set1 = 0, set2 = 0;
   if (set1 < s1) {
+    // the whole carveout as shared memory, so a launch-2 CTA fits beside a launch-1 CTA
     if (cudaFuncSetAttribute(dtc::decode_gateup_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s1) !=
-        cudaSuccess) {
+            cudaSuccess ||
+        cudaFuncSetAttribute(dtc::decode_gateup_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) !=
+            cudaSuccess) {
       cudaGetLastError();
       return set_error(AEOQ_ERR_CUDA, "moe_decode_tc: shared memory attribute (launch 1)");
     }
@@ -494,31 +710,43 @@ extern "C" int aeoq_moe_nvfp4_decode_tc(const void* hidden, const void* top_k_in
   }
   if (set2 < s2) {
     if (cudaFuncSetAttribute(dtc::decode_down_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2) !=
-        cudaSuccess) {
+            cudaSuccess ||
+        cudaFuncSetAttribute(dtc::decode_down_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) !=
+            cudaSuccess) {
       cudaGetLastError();
       return set_error(AEOQ_ERR_CUDA, "moe_decode_tc: shared memory attribute (launch 2)");
     }
     set2 = s2;
   }
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr1[2], attr2[2];
+  attr1[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr1[0].val.programmaticStreamSerializationAllowed = 1;
+  attr1[1].id = cudaLaunchAttributeClusterDimension;   // the K parts of a tile
+  attr1[1].val.clusterDim.x = 1;
+  attr1[1].val.clusterDim.y = (unsigned)pl.parts;
+  attr1[1].val.clusterDim.z = 1;
+  attr2[0] = attr1[0];
+  attr2[1].id = cudaLaunchAttributeClusterDimension;   // the k experts of a row tile
+  attr2[1].val.clusterDim.x = 1;
+  attr2[1].val.clusterDim.y = (unsigned)top_k;
+  attr2[1].val.clusterDim.z = 1;
   cudaLaunchConfig_t c1 = {};
-  c1.gridDim = dim3((unsigned)(I / 64), (unsigned)top_k);
+  c1.gridDim = dim3((unsigned)pl.tiles, (unsigned)pl.parts, (unsigned)top_k);
   c1.blockDim = dim3(dtc::kThreads);
   c1.dynamicSmemBytes = s1;
   c1.stream = st;
-  c1.attrs = attr;
-  c1.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&c1, dtc::decode_gateup_tc_kernel, tg, a);
+  c1.attrs = attr1;
+  c1.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&c1, dtc::decode_gateup_tc_kernel, tw, ts, a, pl);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return set_error(AEOQ_ERR_CUDA, "decode_gateup_tc_kernel: %s", cudaGetErrorString(e));
   }
   cudaLaunchConfig_t c2 = c1;
-  c2.gridDim = dim3((unsigned)(H / 128), (unsigned)top_k);
+  c2.gridDim = dim3((unsigned)(H / pl.N2), (unsigned)top_k);
   c2.dynamicSmemBytes = s2;
-  e = cudaLaunchKernelEx(&c2, dtc::decode_down_tc_kernel, td, a, (int)(top_k * I / 64));
+  c2.attrs = attr2;
+  e = cudaLaunchKernelEx(&c2, dtc::decode_down_tc_kernel, td, a, pl);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return set_error(AEOQ_ERR_CUDA, "decode_down_tc_kernel: %s", cudaGetErrorString(e));

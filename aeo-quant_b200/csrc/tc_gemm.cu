@@ -459,18 +459,26 @@ static EncodeTiledFn encode_fn() {
 }
 
 // 2D uint8 tensor map: rows x row_bytes (row stride ld), box 128 B x box_rows, 128-byte swizzle.
-int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int64_t row_bytes, int64_t ld, int box_rows) {
+// 2D byte tensor map: rows x row_bytes with a row pitch of ld bytes; boxes of
+// box_rows x box_bytes, 128-byte swizzled (operand tiles, box_bytes = 128)
+// or plain (row-major staging of scale rows).
+int make_tmap_bytes(CUtensorMap* m, const void* ptr, int64_t rows, int64_t row_bytes, int64_t ld, int box_bytes,
+                    int box_rows, bool swizzle128) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error(AEOQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)ld};
-  cuuint32_t box[2] = {(cuuint32_t)kKTBytes, (cuuint32_t)box_rows};
+  cuuint32_t box[2] = {(cuuint32_t)box_bytes, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(AEOQ_ERR_INVALID, "tensor map encode failed (%d)", (int)r);
   return AEOQ_OK;
+}
+
+int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int64_t row_bytes, int64_t ld, int box_rows) {
+  return make_tmap_bytes(m, ptr, rows, row_bytes, ld, kKTBytes, box_rows, true);
 }
 
 template <int BN>

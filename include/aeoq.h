@@ -273,19 +273,19 @@ AEOQ_API int aeoq_moe_nvfp4_decode_fused(const void* hidden, const void* top_k_i
 /* ------------------------------------------------------------------------
  * One-token NVFP4 MoE expert forward on the tensor cores (two launches,
  * the second programmatically dependent on the first). Same math and
- * rounding points as aeoq_moe_nvfp4_decode (modeling_nvfp4.py:132-186); the
- * weight scales come as atoms (aeoq_nvfp4_sf_to_atoms): gate_up with
- * geglu_inter = I, down plain. Workspace: *_tc_workspace_size() bytes,
- * 256-aligned, first 256 bytes zero before the first call (each call leaves
- * them zero; calls that overlap on the device must not share it).
- * hidden % 128 == 0 (<= 4096), inter % 64 == 0 (<= 2048), top_k <= 16.
+ * rounding points as aeoq_moe_nvfp4_decode (modeling_nvfp4.py:132-186) and
+ * the same arguments (weight scales in the reference's [E][rows][K/16]
+ * layout) plus an error word: a bounded wait that times out records a
+ * nonzero code there. Workspace: *_tc_workspace_size() bytes, 256-aligned,
+ * no initialization (calls that overlap on the device must not share it).
+ * hidden % 256 == 0, inter % 64 == 0, top_k <= 8 (see *_supported).
  * ------------------------------------------------------------------------ */
 AEOQ_API int aeoq_moe_nvfp4_decode_tc_supported(int64_t top_k, int64_t hidden, int64_t inter);
 AEOQ_API size_t aeoq_moe_nvfp4_decode_tc_workspace_size(int64_t top_k, int64_t hidden, int64_t inter);
 AEOQ_API int aeoq_moe_nvfp4_decode_tc(const void* hidden, const void* top_k_index, int idx_dtype,
                                       const void* top_k_weights, int64_t top_k, const uint8_t* gate_up,
-                                      const uint8_t* gate_up_atoms, const void* gate_up_ts, int gate_up_ts_dtype,
-                                      const uint8_t* down, const uint8_t* down_atoms, const void* down_ts,
+                                      const uint8_t* gate_up_sf, const void* gate_up_ts, int gate_up_ts_dtype,
+                                      const uint8_t* down, const uint8_t* down_sf, const void* down_ts,
                                       int down_ts_dtype, int64_t num_experts, int64_t hidden_dim, int64_t inter_dim,
                                       void* out, void* workspace, size_t workspace_bytes, int* err_word,
                                       void* stream);
