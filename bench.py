@@ -41,10 +41,10 @@ DOWN_BYTES = 2816 * 352 + 2816 * 44
 METRIC = "MoE decode tok/s (M=1 gather) + NVFP4 prefill TFLOPS, % of roofline"
 FALLBACK_HBM_GBS = 6650.0
 
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of the fused decode
-# kernel at this workload, from the ncu capture summarised in
-# profiles/moe_decode_fused_b1.md (None until captured).
-NCU_TRAFFIC_FUSED = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one tensor-core decode
+# (both launches) at this workload, from the ncu capture summarised in
+# profiles/moe_decode_tc_b1.md (None until captured).
+NCU_TRAFFIC_TC = 26983424
 
 
 def parse():
@@ -233,6 +233,7 @@ def main():
     import torch
     import torch.distributed as dist
     from aeo_quant_b200 import _capi as A
+    from aeo_quant_b200.bridges.gemma4 import moe_ops
 
     if world > 1:
         dist.init_process_group("nccl")
@@ -296,11 +297,16 @@ def main():
     uws_n = lib.aeoq_moe_nvfp4_decode_workspace_size(TOPK, H, I)
     uws = torch.empty(uws_n, dtype=torch.uint8, device=dev)
 
+    tws_n = lib.aeoq_moe_nvfp4_decode_tc_workspace_size(TOPK, H, I)
+    tws = torch.zeros(max(tws_n, 1), dtype=torch.uint8, device=dev)
+    err = A.err_word(dev)
+
     def launch(fn, s, ws, ws_n):
         gp, gs, gt, dp, ds, dt = layers[s % L]
+        extra = (err.data_ptr(),) if fn is lib.aeoq_moe_nvfp4_decode_tc else ()
         return fn(hid_d[s].data_ptr(), idx_d[s].data_ptr(), A.I64, wts_d[s].data_ptr(), TOPK,
                   gp.data_ptr(), gs.data_ptr(), gt.data_ptr(), A.F32, dp.data_ptr(), ds.data_ptr(),
-                  dt.data_ptr(), A.F32, E, H, I, out.data_ptr(), ws.data_ptr(), ws_n,
+                  dt.data_ptr(), A.F32, E, H, I, out.data_ptr(), ws.data_ptr(), ws_n, *extra,
                   torch.cuda.current_stream(dev).cuda_stream)
 
     def time_graph(fn, ws, ws_n):
@@ -325,7 +331,11 @@ def main():
         return a0.elapsed_time(a1) / K
 
     stage_ms = {}
+    tc_path = B == 1 and moe_ops.DECODE_PATH in ("auto", "tc") and bool(
+        lib.aeoq_moe_nvfp4_decode_tc_supported(TOPK, H, I))
     if B == 1:
+        if tc_path:
+            stage_ms["tc"] = time_graph(lib.aeoq_moe_nvfp4_decode_tc, tws, tws_n)
         stage_ms["fused"] = time_graph(lib.aeoq_moe_nvfp4_decode_fused, fws, fws_n)
         stage_ms["unfused"] = time_graph(lib.aeoq_moe_nvfp4_decode, uws, uws_n)
 
@@ -365,15 +375,22 @@ def main():
     if rank == 0:
         hbm, peak_src = peaks()
         roof = None
-        if "fused" in stage_ms:
-            alg = TOPK * EXPERT_BYTES + 2 * H * 2 + TOPK * I * 2 * 2
-            ach = alg / (stage_ms["fused"] / 1000.0) / 1e9
-            roof = {"bound": "hbm", "kernel": "moe_decode_fused_kernel", "achieved": round(ach, 1),
-                    "peak": hbm, "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
+        key = "tc" if "tc" in stage_ms else "fused" if "fused" in stage_ms else None
+        if key:
+            # algorithmic bytes: the k experts' packed weights and scales, the
+            # hidden vector in and the output out (intermediates stay on chip
+            # or in L2 and are not counted)
+            alg = TOPK * EXPERT_BYTES + 2 * H * 2
+            ach = alg / (stage_ms[key] / 1000.0) / 1e9
+            roof = {"bound": "hbm",
+                    "kernel": ("decode_gateup_tc_kernel + decode_down_tc_kernel (one programmatically "
+                               "dependent pair)") if key == "tc" else "moe_decode_fused_kernel",
+                    "achieved": round(ach, 1), "peak": hbm,
+                    "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
                     else "of fallback", "unit": "GB/s", "frac": round(ach / hbm, 4),
-                    "traffic": NCU_TRAFFIC_FUSED, "algorithmic_bytes": alg,
-                    "launch_us": round(stage_ms["fused"] * 1000, 3),
-                    "three_launch_path_us": round(stage_ms["unfused"] * 1000, 3)}
+                    "traffic": NCU_TRAFFIC_TC if key == "tc" else None, "algorithmic_bytes": alg,
+                    "launch_us": round(stage_ms[key] * 1000, 3),
+                    "other_paths_us": {k2: round(v * 1000, 3) for k2, v in stage_ms.items() if k2 != key}}
         step_bytes = TOPK * EXPERT_BYTES + 2 * H * 2
         res = {
             "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": K,
@@ -386,7 +403,7 @@ def main():
                        f"{L * 428} MB resident, 26.8 MB streamed per step",
                        "parallelism": f"replicas x{world}", "timing": "one CUDA graph of K steps, CUDA events"},
             "step_hbm_gbs": round(step_bytes / (ms_max / K / 1000.0) / 1e9, 1),
-            "gpu_launches": K,
+            "gpu_launches": (2 if tc_path else 1) * K,
             "clocks": clk.summary(),
             "e2e": {"value": round(e2e_val, 1), "unit": "tok/s", "steps": n_e2e,
                     "h2d_bytes_per_step": B * H * 2 + B * TOPK * 8 + B * TOPK * 2,
