@@ -49,6 +49,9 @@ _SIGS["aeoq_moe_route"] = [_P, _I, _P, _L, _L, _L, _I, _P, _P, _P, _P, _P, _P, _
 _SIGS["aeoq_gather_rows"] = [_P, _P, _P, _P, _P, _P, _I, _P, _L, _L, _L, _P, _P, _P]
 _SIGS["aeoq_requant_rows"] = [_P, _L, _P, _P, _P, _I, _P, _L, _P, _L, _I, _P, _P, _P, _P]
 _SIGS["aeoq_selftest_div_rn"] = [_I, _P, _P, _P]
+_SIGS["aeoq_fp8_gemm"] = [_P, _P, _L, _P, _P, _L, _L, _P, _P, _P]
+_SIGS["aeoq_fp8_gemm_grouped"] = [_P, _P, _L, _P, _P, _I, _P, _P, _L, _L, _L, _I, _P, _P, _L, _P, _P]
+_SIGS["aeoq_fp8_quantize_rows_gather"] = [_P, _L, _P, _P, _L, _L, _P, _L, _P, _P]
 _SIGS["aeoq_moe_nvfp4_decode_tc_supported"] = [_L, _L, _L]
 _SIGS["aeoq_moe_nvfp4_decode_tc_workspace_size"] = [_L, _L, _L]
 _SIGS["aeoq_moe_nvfp4_decode_tc"] = [_P, _P, _I, _P, _L, _P, _P, _P, _I, _P, _P, _P, _I, _L, _L, _L, _P, _P, _Z, _P, _P]

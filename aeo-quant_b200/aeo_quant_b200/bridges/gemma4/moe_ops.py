@@ -189,3 +189,88 @@ def nvfp4_prefill(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_s
         raise ValueError(f"gate_up_proj holds {gu.shape[0]} experts, config says {num_experts}")
     return nvfp4_experts_grouped(hidden.contiguous(), top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf,
                                  dw_ts)
+
+
+# ---------------------------------------------------------------- FP8 experts
+def fp8_scale_rows(scale: torch.Tensor, E: int, N: int) -> torch.Tensor:
+    """Per-output-channel weight scales as a flat f32 (E * N) tensor: accepts
+    the checkpoint's (E, N, 1) bf16 buffer or the preconverted (E, 1, N) f32
+    one (loader.py:47-64); the values are the same."""
+    if scale.numel() != E * N:
+        raise ValueError(f"expected {E * N} weight scales, got shape {tuple(scale.shape)}")
+    return scale.reshape(E * N).to(torch.float32).contiguous()
+
+
+def fp8_linear(x_bf16: torch.Tensor, w_fp8: torch.Tensor, scale_w: torch.Tensor) -> torch.Tensor:
+    """``_fp8_linear`` (modeling.py:89-108): per-row dynamic e4m3 input
+    quantization, then bf16((acc * sa[m]) * sb[n]) on the tensor cores."""
+    A.require_cuda(x_bf16, w_fp8, scale_w)
+    lib = A.load()
+    if x_bf16.dtype != torch.bfloat16:
+        raise ValueError(f"_fp8_linear expects bfloat16 input, got {x_bf16.dtype}")
+    if w_fp8.dim() != 2:
+        raise ValueError(f"w_fp8 must be 2D (N, K), got shape {tuple(w_fp8.shape)}")
+    N, K = w_fp8.shape
+    x2 = x_bf16.reshape(-1, x_bf16.shape[-1]).contiguous()
+    M = x2.shape[0]
+    if x2.shape[1] != K:
+        raise ValueError(f"input features {x2.shape[1]} != weight in_features {K}")
+    dev = x2.device
+    st = A.stream_ptr(dev)
+    sb = scale_w.reshape(N).to(torch.float32).contiguous()
+    q = torch.empty(M, K, dtype=torch.uint8, device=dev)
+    sa = torch.empty(M, dtype=torch.float32, device=dev)
+    A.check(lib.aeoq_fp8_quantize_rows_gather(x2.data_ptr(), K, None, None, M, K, q.data_ptr(), K, sa.data_ptr(), st))
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    wv = w_fp8.contiguous().view(torch.uint8)
+    A.check(lib.aeoq_fp8_gemm(q.data_ptr(), sa.data_ptr(), M, wv.data_ptr(), sb.data_ptr(), N, K, out.data_ptr(),
+                              A.err_word(dev).data_ptr(), st))
+    return out.reshape(*x_bf16.shape[:-1], N)
+
+
+def fp8_experts_grouped(hidden, top_k_index, top_k_weights, gu, gu_sb, dw, dw_sb):
+    """``Gemma4TextExpertsFP8.forward`` (modeling.py:110-146) on the device,
+    no host sync: route by expert, per-row e4m3 quantization of the gathered
+    tokens, grouped gate_up GEMM with the GeGLU epilogue, per-row
+    re-quantization, grouped down GEMM weighted by the routing weights, and
+    the bf16 ``index_add_`` fold in ascending expert order.
+
+    ``gu`` (E, 2I, H) and ``dw`` (E, H, I) e4m3 (any 1-byte view);
+    ``gu_sb`` / ``dw_sb`` flat f32 (E * 2I) / (E * H)."""
+    A.require_cuda(hidden, top_k_index, top_k_weights, gu, dw)
+    lib = A.load()
+    dev = hidden.device
+    E, two_i, H = gu.shape
+    I = two_i // 2
+    T = hidden.shape[0]
+    k = top_k_index.shape[-1]
+    P = T * k
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    if T == 0:
+        return out
+    st = A.stream_ptr(dev)
+    err = A.err_word(dev)
+    tile_n = pick_tile_n(P, E)
+    r = _Route(lib, top_k_index.reshape(T, k), top_k_weights.reshape(T, k), E, tile_n)
+    hidden = hidden.contiguous()
+    gu8 = gu.detach().contiguous().view(torch.uint8)
+    dw8 = dw.detach().contiguous().view(torch.uint8)
+    xq = torch.empty(P, H, dtype=torch.uint8, device=dev)
+    sa = torch.empty(P, dtype=torch.float32, device=dev)
+    A.check(lib.aeoq_fp8_quantize_rows_gather(hidden.data_ptr(), H, r.row_tok.data_ptr(), r.n_rows_ptr, P, H,
+                                              xq.data_ptr(), H, sa.data_ptr(), st))           # (:101-104)
+    h = torch.empty(P, I, dtype=torch.bfloat16, device=dev)
+    A.check(lib.aeoq_fp8_gemm_grouped(xq.data_ptr(), sa.data_ptr(), P, r.grp_off.data_ptr(), r.tile_off.data_ptr(),
+                                      tile_n, gu8.data_ptr(), gu_sb.data_ptr(), E, 2 * I, H, 1, None, h.data_ptr(),
+                                      I * 2, err.data_ptr(), st))                           # (:124-131)
+    hq = torch.empty(P, I, dtype=torch.uint8, device=dev)
+    sh = torch.empty(P, dtype=torch.float32, device=dev)
+    A.check(lib.aeoq_fp8_quantize_rows_gather(h.data_ptr(), I, None, r.n_rows_ptr, P, I, hq.data_ptr(), I,
+                                              sh.data_ptr(), st))
+    c = torch.empty(P, H, dtype=torch.bfloat16, device=dev)
+    A.check(lib.aeoq_fp8_gemm_grouped(hq.data_ptr(), sh.data_ptr(), P, r.grp_off.data_ptr(), r.tile_off.data_ptr(),
+                                      tile_n, dw8.data_ptr(), dw_sb.data_ptr(), E, H, I, 2, r.row_w.data_ptr(),
+                                      c.data_ptr(), H * 2, err.data_ptr(), st))              # (:133-140)
+    A.check(lib.aeoq_moe_combine(c.data_ptr(), r.pair_row.data_ptr(), r.ids.data_ptr(), A.dtype_code(r.ids.dtype),
+                                 T, k, H, 0, out.data_ptr(), st))                          # (:142-145)
+    return out

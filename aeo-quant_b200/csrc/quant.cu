@@ -296,6 +296,65 @@ extern "C" int aeoq_fp8_quantize_rows(const void* x, int dtype, int64_t rows, in
 }
 
 // ---------------------------------------------------------------------------
+// FP8 per-row activation quantizer over gathered rows: output row r is input
+// row idx[r] (identity without idx), r < *n_rows (or max_rows). bf16 input,
+// K % 8 == 0; one warp per row, 16-byte loads. Semantics of _fp8_linear's
+// input quantization (modeling.py:101-104), as AEOQ_FP8_ACTIVATION above.
+// ---------------------------------------------------------------------------
+namespace aeoq {
+
+__global__ void __launch_bounds__(256) fp8_rows_gather_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld,
+                                                              const int* __restrict__ idx,
+                                                              const int* __restrict__ n_rows, int64_t max_rows,
+                                                              int64_t K, uint8_t* __restrict__ q, int64_t q_ld,
+                                                              float* __restrict__ scale_out) {
+  const int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int64_t nr = n_rows ? (int64_t)*n_rows : max_rows;
+  if (r >= nr || r >= max_rows) return;
+  const int64_t src = idx ? (int64_t)idx[r] : r;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + src * ld);
+  uint32_t key = 0;
+  for (int64_t i = lane; i < K / 8; i += 32) {
+    const uint4 u = xr[i];
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) key = max(key, In<AEOQ_BF16>::abs_key(e[j]));
+  }
+  key = warp_umax(key);
+  const float a = nan_max(K ? In<AEOQ_BF16>::key_to_f(key) : 0.0f, In<AEOQ_BF16>::round(1e-4f));
+  const float s = div_rn(a, kFp8Max);
+  if (lane == 0) scale_out[r] = s;
+  uint2* qr = reinterpret_cast<uint2*>(q + r * q_ld);
+  for (int64_t i = lane; i < K / 8; i += 32) {
+    const uint4 u = xr[i];
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w[j >> 2] |= e4m3_encode(div_rn(__bfloat162float(e[j]), s)) << (8 * (j & 3));
+    qr[i] = make_uint2(w[0], w[1]);
+  }
+}
+
+}  // namespace aeoq
+
+extern "C" int aeoq_fp8_quantize_rows_gather(const void* x, int64_t ld, const int* row_idx, const int* n_rows,
+                                             int64_t max_rows, int64_t K, uint8_t* q, int64_t q_ld,
+                                             float* scale_out, void* stream) {
+  AEOQ_REQUIRE(max_rows >= 0 && K >= 0 && ld >= K && q_ld >= K, AEOQ_ERR_INVALID,
+               "fp8_quantize_rows_gather: bad shape");
+  AEOQ_REQUIRE(K % 8 == 0 && ld % 8 == 0 && q_ld % 8 == 0, AEOQ_ERR_INVALID,
+               "fp8_quantize_rows_gather: K and strides must be multiples of 8");
+  if (max_rows == 0 || K == 0) return AEOQ_OK;
+  AEOQ_REQUIRE(x && q && scale_out, AEOQ_ERR_INVALID, "fp8_quantize_rows_gather: null pointer");
+  AEOQ_REQUIRE((uintptr_t)x % 16 == 0 && (uintptr_t)q % 8 == 0, AEOQ_ERR_INVALID,
+               "fp8_quantize_rows_gather: x 16-byte and q 8-byte alignment required");
+  fp8_rows_gather_kernel<<<(unsigned)((max_rows + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+      (const __nv_bfloat16*)x, ld, row_idx, n_rows, max_rows, K, q, q_ld, scale_out);
+  return check_launch("fp8_rows_gather_kernel");
+}
+
+// ---------------------------------------------------------------------------
 // NVFP4 dequantizer (quant.py:188-212): bf16(value * block_scale * ts),
 // evaluated left to right in float32. One thread per 16-element block.
 // ---------------------------------------------------------------------------

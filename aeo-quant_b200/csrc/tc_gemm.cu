@@ -28,6 +28,12 @@
 // derived once per weight tensor (aeoq_nvfp4_sf_to_atoms); activations'
 // atoms are written by the kernels that produce them, tile by tile.
 //
+// FP8 instance (kF8 = true): A and B are e4m3 codes (one per byte, K = 128
+// values per 128-byte stage row, four tcgen05.mma kind::f8f6f4 of K = 32),
+// no scale atoms; the epilogue applies the rowwise scales of the reference's
+// torch._scaled_mm call (bridges/gemma4/modeling.py:101-108):
+// y = (acc * sa[token]) * sb[weight row], f32.
+//
 // No TMA multicast anywhere: every CTA loads its own tiles.
 #include <cuda.h>
 
@@ -76,6 +82,8 @@ struct TcParams {
   int64_t ldc;                            // bytes per output row
   int64_t c_slot_stride;                  // bytes between slots (mode 0)
   uint32_t* grp_amax;                     // kEpiGeglu: per-expert |h| max key (atomicMax)
+  const float* sa_rows;                   // FP8: per activation (B) row scale, f32
+  const float* sb_rows;                   // FP8: per weight row scale, f32 [num_experts * n_out]
   int* err;                               // device error word (bounded waits)
   uint64_t* trace;                        // development builds only: per-CTA phase stamps
   int dbg;                                // development builds only: experiment switches
@@ -101,15 +109,16 @@ struct TcSmem {
   uint64_t empty[kTcMaxStages];
   uint64_t accum;
   uint32_t tmem_base;
+  float colscale[256];   // FP8: the tile's activation row scales
 };
 
-template <int BN>
+template <int BN, bool kF8 = false>
 struct TcLayout {
   static constexpr int kSfbAtoms = (BN + 127) / 128;
   static constexpr size_t kA = 128 * kKTBytes;             // 16 KB
   static constexpr size_t kB = (size_t)BN * kKTBytes;
-  static constexpr size_t kSfa = 4 * 512;
-  static constexpr size_t kSfb = (size_t)4 * 512 * kSfbAtoms;
+  static constexpr size_t kSfa = kF8 ? 0 : 4 * 512;
+  static constexpr size_t kSfb = kF8 ? 0 : (size_t)4 * 512 * kSfbAtoms;
   static constexpr size_t kStage = kA + kB + kSfa + kSfb;
   // as many stages as the shared-memory budget holds (at most 8)
   static constexpr int kStages =
@@ -120,8 +129,9 @@ struct TcLayout {
   static constexpr size_t kXchg = 64 * (size_t)BN * 4;
   static constexpr size_t kOut = (size_t)BN * 128 * 4;
   static_assert(kXchg + kOut <= kStages * kStage, "epilogue buffers must fit in the stage ring");
-  static constexpr size_t kBytes = 1024 + kStages * kStage + 256;
-  static constexpr uint32_t kTmemCols = (BN + 32 * kSfbAtoms + 16 <= 256) ? 256 : 512;
+  static constexpr size_t kBytes = 1024 + kStages * kStage + sizeof(TcSmem) + 64;
+  static constexpr uint32_t kTmemCols =
+      kF8 ? (BN <= 32 ? 32u : (uint32_t)BN) : ((BN + 32 * kSfbAtoms + 16 <= 256) ? 256u : 512u);
   static constexpr uint32_t kSfaCol = BN;                  // 16 columns
   static constexpr uint32_t kSfbCol = BN + 16;             // 16 * kSfbAtoms columns
 };
@@ -190,11 +200,12 @@ __device__ __forceinline__ void tmem_cols(uint32_t taddr, float (&v)[32]) {
   }
 }
 
-template <int BN>
+template <int BN, bool kF8>
 __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                                                                       const __grid_constant__ CUtensorMap tmB,
                                                                       const TcParams p) {
-  using L = TcLayout<BN>;
+  using L = TcLayout<BN, kF8>;
+  constexpr int kStepK = kF8 ? 32 : 64;      // K values per MMA (32 bytes of a row)
   extern __shared__ __align__(1024) uint8_t dsmem[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~uintptr_t(1023));
   uint8_t* stage0 = base;
@@ -210,8 +221,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
   // A rows of this tile: 128 consecutive weight rows, or for GeGLU 64 gate
   // rows (n0..n0+63) and the matching 64 up rows (n0 + n_out/2 ...).
   const int64_t a_row_base = ti.expert * p.n_out;
-  const int num_kt = (int)((p.K + kKT - 1) / kKT);
-  const int kb_total = (int)(p.K / 64);
+  const int num_kt = (int)((p.K + 4 * kStepK - 1) / (4 * kStepK));
+  const int kb_total = (int)(p.K / kStepK);
 
   auto stA = [&](int s) { return stage0 + s * L::kStage; };
   auto stB = [&](int s) { return stage0 + s * L::kStage + L::kA; };
@@ -256,12 +267,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
         { uint64_t w1_; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(w1_)); pwait_ += w1_ - w0_; }
 #endif
         const int nkb = min(4, kb_total - kt * 4);
-        const uint32_t sfa_bytes = (uint32_t)nkb * 512, sfb_bytes = (uint32_t)nkb * L::kSfbAtoms * 512;
+        const uint32_t sfa_bytes = kF8 ? 0u : (uint32_t)nkb * 512;
+        const uint32_t sfb_bytes = kF8 ? 0u : (uint32_t)nkb * L::kSfbAtoms * 512;
         const int32_t x = kt * kKTBytes;
         if (!leader) continue;
         sm100::mbar_arrive_expect_tx(&sh->full[s], (uint32_t)(L::kA + L::kB) + sfa_bytes + sfb_bytes);
-        bulk_g2s(stSFA(s), sfa_base + (size_t)kt * 4 * 512, sfa_bytes, &sh->full[s]);
-        bulk_g2s(stSFB(s), sfb_base + (size_t)kt * 4 * L::kSfbAtoms * 512, sfb_bytes, &sh->full[s]);
+        if constexpr (!kF8) {
+          bulk_g2s(stSFA(s), sfa_base + (size_t)kt * 4 * 512, sfa_bytes, &sh->full[s]);
+          bulk_g2s(stSFB(s), sfb_base + (size_t)kt * 4 * L::kSfbAtoms * 512, sfb_bytes, &sh->full[s]);
+        }
         if (geglu) {
           const int64_t n0 = m_tile * 64;
           sm100::tma_load_2d(stA(s), &tmA, x, (int32_t)(a_row_base + n0), &sh->full[s]);
@@ -283,7 +297,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
 #ifdef AEOQ_TC_TRACE
       uint64_t mwait_ = 0, mcp_ = 0, mmma_ = 0;
 #endif
-      const uint32_t idesc = sm100::idesc_nvf4(BN);
+      const uint32_t idesc = kF8 ? sm100::idesc_f8(BN) : sm100::idesc_nvf4(BN);
       for (int kt = 0; kt < num_kt; ++kt) {
         const int s = kt % L::kStages;
         const uint32_t ph = (kt / L::kStages) & 1;
@@ -300,7 +314,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
 #ifdef AEOQ_TC_TRACE
         if (!((p.dbg & 1) && kt > 0))
 #endif
-        if (leader)
+        if (!kF8 && leader)
         for (int kb = 0; kb < nkb; ++kb) {
           sm100::tc_cp_32x128b_warpx4(tmem + L::kSfaCol + 4 * kb, sm100::sdesc_sf_atom(sm100::smem_u32(stSFA(s) + kb * 512)));
 #pragma unroll
@@ -317,8 +331,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
         for (int kb = 0; kb < nkb; ++kb) {
           const uint64_t ad = sm100::sdesc_k_sw128(sm100::smem_u32(stA(s)) + kb * 32);
           const uint64_t bd = sm100::sdesc_k_sw128(sm100::smem_u32(stB(s)) + kb * 32);
-          sm100::tc_mma_nvf4(tmem, ad, bd, idesc, tmem + L::kSfaCol + 4 * kb,
-                             tmem + L::kSfbCol + 4 * kb * L::kSfbAtoms, (kt | kb) ? 1u : 0u);
+          if constexpr (kF8)
+            sm100::tc_mma_f8(tmem, ad, bd, idesc, (kt | kb) ? 1u : 0u);
+          else
+            sm100::tc_mma_nvf4(tmem, ad, bd, idesc, tmem + L::kSfaCol + 4 * kb,
+                               tmem + L::kSfbCol + 4 * kb * L::kSfbAtoms, (kt | kb) ? 1u : 0u);
         }
 #ifdef AEOQ_TC_TRACE
         mmma_ += clock64() - w2_;
@@ -336,9 +353,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;            // TMEM lane quadrant this warp may access
     const int row = 32 * q + lane;     // accumulator row = weight row in the tile
-    float alpha;                       // read while the main loop runs
-    if (p.epi == kEpiScaleRow) alpha = p.grp_alpha_ts[ti.expert] * load_scalar_f(p.w_ts, p.w_ts_dt);
-    else alpha = load_scalar_f(p.a_ts, p.a_ts_dt) * load_scalar_f(p.w_ts, p.w_ts_dt);
+    // Scales, read while the main loop runs. NVFP4: one alpha per tile.
+    // FP8: this row's weight scale (GeGLU tiles: gate rows n0.., up rows
+    // n_out/2 + n0..) and the tile's activation row scales in shared memory.
+    float alpha = 1.0f;
+    float* colscale = sh->colscale;
+    if constexpr (kF8) {
+      const int64_t wrow = geglu ? (row < 64 ? m_tile * 64 + row : p.n_out / 2 + m_tile * 64 + (row - 64))
+                                 : m_tile * 128 + row;
+      alpha = p.sb_rows[ti.expert * p.n_out + wrow];
+      for (int t = tid - 64; t < BN; t += 128) colscale[t] = t < ti.n_valid ? p.sa_rows[ti.b_row0 + t] : 0.0f;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+    } else {
+      if (p.epi == kEpiScaleRow) alpha = p.grp_alpha_ts[ti.expert] * load_scalar_f(p.w_ts, p.w_ts_dt);
+      else alpha = load_scalar_f(p.a_ts, p.a_ts_dt) * load_scalar_f(p.w_ts, p.w_ts_dt);
+    }
+    // accumulator -> f32 value of output (row, token t)
+    auto scaled = [&](float acc, int t) { return kF8 ? (acc * colscale[t]) * alpha : acc * alpha; };
     const bool ok = sm100::mbar_wait(&sh->accum, 0, p.err, 14);
     if (tid == 64) TC_TRACE(6);
     sm100::tc_fence_after();
@@ -367,7 +398,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
         for (int j = 0; j < kChunk; ++j) {
           const int t = c0 + j;
           if (t < BN) {
-            float y = v[j] * alpha;
+            float y = scaled(v[j], t);
             if (p.epi == kEpiScaleRow)
               y = (t < ti.n_valid) ? bf16r(y) * __bfloat162float(p.row_w[ti.c_row0 + t]) : 0.f;
             if (es == 4) reinterpret_cast<float*>(outs)[t * ncol + row] = y;
@@ -383,7 +414,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
         if (row >= 64) {
 #pragma unroll
           for (int j = 0; j < kChunk; ++j)
-            if (c0 + j < BN) xchg[(row - 64) * BN + c0 + j] = bf16r(v[j] * alpha);
+            if (c0 + j < BN) xchg[(row - 64) * BN + c0 + j] = bf16r(scaled(v[j], c0 + j));
         }
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -395,7 +426,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
           for (int j = 0; j < kChunk; ++j) {
             const int t = c0 + j;
             if (t < BN) {
-              const float g = bf16r(v[j] * alpha);
+              const float g = bf16r(scaled(v[j], t));
               const float u = xchg[row * BN + t];
               const __nv_bfloat16 hv = __float2bfloat16_rn(bf16r(gelu_tanh(g)) * u);
               reinterpret_cast<__nv_bfloat16*>(outs)[t * ncol + row] = hv;
@@ -481,19 +512,20 @@ int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int64_t row_bytes, 
   return make_tmap_bytes(m, ptr, rows, row_bytes, ld, kKTBytes, box_rows, true);
 }
 
-template <int BN>
+template <int BN, bool kF8>
 static int launch_tc(const uint8_t* a, int64_t a_rows, const uint8_t* b, const TcParams& p, dim3 grid,
                      cudaStream_t st) {
-  using L = TcLayout<BN>;
+  using L = TcLayout<BN, kF8>;
   CUtensorMap ta, tb;
-  int rc = make_tmap(&ta, a, a_rows, p.K / 2, p.K / 2, p.epi == kEpiGeglu ? 64 : 128);
+  const int64_t row_bytes = kF8 ? p.K : p.K / 2;
+  int rc = make_tmap(&ta, a, a_rows, row_bytes, row_bytes, p.epi == kEpiGeglu ? 64 : 128);
   if (rc) return rc;
-  rc = make_tmap(&tb, b, p.b_rows, p.K / 2, p.K / 2, BN);
+  rc = make_tmap(&tb, b, p.b_rows, row_bytes, row_bytes, BN);
   if (rc) return rc;
-  static size_t set_bytes[6] = {0, 0, 0, 0, 0, 0};
-  const int slot = BN == 8 ? 4 : BN == 16 ? 5 : BN == 32 ? 0 : BN == 64 ? 1 : BN == 128 ? 2 : 3;
+  static size_t set_bytes[12] = {};
+  const int slot = (BN == 8 ? 4 : BN == 16 ? 5 : BN == 32 ? 0 : BN == 64 ? 1 : BN == 128 ? 2 : 3) + (kF8 ? 6 : 0);
   if (set_bytes[slot] < L::kBytes) {
-    cudaError_t e = cudaFuncSetAttribute(nvfp4_tc_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(nvfp4_tc_gemm_kernel<BN, kF8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)L::kBytes);
     if (e != cudaSuccess) {
       cudaGetLastError();
@@ -505,24 +537,30 @@ static int launch_tc(const uint8_t* a, int64_t a_rows, const uint8_t* b, const T
   TcParams pt = p;
   if (const char* tp = getenv("AEOQ_TC_TRACE_PTR")) pt.trace = reinterpret_cast<uint64_t*>(strtoull(tp, nullptr, 10));
   if (const char* dp = getenv("AEOQ_TC_DBG")) pt.dbg = atoi(dp);
-  nvfp4_tc_gemm_kernel<BN><<<grid, kTcThreads, L::kBytes, st>>>(ta, tb, pt);
+  nvfp4_tc_gemm_kernel<BN, kF8><<<grid, kTcThreads, L::kBytes, st>>>(ta, tb, pt);
 #else
-  nvfp4_tc_gemm_kernel<BN><<<grid, kTcThreads, L::kBytes, st>>>(ta, tb, p);
+  nvfp4_tc_gemm_kernel<BN, kF8><<<grid, kTcThreads, L::kBytes, st>>>(ta, tb, p);
 #endif
-  return check_launch("nvfp4_tc_gemm_kernel");
+  return check_launch(kF8 ? "fp8_tc_gemm_kernel" : "nvfp4_tc_gemm_kernel");
+}
+
+template <bool kF8>
+int tc_gemm_dispatch_kind(int bn, const uint8_t* a, int64_t a_rows, const uint8_t* b, const TcParams& p, dim3 grid,
+                          cudaStream_t st) {
+  switch (bn) {
+    case 8: return launch_tc<8, kF8>(a, a_rows, b, p, grid, st);
+    case 16: return launch_tc<16, kF8>(a, a_rows, b, p, grid, st);
+    case 32: return launch_tc<32, kF8>(a, a_rows, b, p, grid, st);
+    case 64: return launch_tc<64, kF8>(a, a_rows, b, p, grid, st);
+    case 128: return launch_tc<128, kF8>(a, a_rows, b, p, grid, st);
+    case 256: return launch_tc<256, kF8>(a, a_rows, b, p, grid, st);
+  }
+  return set_error(AEOQ_ERR_INVALID, "tc_gemm: unsupported tile N %d", bn);
 }
 
 int tc_gemm_dispatch(int bn, const uint8_t* a, int64_t a_rows, const uint8_t* b, const TcParams& p, dim3 grid,
                      cudaStream_t st) {
-  switch (bn) {
-    case 8: return launch_tc<8>(a, a_rows, b, p, grid, st);
-    case 16: return launch_tc<16>(a, a_rows, b, p, grid, st);
-    case 32: return launch_tc<32>(a, a_rows, b, p, grid, st);
-    case 64: return launch_tc<64>(a, a_rows, b, p, grid, st);
-    case 128: return launch_tc<128>(a, a_rows, b, p, grid, st);
-    case 256: return launch_tc<256>(a, a_rows, b, p, grid, st);
-  }
-  return set_error(AEOQ_ERR_INVALID, "tc_gemm: unsupported tile N %d", bn);
+  return tc_gemm_dispatch_kind<false>(bn, a, a_rows, b, p, grid, st);
 }
 
 int pick_bn(int64_t M) {
@@ -641,4 +679,78 @@ extern "C" int aeoq_nvfp4_gemm_grouped(const uint8_t* b, const uint8_t* b_sf, in
   const unsigned gx = (unsigned)(epi == kEpiGeglu ? (N / 2) / 64 : N / 128);
   dim3 grid(gx, (unsigned)max_tiles, 1);
   return tc_gemm_dispatch(tile_n, w, num_experts * N, b, p, grid, (cudaStream_t)stream);
+}
+
+// ---------------------------------------------------------------- FP8
+// torch._scaled_mm(x_fp8, w_fp8.t(), scale_a, scale_b, out_dtype=bf16) of
+// _fp8_linear (modeling.py:105-108): C[m][n] = bf16((acc * sa[m]) * sb[n]).
+extern "C" int aeoq_fp8_gemm(const uint8_t* a, const float* sa, int64_t M, const uint8_t* w, const float* sb,
+                             int64_t N, int64_t K, void* c, int* err_word, void* stream) {
+  AEOQ_REQUIRE(M >= 0 && N >= 0 && K >= 0, AEOQ_ERR_INVALID, "fp8_gemm: negative shape");
+  AEOQ_REQUIRE(N % 128 == 0, AEOQ_ERR_INVALID, "fp8_gemm: N (%lld) must be a multiple of 128", (long long)N);
+  AEOQ_REQUIRE(K % 32 == 0 && K > 0, AEOQ_ERR_INVALID, "fp8_gemm: K (%lld) must be a multiple of 32", (long long)K);
+  if (M * N == 0) return AEOQ_OK;
+  AEOQ_REQUIRE(a && sa && w && sb && c && err_word, AEOQ_ERR_INVALID, "fp8_gemm: null pointer");
+  AEOQ_REQUIRE((uintptr_t)a % 16 == 0 && (uintptr_t)w % 16 == 0, AEOQ_ERR_INVALID,
+               "fp8_gemm: operands must be 16-byte aligned");
+  const int tile_n = aeoq_nvfp4_tile_n(M, N, 1);
+  TcParams p{};
+  p.n_out = N;
+  p.K = K;
+  p.num_experts = 1;
+  p.b_rows = M;
+  p.tiles_per_slot = (M + tile_n - 1) / tile_n;
+  p.mode = 0;
+  p.M = M;
+  p.epi = kEpiStore;
+  p.c = c;
+  p.c_dt = AEOQ_BF16;
+  p.ldc = N * 2;
+  p.sa_rows = sa;
+  p.sb_rows = sb;
+  p.err = err_word;
+  dim3 grid((unsigned)(N / 128), (unsigned)((M + tile_n - 1) / tile_n), 1);
+  return tc_gemm_dispatch_kind<true>(tile_n, w, N, a, p, grid, (cudaStream_t)stream);
+}
+
+// Grouped FP8 expert GEMM over expert-sorted rows (aeoq_moe_route layout).
+// epi 0: C = bf16((acc * sa[r]) * sb[e][n]); 1: GeGLU over the gate/up halves
+// (N = 2I rows, output I wide): h = bf16(bf16(gelu(bf16(g))) * bf16(u));
+// 2: down, bf16(bf16(y) * row_w[r]) (modeling.py:122-146).
+extern "C" int aeoq_fp8_gemm_grouped(const uint8_t* b, const float* sa_rows, int64_t max_rows, const int* grp_off,
+                                     const int* tile_off, int tile_n, const uint8_t* w, const float* sb_rows,
+                                     int64_t num_experts, int64_t N, int64_t K, int epi, const void* row_w, void* c,
+                                     int64_t ldc, int* err_word, void* stream) {
+  AEOQ_REQUIRE(N % 128 == 0 && K % 32 == 0 && K > 0, AEOQ_ERR_INVALID,
+               "fp8_gemm_grouped: N %% 128 == 0 and K %% 32 == 0 required");
+  AEOQ_REQUIRE(epi >= 0 && epi <= 2, AEOQ_ERR_INVALID, "fp8_gemm_grouped: bad epilogue %d", epi);
+  AEOQ_REQUIRE(tile_n == 8 || tile_n == 16 || tile_n == 32 || tile_n == 64 || tile_n == 128 || tile_n == 256,
+               AEOQ_ERR_INVALID, "fp8_gemm_grouped: tile_n must be 8..256, a power of two");
+  AEOQ_REQUIRE(num_experts >= 1 && num_experts <= 1024, AEOQ_ERR_INVALID, "fp8_gemm_grouped: bad expert count");
+  if (max_rows <= 0) return AEOQ_OK;
+  AEOQ_REQUIRE(b && sa_rows && grp_off && tile_off && w && sb_rows && c && err_word, AEOQ_ERR_INVALID,
+               "fp8_gemm_grouped: null pointer");
+  AEOQ_REQUIRE(epi != 2 || row_w, AEOQ_ERR_INVALID, "fp8_gemm_grouped: down epilogue needs row weights");
+  AEOQ_REQUIRE((uintptr_t)b % 16 == 0 && (uintptr_t)w % 16 == 0, AEOQ_ERR_INVALID,
+               "fp8_gemm_grouped: operands must be 16-byte aligned");
+  TcParams p{};
+  p.n_out = N;
+  p.K = K;
+  p.num_experts = num_experts;
+  p.b_rows = max_rows;
+  p.mode = 1;
+  p.grp_off = grp_off;
+  p.tile_off = tile_off;
+  p.epi = epi;
+  p.row_w = reinterpret_cast<const __nv_bfloat16*>(row_w);
+  p.c = c;
+  p.c_dt = AEOQ_BF16;
+  p.ldc = ldc;
+  p.sa_rows = sa_rows;
+  p.sb_rows = sb_rows;
+  p.err = err_word;
+  const int64_t max_tiles = (max_rows + tile_n - 1) / tile_n + num_experts;
+  const unsigned gx = (unsigned)(epi == kEpiGeglu ? (N / 2) / 64 : N / 128);
+  dim3 grid(gx, (unsigned)max_tiles, 1);
+  return tc_gemm_dispatch_kind<true>(tile_n, w, num_experts * N, b, p, grid, (cudaStream_t)stream);
 }

@@ -170,6 +170,29 @@ AEOQ_API int aeoq_nvfp4_gemm_grouped(const uint8_t* b, const uint8_t* b_sf_atoms
                                      const void* row_w, uint32_t* grp_amax, void* c, int64_t ldc, int* err_word,
                                      void* stream);
 
+/* FP8 tensor-core GEMMs (tcgen05.mma kind::f8f6f4, e4m3 x e4m3 -> f32) with
+ * the rowwise scaling of torch._scaled_mm as _fp8_linear calls it
+ * (bridges/gemma4/modeling.py:89-108).
+ * aeoq_fp8_gemm: a (M, K) e4m3 rows, sa (M) f32; w (N, K) e4m3, sb (N) f32;
+ *   C (M, N) bf16 = bf16((acc * sa[m]) * sb[n]). N % 128 == 0, K % 32 == 0.
+ * aeoq_fp8_gemm_grouped: expert-sorted rows b (max_rows, K) with sa_rows;
+ *   w (E, N, K), sb_rows (E * N) f32; epi 0 plain, 1 GeGLU (N = 2I, output
+ *   I wide, bf16(bf16(gelu(g)) * u)), 2 down weighted by row_w (bf16). */
+AEOQ_API int aeoq_fp8_gemm(const uint8_t* a, const float* sa, int64_t M, const uint8_t* w, const float* sb,
+                           int64_t N, int64_t K, void* c, int* err_word, void* stream);
+AEOQ_API int aeoq_fp8_gemm_grouped(const uint8_t* b, const float* sa_rows, int64_t max_rows, const int* grp_off,
+                                   const int* tile_off, int tile_n, const uint8_t* w, const float* sb_rows,
+                                   int64_t num_experts, int64_t N, int64_t K, int epi, const void* row_w, void* c,
+                                   int64_t ldc, int* err_word, void* stream);
+
+/* FP8 per-row activation quantization (_fp8_linear, modeling.py:101-104) of
+ * gathered bf16 rows: q[r] = e4m3(x[idx[r]] / sa[r]), sa[r] = max(amax, 1e-4)
+ * / 448 (f32), for r < *n_rows (device count; max_rows bounds the launch).
+ * idx = NULL reads row r. K, ld, q_ld multiples of 8. */
+AEOQ_API int aeoq_fp8_quantize_rows_gather(const void* x, int64_t ld, const int* row_idx, const int* n_rows,
+                                           int64_t max_rows, int64_t K, uint8_t* q, int64_t q_ld,
+                                           float* scale_out, void* stream);
+
 /* Device-side grouping of (token, slot) pairs by expert (replaces the
  * one_hot / nonzero / where scaffolding, modeling_nvfp4.py:208-222, and
  * modeling.py:111-121): counts, row offsets, token-tile offsets for tile_n,

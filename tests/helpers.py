@@ -45,3 +45,22 @@ def routing(T, E, k, seed):
     idx = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)])
     w = torch.softmax(torch.randn(T, k, generator=g), -1).to(torch.bfloat16)
     return idx, w
+
+
+def bf16_ulp(x) -> np.ndarray:
+    """Spacing of bf16 values at |x| (2^(e-7) for normal x in [2^e, 2^(e+1)))."""
+    a = np.abs(np.asarray(x, np.float64))
+    e = np.floor(np.log2(np.maximum(a, 2.0 ** -126)))
+    return np.exp2(e - 7)
+
+
+def within_tol_or_ulp(out, ref, tol=TOL) -> bool:
+    """max|err| <= tol * max|ref|, where an output one bf16 ulp from the
+    reference also passes. An f32 accumulation in another order than the f64
+    oracle's sits a few f32 ulps from it and, at a bf16 rounding boundary,
+    rounds to the neighbouring bf16 value: one ulp is up to 2^-8 of the value,
+    above 2e-3 * max|ref| for outputs near the maximum."""
+    out = np.asarray(out, np.float64)
+    ref = np.asarray(ref, np.float64)
+    lim = np.maximum(tol * np.max(np.abs(ref)), bf16_ulp(ref))
+    return bool(np.all(np.abs(out - ref) <= lim))
