@@ -1,0 +1,161 @@
+"""Expert-parallel NVFP4 expert layer: experts sharded over the ranks of a
+process group, tokens sharded by sequence, NCCL all-to-all dispatch and
+combine.
+
+Semantics are those of the one-GPU prefill forward
+(aeo_quant ``src/aeo_quant/bridges/gemma4/modeling_nvfp4.py:188-255``) over
+the union of all ranks' tokens, bit for bit:
+
+* the activation tensor scale comes from the global amax (one
+  all-reduce(max) of a scalar; ``quantize_2d_to_nvfp4`` over the whole
+  batch, :203-206), and each rank quantizes its own tokens with it;
+* every routed (token, slot) pair is sent, NVFP4-packed (H/2 bytes of E2M1
+  plus H/16 e4m3 scales, 3.6x fewer bytes than bf16), to the rank owning
+  its expert; an expert's rows therefore all meet on one rank, so its
+  per-expert down re-quantization (:239-244) sees exactly the rows it
+  would on one GPU;
+* the weighted expert outputs travel back to the token's rank, which folds
+  them per token in ascending expert order with bf16 rounding after each
+  add (``index_add_``, :250-253).
+
+Rank r owns experts [r * E/world, (r+1) * E/world). Pairs whose expert id
+is outside [0, E) are dropped (:209-211). ``ep_moe_forward`` is the
+orchestration shared by every backend; the expert arithmetic, the payload
+codec and the combine are supplied by an ``ops`` object (``NVFP4EpOps``
+for the CUDA library).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ... import _capi as A
+from ...gpu.quant import _nvfp4_quantize_rows
+from . import moe_ops
+
+
+def _all_to_all_rows(rows: torch.Tensor, send_counts, recv_counts, group) -> torch.Tensor:
+    out = torch.empty((sum(recv_counts),) + tuple(rows.shape[1:]), dtype=rows.dtype, device=rows.device)
+    dist.all_to_all_single(out, rows.contiguous(), list(recv_counts), list(send_counts), group=group)
+    return out
+
+
+def plan_dispatch(top_k_index: torch.Tensor, num_experts: int, world: int):
+    """Send order of the (token, slot) pairs, grouped by owning rank.
+
+    Returns ``(send_pairs, send_counts, dest)``: pair indices (t * k + j) in
+    send order (by destination rank, then pair index), pairs per destination
+    rank, and each pair's destination (``world`` for dropped pairs)."""
+    if num_experts % world:
+        raise ValueError(f"num_experts ({num_experts}) must be divisible by the world size ({world})")
+    e_loc = num_experts // world
+    ids = top_k_index.reshape(-1).to(torch.int64)
+    n = ids.numel()
+    valid = (ids >= 0) & (ids < num_experts)
+    dest = torch.where(valid, torch.div(ids, e_loc, rounding_mode="floor"), torch.full_like(ids, world))
+    key = dest * n + torch.arange(n, device=ids.device)
+    order = torch.argsort(key)
+    counts = torch.bincount(dest, minlength=world + 1)[:world]
+    n_send = int(counts.sum().item())
+    return order[:n_send], counts, dest
+
+
+def ep_moe_forward(hidden, top_k_index, top_k_weights, *, num_experts: int, group, ops):
+    """One expert-parallel MoE layer over ``group`` (see module docstring)."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    e_loc = num_experts // world
+    T, k = top_k_index.shape
+    dev = hidden.device
+    send_pairs, send_counts, _ = plan_dispatch(top_k_index, num_experts, world)
+
+    # counts: one small all-to-all, then the split sizes on the host
+    recv_counts_t = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts_t, send_counts, group=group)
+    sc = send_counts.tolist()
+    rc = recv_counts_t.tolist()
+
+    ts = ops.global_scale(hidden, group)
+    payload = ops.encode(hidden, ts)                     # per-token row tensors
+    send_tok = torch.div(send_pairs, k, rounding_mode="floor")
+    ids = top_k_index.reshape(-1).to(torch.int64)
+    wbits = top_k_weights.reshape(-1).to(torch.bfloat16).view(torch.int16).to(torch.int32)
+    local_id = (ids[send_pairs] - torch.div(ids[send_pairs], e_loc, rounding_mode="floor") * e_loc).to(torch.int32)
+    meta = torch.stack([local_id, wbits[send_pairs]], dim=1)
+
+    recv_payload = [_all_to_all_rows(p[send_tok], sc, rc, group) for p in payload]
+    recv_meta = _all_to_all_rows(meta, sc, rc, group)
+    recv_w = recv_meta[:, 1].to(torch.int16).view(torch.bfloat16)
+    out_rows = ops.experts(recv_payload, recv_meta[:, 0], recv_w, ts, rank * e_loc)   # (n_recv, H)
+
+    back = _all_to_all_rows(out_rows, rc, sc, group)     # in this rank's send order
+    pair_row = torch.full((T * k,), -1, dtype=torch.int32, device=dev)
+    pair_row[send_pairs] = torch.arange(send_pairs.numel(), dtype=torch.int32, device=dev)
+    return ops.combine(back, pair_row, top_k_index, T, k)
+
+
+class NVFP4EpOps:
+    """The CUDA library's arithmetic for ``ep_moe_forward``: the rank's
+    local experts (E/world of them) with the reference's buffers."""
+
+    def __init__(self, gu, gu_sf, gu_ts, dw, dw_sf, dw_ts):
+        self.gu, self.gu_sf, self.gu_ts = gu, gu_sf, gu_ts
+        self.dw, self.dw_sf, self.dw_ts = dw, dw_sf, dw_ts
+        self.lib = A.load()
+
+    def global_scale(self, hidden, group):
+        # amax over every rank's tokens, then ts = bf16(amax / 2688) >= 1e-12
+        # in the input dtype (quant.py:167-168)
+        amax = hidden.abs().amax().to(torch.float32).reshape(1)
+        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=group)
+        return (amax[0].to(hidden.dtype) / 2688.0).clamp(min=1e-12)
+
+    def encode(self, hidden, ts):
+        packed, sf, _ = _nvfp4_quantize_rows(hidden.contiguous(), ts)
+        return [packed, sf.view(torch.uint8)]
+
+    def experts(self, payload, local_ids, weights, ts, first_expert):
+        packed, sf = payload
+        n = packed.shape[0]
+        H = self.dw.shape[1]
+        if n == 0:
+            return torch.empty(0, H, dtype=torch.bfloat16, device=packed.device)
+        E = self.gu.shape[0]
+        r = moe_ops._Route(self.lib, local_ids.reshape(n, 1), weights.reshape(n, 1), E, moe_ops.pick_tile_n(n, E))
+        c_sorted = moe_ops._nvfp4_expert_rows(self.lib, r, packed, sf, ts, self.gu, self.gu_sf, self.gu_ts,
+                                              self.dw, self.dw_sf, self.dw_ts, False)
+        return c_sorted[r.pair_row.to(torch.int64)]
+
+    def combine(self, rows, pair_row, top_k_index, T, k):
+        H = self.dw.shape[1]
+        dev = pair_row.device
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        ids = top_k_index.contiguous()
+        if rows.shape[0] == 0:
+            rows = torch.zeros(1, H, dtype=torch.bfloat16, device=dev)
+        A.check(self.lib.aeoq_moe_combine(rows.contiguous().data_ptr(), pair_row.data_ptr(), ids.data_ptr(),
+                                          A.dtype_code(ids.dtype), T, k, H, 0, out.data_ptr(), A.stream_ptr(dev)))
+        return out
+
+
+class ExpertParallelNVFP4(torch.nn.Module):
+    """One rank's share of an expert-parallel ``Gemma4TextExpertsNVFP4``.
+
+    Holds experts [rank * E/world, (rank+1) * E/world) with the reference's
+    buffer names (first dimension E/world); ``forward`` takes this rank's
+    tokens and returns their outputs."""
+
+    def __init__(self, local_experts, num_experts: int, group=None):
+        super().__init__()
+        self.local = local_experts
+        self.num_experts = num_experts
+        self.group = group
+
+    def forward(self, hidden_states, top_k_index, top_k_weights):
+        m = self.local
+        if hidden_states.dtype != torch.bfloat16:
+            raise ValueError(f"hidden_states must be bfloat16, got {hidden_states.dtype}")
+        ops = NVFP4EpOps(m.gate_up_proj, m.gate_up_proj_scale, m.gate_up_proj_scale_2,
+                         m.down_proj, m.down_proj_scale, m.down_proj_scale_2)
+        return ep_moe_forward(hidden_states, top_k_index, top_k_weights, num_experts=self.num_experts,
+                              group=self.group, ops=ops)

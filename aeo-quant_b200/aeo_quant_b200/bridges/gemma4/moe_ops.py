@@ -124,42 +124,32 @@ class _Route:
         return self.grp_off.data_ptr() + 4 * self.E
 
 
-def nvfp4_experts_grouped(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf, dw_ts,
-                          one_token_semantics=False):
-    """Expert forward over any number of tokens on the device, no host sync.
-
-    Prefill semantics (modeling_nvfp4.py:188-255): one global activation
-    quant, per-expert gate_up, GeGLU, per-expert re-quantized down, weighted
-    combine folded in expert order with bf16 rounding after each add. With
-    ``one_token_semantics`` the down input shares one tensor scale and the
-    combine sums in f32 (modeling_nvfp4.py:132-186).
-    """
-    A.require_cuda(hidden, top_k_index, top_k_weights, gu, dw)
-    lib = A.load()
-    dev = hidden.device
+def _nvfp4_expert_rows(lib, r, a_packed, a_sf, a_ts, gu, gu_sf, gu_ts, dw, dw_sf, dw_ts, one_token_semantics):
+    """Grouped expert pipeline over quantized token rows: gather by expert,
+    gate_up GEMM with the GeGLU epilogue (per-expert |h| maxima), NVFP4
+    re-quantization (per-expert tensor scale, or one shared with
+    ``one_token_semantics``), down GEMM weighted by the routing weights.
+    Returns the (pairs, H) bf16 outputs in expert-sorted row order
+    (``r.pair_row`` maps each (token, slot) pair to its row)."""
+    dev = a_packed.device
     E, two_i, h_half = gu.shape
     H, I = h_half * 2, two_i // 2
-    T = hidden.shape[0]
-    k = top_k_index.shape[-1]
-    P = T * k
+    P, tile_n = r.P, r.tile_n
     st = A.stream_ptr(dev)
     err = A.err_word(dev)
-    tile_n = pick_tile_n(P, E)
-    r = _Route(lib, top_k_index.reshape(T, k), top_k_weights.reshape(T, k), E, tile_n)
     gu_atoms = A.weight_atoms(gu_sf, E, 2 * I, H, geglu_inter=I)
     dw_atoms = A.weight_atoms(dw_sf, E, H, I)
     max_tiles = (P + tile_n - 1) // tile_n + E
-    hp, hs, hts = quantize_2d_to_nvfp4(hidden)                                   # (:203-206)
     a_sorted = torch.empty(P, H // 2, dtype=torch.uint8, device=dev)
     a_sorted_sf = torch.empty(lib.aeoq_nvfp4_act_atoms_size(max_tiles, H, tile_n), dtype=torch.uint8, device=dev)
-    A.check(lib.aeoq_gather_rows(hp.data_ptr(), hs.data_ptr(), r.row_tok.data_ptr(), r.row_exp.data_ptr(),
+    A.check(lib.aeoq_gather_rows(a_packed.data_ptr(), a_sf.data_ptr(), r.row_tok.data_ptr(), r.row_exp.data_ptr(),
                                  r.grp_off.data_ptr(), r.tile_off.data_ptr(), tile_n, r.n_rows_ptr, P, H // 2,
                                  H // 16, a_sorted.data_ptr(), a_sorted_sf.data_ptr(), st))
     amax = torch.zeros(E, dtype=torch.int32, device=dev)
     h_sorted = torch.empty(P, I, dtype=torch.bfloat16, device=dev)
     A.check(lib.aeoq_nvfp4_gemm_grouped(a_sorted.data_ptr(), a_sorted_sf.data_ptr(), P, r.grp_off.data_ptr(),
                                         r.tile_off.data_ptr(), tile_n, gu.data_ptr(), gu_atoms.data_ptr(), E, 2 * I, H,
-                                        1, hts.data_ptr(), A.dtype_code(hts.dtype), gu_ts.data_ptr(),
+                                        1, a_ts.data_ptr(), A.dtype_code(a_ts.dtype), gu_ts.data_ptr(),
                                         A.dtype_code(gu_ts.dtype), None, None, amax.data_ptr(), h_sorted.data_ptr(),
                                         I * 2, err.data_ptr(), st))
     hq = torch.empty(P, I // 2, dtype=torch.uint8, device=dev)
@@ -174,10 +164,33 @@ def nvfp4_experts_grouped(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, 
                                         r.tile_off.data_ptr(), tile_n, dw.data_ptr(), dw_atoms.data_ptr(), E, H, I,
                                         2, None, 0, dw_ts.data_ptr(), A.dtype_code(dw_ts.dtype), ts_e.data_ptr(),
                                         r.row_w.data_ptr(), None, c_sorted.data_ptr(), H * 2, err.data_ptr(), st))
+    return c_sorted
+
+
+def nvfp4_experts_grouped(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf, dw_ts,
+                          one_token_semantics=False):
+    """Expert forward over any number of tokens on the device, no host sync.
+
+    Prefill semantics (modeling_nvfp4.py:188-255): one global activation
+    quant, per-expert gate_up, GeGLU, per-expert re-quantized down, weighted
+    combine folded in expert order with bf16 rounding after each add. With
+    ``one_token_semantics`` the down input shares one tensor scale and the
+    combine sums in f32 (modeling_nvfp4.py:132-186).
+    """
+    A.require_cuda(hidden, top_k_index, top_k_weights, gu, dw)
+    lib = A.load()
+    dev = hidden.device
+    E, two_i, h_half = gu.shape
+    H = h_half * 2
+    T = hidden.shape[0]
+    k = top_k_index.shape[-1]
+    r = _Route(lib, top_k_index.reshape(T, k), top_k_weights.reshape(T, k), E, pick_tile_n(T * k, E))
+    hp, hs, hts = quantize_2d_to_nvfp4(hidden)                                   # (:203-206)
+    c_sorted = _nvfp4_expert_rows(lib, r, hp, hs, hts, gu, gu_sf, gu_ts, dw, dw_sf, dw_ts, one_token_semantics)
     out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
     A.check(lib.aeoq_moe_combine(c_sorted.data_ptr(), r.pair_row.data_ptr(), r.ids.data_ptr(),
                                  A.dtype_code(r.ids.dtype), T, k, H, 1 if one_token_semantics else 0,
-                                 out.data_ptr(), st))
+                                 out.data_ptr(), A.stream_ptr(dev)))
     return out
 
 

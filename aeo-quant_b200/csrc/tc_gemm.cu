@@ -34,7 +34,7 @@
 // torch._scaled_mm call (bridges/gemma4/modeling.py:101-108):
 // y = (acc * sa[token]) * sb[weight row], f32.
 //
-// No TMA multicast anywhere: every CTA loads its own tiles.
+// Every CTA loads its own operand tiles; no tile is shared across CTAs.
 #include <cuda.h>
 
 #include <cstdlib>

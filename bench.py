@@ -57,6 +57,10 @@ def parse():
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
+    p.add_argument("--workload", default="decode", choices=["decode", "ep"],
+                   help="decode: config 1 (default); ep: config 4, expert-parallel prefill stack")
+    p.add_argument("--tokens", type=int, default=32 * 2048, help="ep: tokens over all ranks")
+    p.add_argument("--ep-layers", type=int, default=4)
     return p.parse_args()
 
 
@@ -224,11 +228,122 @@ def run_reference(args, rank):
     }), flush=True)
 
 
+def main_ep(args, rank, world, local):
+    """Config 4: a stack of NVFP4 MoE layers (config-2 shapes), experts
+    sharded E/world per GPU, tokens sharded by sequence, NCCL all-to-all
+    dispatch (NVFP4-packed rows) and combine (bf16 rows). One step = the
+    whole stack over all ranks' tokens; value = tokens / max-over-ranks
+    device time (strong scaling: the token count is fixed)."""
+    import torch
+    import torch.distributed as dist
+    from aeo_quant_b200.bridges.gemma4.expert_parallel import ExpertParallelNVFP4
+    from aeo_quant_b200.bridges.gemma4.modeling_nvfp4 import Gemma4TextExpertsNVFP4
+    from aeo_quant_b200.gpu import quant as Q
+    import types
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    else:
+        dist.init_process_group("nccl", init_method="tcp://127.0.0.1:29599", rank=0, world_size=1, device_id=dev)
+    K, W = args.steps, max(3, args.warmup)
+    e_loc = E // world
+    T = args.tokens // world
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    cfg = types.SimpleNamespace(num_experts=e_loc, hidden_size=H, moe_intermediate_size=I,
+                                hidden_activation="gelu_pytorch_tanh")
+    layers = []
+    for l in range(args.ep_layers):
+        gl = torch.Generator(device=dev).manual_seed(10 * l + 1)   # same weights on every rank
+        m = Gemma4TextExpertsNVFP4(cfg).to(dev)
+        for r in range(world):   # draw every rank's slice so the stack is independent of world
+            wgu = (torch.randn(e_loc, 2 * I, H, generator=gl, device=dev) * 0.02).to(torch.bfloat16)
+            wd = (torch.randn(e_loc, H, I, generator=gl, device=dev) * 0.02).to(torch.bfloat16)
+            if r == rank:
+                gp, gs, gt = Q.quantize_3d_to_nvfp4(wgu)
+                dp, ds, dt = Q.quantize_3d_to_nvfp4(wd)
+            del wgu, wd
+        m.gate_up_proj.copy_(gp); m.gate_up_proj_scale.copy_(gs); m.gate_up_proj_scale_2.copy_(gt.float())
+        m.down_proj.copy_(dp); m.down_proj_scale.copy_(ds); m.down_proj_scale_2.copy_(dt.float())
+        layers.append(ExpertParallelNVFP4(m, E))
+    hid = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    # Zipf(s=1.2) over a seeded permutation of the experts, 8 distinct per token
+    perm = torch.randperm(E, generator=torch.Generator().manual_seed(5)).to(dev)
+    p = 1.0 / torch.arange(1, E + 1, device=dev, dtype=torch.float32) ** 1.2
+    ids = perm[torch.multinomial(p.expand(T, E), TOPK, replacement=False, generator=g)]
+    wts = torch.softmax(torch.randn(T, TOPK, generator=g, device=dev), -1).to(torch.bfloat16)
+
+    def step(x):
+        for lay in layers:
+            x = lay(x, ids, wts)
+        return x
+
+    for _ in range(W):
+        step(hid)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record()
+        for _ in range(K):
+            y = step(hid)
+        ev1.record()
+        torch.cuda.synchronize()
+    dist.barrier()
+    t = torch.tensor([ev0.elapsed_time(ev1)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    value = args.tokens * K / (ms / 1000.0)
+    flops = args.tokens * TOPK * 2 * (1408 * 2816 + 2816 * 704) * args.ep_layers * K
+    # e2e: this rank's tokens from pinned host memory, the output back
+    hid_h = hid.cpu().pin_memory()
+    out_h = torch.empty_like(hid_h).pin_memory()
+    dist.barrier()
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record()
+    x_in = torch.empty_like(hid)
+    for _ in range(K):
+        x_in.copy_(hid_h, non_blocking=True)
+        out_h.copy_(step(x_in), non_blocking=True)
+    b1.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([b0.elapsed_time(b1)], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e = args.tokens * K / (float(te.item()) / 1000.0)
+    if rank == 0:
+        ach = flops / (ms / 1000.0) / 1e12 / world
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp4(e2m1)+e4m3 scales, fp32 accumulate, bf16 io",
+            "data": "synthetic (bf16 N(0,0.02) weights quantized on device; N(0,1) hidden; Zipf(1.2) top-8)",
+            "config": {"workload": f"config4: expert-parallel NVFP4 MoE stack, {args.ep_layers} layers, "
+                                   f"{args.tokens} tokens over {world} GPU(s)",
+                       "experts": E, "experts_per_gpu": e_loc, "hidden": H, "intermediate": I, "top_k": TOPK,
+                       "parallelism": f"ep{world}", "timing": "CUDA events around K steps, max over ranks",
+                       "l2": "inputs larger than L2 (activations and expert weights per step)"},
+            "gpu_launches": None,
+            "clocks": clk.summary(),
+            "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": args.tokens * H * 2,
+                    "d2h_bytes_per_step": args.tokens * H * 2},
+            "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": 9000.0, "unit": "TFLOP/s",
+                         "frac": round(ach / 9000.0, 4), "peak_source": "nominal dense FP4 (no measured FP4 peak)",
+                         "traffic": None, "per": "GPU"},
+        }), flush=True)
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.workload == "ep":
+        main_ep(args, rank, world, local)
         return
     import torch
     import torch.distributed as dist

@@ -1,0 +1,59 @@
+"""Expert-parallel dispatch/combine: two gloo ranks on CPU run the shared
+orchestration with oracle arithmetic; their outputs must equal the
+one-process oracle prefill forward over all tokens, bit for bit."""
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe as OM
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return str(s.getsockname()[1])
+
+
+@pytest.mark.parametrize("case", [0, 1])
+def test_ep_two_ranks_match_one_process(tmp_path, case):
+    sys.path.insert(0, HERE)
+    from ep_worker import case_inputs
+    world, port = 2, _free_port()
+    outs = [str(tmp_path / f"r{r}.npz") for r in range(world)]
+    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "ep_worker.py"), str(r), str(world), port,
+                               outs[r], str(case)], stdout=subprocess.PIPE, stderr=subprocess.STDOUT)
+             for r in range(world)]
+    logs = []
+    for p in procs:
+        try:
+            logs.append(p.communicate(timeout=240)[0].decode(errors="replace"))
+        except subprocess.TimeoutExpired:
+            p.kill()
+            pytest.fail("expert-parallel worker timed out")
+    assert all(p.returncode == 0 for p in procs), "\n".join(logs)
+    m, hidden, ids, w = case_inputs(case)
+    ref = OM.nvfp4_prefill(m, hidden, ids, w)
+    y = np.zeros_like(ref)
+    for o in outs:
+        d = np.load(o)
+        y[int(d["lo"]):int(d["hi"])] = d["y"]
+    np.testing.assert_array_equal(y.view(np.uint32), ref.view(np.uint32))
+
+
+def test_plan_dispatch_groups_pairs_by_rank():
+    sys.path.insert(0, os.path.join(os.path.dirname(HERE), "aeo-quant_b200"))
+    from aeo_quant_b200.bridges.gemma4.expert_parallel import plan_dispatch
+    ids = torch.tensor([[7, 0, 4], [1, 8, 5]])          # E = 8, world = 2: experts 0-3 on rank 0
+    send, counts, dest = plan_dispatch(ids, 8, 2)
+    assert counts.tolist() == [2, 3]
+    assert send.tolist() == [1, 3, 0, 2, 5]             # rank 0: pairs 1, 3; rank 1: pairs 0, 2, 5
+    assert dest.tolist() == [1, 0, 1, 0, 2, 1]          # id 8 (== E) is dropped
+    with pytest.raises(ValueError, match="divisible by the world size"):
+        plan_dispatch(ids, 8, 3)
