@@ -89,10 +89,10 @@ def nvfp4_decode(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf
 def pick_tile_n(n_pairs: int, num_experts: int) -> int:
     """Token-tile width of the grouped GEMMs from the mean rows per expert."""
     avg = max(1, n_pairs // max(1, min(num_experts, n_pairs)))
-    for bn in (8, 16, 32, 64, 128):
+    for bn in (8, 16, 32, 64):
         if avg <= bn:
             return bn
-    return 256
+    return 128   # the persistent kernel (accumulator double-buffered in TMEM)
 
 
 class _Route:

@@ -37,6 +37,7 @@
 // Every CTA loads its own operand tiles; no tile is shared across CTAs.
 #include <cuda.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <mutex>
 
@@ -45,7 +46,8 @@
 
 namespace aeoq {
 
-constexpr int kTcThreads = 192;
+constexpr int kEpiWarps = 8;                       // two per TMEM lane quadrant
+constexpr int kTcThreads = 64 + 32 * kEpiWarps;    // producer, MMA issuer, epilogue
 constexpr int kTcStages = 4;
 constexpr int kKT = 256;            // K values per stage
 constexpr int kKTBytes = kKT / 2;   // 128 B per row per stage
@@ -84,6 +86,7 @@ struct TcParams {
   uint32_t* grp_amax;                     // kEpiGeglu: per-expert |h| max key (atomicMax)
   const float* sa_rows;                   // FP8: per activation (B) row scale, f32
   const float* sb_rows;                   // FP8: per weight row scale, f32 [num_experts * n_out]
+  int tiles_x, tiles_y, tiles_z;          // persistent kernel: tile grid (mode 1: tiles_y read on device)
   int* err;                               // device error word (bounded waits)
   uint64_t* trace;                        // development builds only: per-CTA phase stamps
   int dbg;                                // development builds only: experiment switches
@@ -120,18 +123,23 @@ struct TcLayout {
   static constexpr size_t kSfa = kF8 ? 0 : 4 * 512;
   static constexpr size_t kSfb = kF8 ? 0 : (size_t)4 * 512 * kSfbAtoms;
   static constexpr size_t kStage = kA + kB + kSfa + kSfb;
-  // as many stages as the shared-memory budget holds (at most 8)
-  static constexpr int kStages =
-      (int)((220 * 1024 - 1280) / kStage) < kTcMaxStages ? (int)((220 * 1024 - 1280) / kStage) : kTcMaxStages;
+  // Tiles up to 128 tokens wide run two CTAs per SM (half the shared memory
+  // and at most 256 TMEM columns each), so one CTA's epilogue overlaps the
+  // other's main loop; wider tiles take the whole SM.
+  static constexpr int kCtasPerSm = (BN <= 128) ? 2 : 1;
+  // two CTAs: 2 x (kBytes + 1 KB reserved) within the SM's 228 KB
+  static constexpr size_t kBudget =
+      kCtasPerSm == 2 ? (113 * 1024 - 1024 - sizeof(TcSmem) - 64) : (220 * 1024 - 1280 - sizeof(TcSmem));
+  // as many stages as the budget holds (at most 8)
+  static constexpr int kStages = (int)(kBudget / kStage) < kTcMaxStages ? (int)(kBudget / kStage) : kTcMaxStages;
   // The epilogue reuses the stage ring, idle once the accumulator is
-  // complete: the GeGLU exchange of the up half (64 x BN f32) and the
-  // output tile staged for coalesced row stores (BN x 128 x 4 B at most).
+  // complete, for the GeGLU exchange of the up half (64 x BN f32).
   static constexpr size_t kXchg = 64 * (size_t)BN * 4;
-  static constexpr size_t kOut = (size_t)BN * 128 * 4;
-  static_assert(kXchg + kOut <= kStages * kStage, "epilogue buffers must fit in the stage ring");
+  static_assert(kXchg <= kStages * kStage, "the GeGLU exchange must fit in the stage ring");
   static constexpr size_t kBytes = 1024 + kStages * kStage + sizeof(TcSmem) + 64;
   static constexpr uint32_t kTmemCols =
       kF8 ? (BN <= 32 ? 32u : (uint32_t)BN) : ((BN + 32 * kSfbAtoms + 16 <= 256) ? 256u : 512u);
+  static_assert(kCtasPerSm == 1 || kTmemCols <= 256, "two CTAs per SM need at most 256 TMEM columns each");
   static constexpr uint32_t kSfaCol = BN;                  // 16 columns
   static constexpr uint32_t kSfbCol = BN + 16;             // 16 * kSfbAtoms columns
 };
@@ -145,20 +153,20 @@ struct TileInfo {
 };
 
 template <int BN>
-__device__ __forceinline__ TileInfo resolve_tile(const TcParams& p) {
+__device__ __forceinline__ TileInfo resolve_tile_at(const TcParams& p, int y_tile, int z_slot) {
   TileInfo t{};
   if (p.mode == 0) {
-    const int64_t s = blockIdx.z;
-    const int64_t tb = (int64_t)blockIdx.y * BN;
+    const int64_t s = z_slot;
+    const int64_t tb = (int64_t)y_tile * BN;
     t.slot = s;
     t.expert = p.ids ? load_index(p.ids, p.ids_dt, s) : s;
     t.b_row0 = s * p.b_slot_rows + tb;
     t.c_row0 = tb;
-    t.tile = (p.b_slot_rows ? s * p.tiles_per_slot : 0) + blockIdx.y;
+    t.tile = (p.b_slot_rows ? s * p.tiles_per_slot : 0) + y_tile;
     t.n_valid = (int)min((int64_t)BN, p.M - tb);
     t.active = t.n_valid > 0;
   } else {
-    const int y = blockIdx.y;
+    const int y = y_tile;
     const int E = (int)p.num_experts;
     if (y >= p.tile_off[E]) {
       t.active = false;
@@ -183,6 +191,11 @@ __device__ __forceinline__ TileInfo resolve_tile(const TcParams& p) {
   return t;
 }
 
+template <int BN>
+__device__ __forceinline__ TileInfo resolve_tile(const TcParams& p) {
+  return resolve_tile_at<BN>(p, (int)blockIdx.y, (int)blockIdx.z);
+}
+
 // min(BN, 32) accumulator columns of this thread's TMEM lane, one wait.
 template <int BN>
 __device__ __forceinline__ void tmem_cols(uint32_t taddr, float (&v)[32]) {
@@ -200,8 +213,62 @@ __device__ __forceinline__ void tmem_cols(uint32_t taddr, float (&v)[32]) {
   }
 }
 
+// Stores 8 tokens x the warp's 32 output columns as bf16. On entry lane L
+// holds column L's values for the 8 tokens in y[]; an 8x8 transpose inside
+// each group of 8 lanes (three butterfly stages of shuffles) leaves lane
+// 8g + i with token i's values for columns 8g .. 8g+7, written as one
+// 16-byte store. row0 = output of token 0, column 0 of the warp; tokens >=
+// n_ok are not written.
+__device__ __forceinline__ void store_8tok_bf16(float (&y)[8], char* row0, int64_t ldc, int n_ok, int lane) {
+#pragma unroll
+  for (int s = 4; s >= 1; s >>= 1) {
+    const bool up = (lane & s) != 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j & s) continue;
+      const float send = up ? y[j] : y[j | s];
+      const float recv = __shfl_xor_sync(0xffffffffu, send, s);
+      if (up) y[j] = recv; else y[j | s] = recv;
+    }
+  }
+  const int i = lane & 7, g = lane >> 3;
+  if (i < n_ok) {
+    __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = __float2bfloat16_rn(y[j]);
+    *reinterpret_cast<uint4*>(row0 + i * ldc + 16 * g) = *reinterpret_cast<const uint4*>(o);
+  }
+}
+
+// N (8, 16, 32 or 64) accumulator columns of this thread's TMEM lane, one wait.
+template <int N, int VN>
+__device__ __forceinline__ void tmem_chunk(uint32_t taddr, float (&v)[VN]) {
+  if constexpr (N == 64) {
+    uint32_t r0[32], r1[32];
+    sm100::tmem_ld32_nowait(taddr, r0);
+    sm100::tmem_ld32_nowait(taddr + 32, r1);
+    sm100::tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      v[i] = __uint_as_float(r0[i]);
+      v[32 + i] = __uint_as_float(r1[i]);
+    }
+  } else if constexpr (N == 32) {
+    uint32_t r[32];
+    sm100::tmem_ld32_nowait(taddr, r);
+    sm100::tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  } else {
+    float w[16];
+    sm100::tmem_ld16(taddr, w);   // reads 16 columns; only N of them are used
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = w[i];
+  }
+}
+
 template <int BN, bool kF8>
-__global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+__global__ void __launch_bounds__(kTcThreads, (BN <= 128) ? 2 : 1) nvfp4_tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                                                                       const __grid_constant__ CUtensorMap tmB,
                                                                       const TcParams p) {
   using L = TcLayout<BN, kF8>;
@@ -246,50 +313,59 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
   const uint32_t tmem = sh->tmem_base;
   if (tid == 0) TC_TRACE(1);
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    {
-      const bool leader = sm100::elect_one();
-#ifdef AEOQ_TC_TRACE
-      uint64_t pwait_ = 0;
-#endif
-      const int64_t m_tiles = p.n_out / 128;
-      const uint8_t* sfa_base = p.sfa + ((ti.expert * m_tiles + m_tile) * kb_total) * 512;
-      const uint8_t* sfb_base = p.sfb + (ti.tile * kb_total) * (size_t)L::kSfbAtoms * 512;
-      for (int kt = 0; kt < num_kt; ++kt) {
-        const int s = kt % L::kStages;
-        const uint32_t ph = (kt / L::kStages) & 1;
-#ifdef AEOQ_TC_TRACE
-        uint64_t w0_; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(w0_));
-#endif
-        if (!sm100::mbar_wait(&sh->empty[s], ph ^ 1, p.err, 11)) break;
-#ifdef AEOQ_TC_TRACE
-        { uint64_t w1_; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(w1_)); pwait_ += w1_ - w0_; }
-#endif
-        const int nkb = min(4, kb_total - kt * 4);
-        const uint32_t sfa_bytes = kF8 ? 0u : (uint32_t)nkb * 512;
-        const uint32_t sfb_bytes = kF8 ? 0u : (uint32_t)nkb * L::kSfbAtoms * 512;
-        const int32_t x = kt * kKTBytes;
-        if (!leader) continue;
-        sm100::mbar_arrive_expect_tx(&sh->full[s], (uint32_t)(L::kA + L::kB) + sfa_bytes + sfb_bytes);
-        if constexpr (!kF8) {
-          bulk_g2s(stSFA(s), sfa_base + (size_t)kt * 4 * 512, sfa_bytes, &sh->full[s]);
-          bulk_g2s(stSFB(s), sfb_base + (size_t)kt * 4 * L::kSfbAtoms * 512, sfb_bytes, &sh->full[s]);
+  // ------------------------------------------------------------ producers
+  // Each ring slot's copies are split by operand: request r = 4 * slot + op
+  // (op 0 the A tile, which also posts the stage's expected bytes, 1 the B
+  // tile, 2 and 3 the two scale-atom blocks; FP8 has ops 0 and 1) is issued
+  // by producer r % kProducers (warp 0 and the epilogue warps, idle until
+  // the accumulator is complete). A producer issues every use of its
+  // requests in order, so each parity wait on a slot's empty barrier refers
+  // to the previous use of that slot. One warp's copies complete one after
+  // another, so spreading them over many warps multiplies the fill rate.
+  // (A copy may complete before the stage's expected bytes are posted; the
+  // barrier's transaction count then dips below zero until they are.)
+  constexpr int kProducers = 1 + kEpiWarps;
+  constexpr int kOps = kF8 ? 2 : 4;
+  const int pidx = warp == 0 ? 0 : warp - 1;   // warps 2.. -> 1..
+  if (warp != 1) {
+    const bool leader = sm100::elect_one();
+    const int64_t m_tiles = p.n_out / 128;
+    const uint8_t* sfa_base = p.sfa + ((ti.expert * m_tiles + m_tile) * kb_total) * 512;
+    const uint8_t* sfb_base = p.sfb + (ti.tile * kb_total) * (size_t)L::kSfbAtoms * 512;
+    for (int kt = 0; kt < num_kt; ++kt) {
+      const int s = kt % L::kStages;
+      const uint32_t ph = (kt / L::kStages) & 1;
+      const int nkb = min(4, kb_total - kt * 4);
+      const uint32_t sfa_bytes = kF8 ? 0u : (uint32_t)nkb * 512;
+      const uint32_t sfb_bytes = kF8 ? 0u : (uint32_t)nkb * L::kSfbAtoms * 512;
+      const int32_t x = kt * kKTBytes;
+      for (int op = 0; op < kOps; ++op) {
+        if ((kOps * s + op) % kProducers != pidx) continue;
+        if (!sm100::mbar_wait(&sh->empty[s], ph ^ 1, p.err, 11)) { kt = num_kt; break; }
+        if (leader) {
+          if (op == 0) {
+            sm100::mbar_arrive_expect_tx(&sh->full[s], (uint32_t)(L::kA + L::kB) + sfa_bytes + sfb_bytes);
+            if (geglu) {
+              const int64_t n0 = m_tile * 64;
+              sm100::tma_load_2d(stA(s), &tmA, x, (int32_t)(a_row_base + n0), &sh->full[s]);
+              sm100::tma_load_2d(stA(s) + 64 * kKTBytes, &tmA, x, (int32_t)(a_row_base + p.n_out / 2 + n0),
+                                 &sh->full[s]);
+            } else {
+              sm100::tma_load_2d(stA(s), &tmA, x, (int32_t)(a_row_base + m_tile * 128), &sh->full[s]);
+            }
+          } else if (op == 1) {
+            sm100::tma_load_2d(stB(s), &tmB, x, (int32_t)ti.b_row0, &sh->full[s]);
+          } else if constexpr (!kF8) {
+            if (op == 2) bulk_g2s(stSFA(s), sfa_base + (size_t)kt * 4 * 512, sfa_bytes, &sh->full[s]);
+            else bulk_g2s(stSFB(s), sfb_base + (size_t)kt * 4 * L::kSfbAtoms * 512, sfb_bytes, &sh->full[s]);
+          }
         }
-        if (geglu) {
-          const int64_t n0 = m_tile * 64;
-          sm100::tma_load_2d(stA(s), &tmA, x, (int32_t)(a_row_base + n0), &sh->full[s]);
-          sm100::tma_load_2d(stA(s) + 64 * kKTBytes, &tmA, x, (int32_t)(a_row_base + p.n_out / 2 + n0),
-                             &sh->full[s]);
-        } else {
-          sm100::tma_load_2d(stA(s), &tmA, x, (int32_t)(a_row_base + m_tile * 128), &sh->full[s]);
-        }
-        sm100::tma_load_2d(stB(s), &tmB, x, (int32_t)ti.b_row0, &sh->full[s]);
+        __syncwarp();
       }
-#ifdef AEOQ_TC_TRACE
-      (void)pwait_;
-#endif
     }
+  }
+  if (warp == 0) {
+    // producer only
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     {
@@ -353,6 +429,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;            // TMEM lane quadrant this warp may access
     const int row = 32 * q + lane;     // accumulator row = weight row in the tile
+    // the two warps of a quadrant split the tile's tokens
+    constexpr int kHalf = BN >= 16 ? BN / 2 : BN;
+    const int hseg = (warp - 2) >> 2;
+    const int tbeg = hseg * kHalf, tend = min(BN, tbeg + kHalf);
     // Scales, read while the main loop runs. NVFP4: one alpha per tile.
     // FP8: this row's weight scale (GeGLU tiles: gate rows n0.., up rows
     // n_out/2 + n0..) and the tile's activation row scales in shared memory.
@@ -362,8 +442,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
       const int64_t wrow = geglu ? (row < 64 ? m_tile * 64 + row : p.n_out / 2 + m_tile * 64 + (row - 64))
                                  : m_tile * 128 + row;
       alpha = p.sb_rows[ti.expert * p.n_out + wrow];
-      for (int t = tid - 64; t < BN; t += 128) colscale[t] = t < ti.n_valid ? p.sa_rows[ti.b_row0 + t] : 0.0f;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      for (int t = tid - 64; t < BN; t += 32 * kEpiWarps) colscale[t] = t < ti.n_valid ? p.sa_rows[ti.b_row0 + t] : 0.0f;
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
     } else {
       if (p.epi == kEpiScaleRow) alpha = p.grp_alpha_ts[ti.expert] * load_scalar_f(p.w_ts, p.w_ts_dt);
       else alpha = load_scalar_f(p.a_ts, p.a_ts_dt) * load_scalar_f(p.w_ts, p.w_ts_dt);
@@ -375,82 +455,99 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
     sm100::tc_fence_after();
     char* cbase = reinterpret_cast<char*>(p.c) + ti.slot * p.c_slot_stride;
     uint32_t hkey = 0;
-    // Output tile staged in shared memory as [token][column] so the global
-    // stores are whole 16-byte pieces of output rows.
-    uint8_t* outs = base + L::kXchg;
     const int ncol = geglu ? 64 : 128;
     const int es = (p.epi == kEpiStore && p.c_dt == AEOQ_F32) ? 4 : 2;
-    constexpr int kChunk = BN < 32 ? BN : 32;   // columns per tcgen05.ld batch
+    // Stores go straight from registers. A thread owns one output column
+    // (its weight row); bf16 outputs are transposed in 8-token groups so each
+    // lane writes 8 consecutive columns of one token (16 bytes); f32 outputs
+    // are written per element (a warp covers 128 contiguous bytes).
+    const int64_t col_w = (int64_t)m_tile * ncol + 32 * (q & (geglu ? 1 : 3));   // warp's first column
+    char* cwarp = cbase + ti.c_row0 * p.ldc + col_w * es;
+    constexpr int kChunk = kHalf < 32 ? kHalf : 32;   // columns per TMEM wait
+    const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
 #ifdef AEOQ_TC_TRACE
     long long e_ld = 0, e_st = 0, e0_ = clock64();
 #endif
     if (p.epi != kEpiGeglu) {
-      for (int c0 = 0; c0 < BN; c0 += kChunk) {
-        float v[32];
+      for (int c0 = tbeg; c0 < tend; c0 += kChunk) {
+        float v[kChunk < 16 ? 16 : kChunk];
 #ifdef AEOQ_TC_TRACE
         const long long a_ = clock64();
 #endif
-        tmem_cols<BN>(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+        tmem_chunk<kChunk>(tq + (uint32_t)c0, v);
 #ifdef AEOQ_TC_TRACE
         e_ld += clock64() - a_;
 #endif
 #pragma unroll
-        for (int j = 0; j < kChunk; ++j) {
-          const int t = c0 + j;
-          if (t < BN) {
-            float y = scaled(v[j], t);
-            if (p.epi == kEpiScaleRow)
-              y = (t < ti.n_valid) ? bf16r(y) * __bfloat162float(p.row_w[ti.c_row0 + t]) : 0.f;
-            if (es == 4) reinterpret_cast<float*>(outs)[t * ncol + row] = y;
-            else reinterpret_cast<__nv_bfloat16*>(outs)[t * ncol + row] = __float2bfloat16_rn(y);
+        for (int g8 = 0; g8 < kChunk; g8 += 8) {
+          const int t0 = c0 + g8;
+          float y[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int t = t0 + j;
+            float val = (t < ti.n_valid) ? scaled(v[g8 + j], t) : 0.0f;
+            if (p.epi == kEpiScaleRow && t < ti.n_valid) val = bf16r(val) * __bfloat162float(p.row_w[ti.c_row0 + t]);
+            y[j] = val;
+          }
+          if (!ok) continue;
+#ifdef AEOQ_TC_TRACE
+          if (p.dbg & 4) { if (y[0] == 12345.f) *reinterpret_cast<float*>(cwarp) = y[1]; continue; }
+          if (p.dbg & 8) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              if (t0 + j < ti.n_valid) *reinterpret_cast<__nv_bfloat16*>(cwarp + (t0 + j) * p.ldc + 2 * lane) = __float2bfloat16_rn(y[j]);
+            continue;
+          }
+#endif
+          if (es == 2) {
+            store_8tok_bf16(y, cwarp + t0 * p.ldc, p.ldc, ti.n_valid - t0, lane);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              if (t0 + j < ti.n_valid) *reinterpret_cast<float*>(cwarp + (t0 + j) * p.ldc + 4 * lane) = y[j];
           }
         }
       }
     } else {
       // GeGLU: rows 64..127 (up) hand bf16(alpha*acc) to rows 0..63 (gate)
-      for (int c0 = 0; c0 < BN; c0 += kChunk) {
-        float v[32];
-        tmem_cols<BN>(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
-        if (row >= 64) {
+      if (row >= 64) {
+        for (int c0 = tbeg; c0 < tend; c0 += kChunk) {
+          float v[kChunk < 16 ? 16 : kChunk];
+          tmem_chunk<kChunk>(tq + (uint32_t)c0, v);
 #pragma unroll
-          for (int j = 0; j < kChunk; ++j)
-            if (c0 + j < BN) xchg[(row - 64) * BN + c0 + j] = bf16r(scaled(v[j], c0 + j));
+          for (int j = 0; j < kChunk; ++j) xchg[(row - 64) * BN + c0 + j] = bf16r(scaled(v[j], c0 + j));
         }
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
       if (q < 2) {
-        for (int c0 = 0; c0 < BN; c0 += kChunk) {
-          float v[32];
-          tmem_cols<BN>(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+        for (int c0 = tbeg; c0 < tend; c0 += kChunk) {
+          float v[kChunk < 16 ? 16 : kChunk];
+          tmem_chunk<kChunk>(tq + (uint32_t)c0, v);
 #pragma unroll
-          for (int j = 0; j < kChunk; ++j) {
-            const int t = c0 + j;
-            if (t < BN) {
-              const float g = bf16r(scaled(v[j], t));
-              const float u = xchg[row * BN + t];
-              const __nv_bfloat16 hv = __float2bfloat16_rn(bf16r(gelu_tanh(g)) * u);
-              reinterpret_cast<__nv_bfloat16*>(outs)[t * ncol + row] = hv;
-              if (t < ti.n_valid) hkey = max(hkey, In<AEOQ_BF16>::abs_key(hv));
+          for (int g8 = 0; g8 < kChunk; g8 += 8) {
+            const int t0 = c0 + g8;
+            float y[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int t = t0 + j;
+              float hvf = 0.0f;
+              if (t < ti.n_valid) {
+                const float gv = bf16r(scaled(v[g8 + j], t));
+                const float u = xchg[row * BN + t];
+                const __nv_bfloat16 hv = __float2bfloat16_rn(bf16r(gelu_tanh(gv)) * u);
+                hkey = max(hkey, In<AEOQ_BF16>::abs_key(hv));
+                hvf = __bfloat162float(hv);
+              }
+              y[j] = hvf;
             }
+            if (ok) store_8tok_bf16(y, cwarp + t0 * p.ldc, p.ldc, ti.n_valid - t0, lane);
           }
         }
       }
     }
 #ifdef AEOQ_TC_TRACE
     const long long e1_ = clock64();
-#endif
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (ok) {
-      const int chunks = ncol * es / 16;             // 16-byte pieces per output row
-      const int64_t col0 = (int64_t)m_tile * ncol * es;
-      for (int idx = tid - 64; idx < ti.n_valid * chunks; idx += 128) {
-        const int t = idx / chunks, c = idx - t * chunks;
-        *reinterpret_cast<uint4*>(cbase + (ti.c_row0 + t) * p.ldc + col0 + 16 * c) =
-            *reinterpret_cast<const uint4*>(outs + (size_t)t * ncol * es + 16 * c);
-      }
-    }
-#ifdef AEOQ_TC_TRACE
-    e_st = clock64() - e1_;
+    e_st = 0;
     if (tid == 64 && p.trace) {
       const uint64_t c_ = blockIdx.x + (uint64_t)gridDim.x * (blockIdx.y + (uint64_t)gridDim.y * blockIdx.z);
       if (c_ < 8192) { p.trace[c_ * 8 + 5] = e_ld; p.trace[c_ * 8 + 6] = e1_ - e0_; p.trace[c_ * 8 + 1] = e_st; }
@@ -468,6 +565,351 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_gemm_kernel(const __gr
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, L::kTmemCols);
   }
+}
+
+
+int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int64_t row_bytes, int64_t ld, int box_rows);
+
+// ---------------------------------------------------------------- persistent
+// Persistent variant: one CTA per SM walks a static tile schedule (weight
+// tiles fastest, so the CTAs working at the same time share token tiles in
+// L2). The producers run ahead across tile boundaries, and the accumulator
+// is double-buffered in TMEM: the epilogue of tile i (eight warps, two per
+// lane quadrant) overlaps the main loop of tile i + 1.
+//   warps 0, 2, 3   producers (ring slot s is filled by producer s % 3)
+//   warp 1          TMEM owner + MMA issuer
+//   warps 4 .. 11   epilogue
+constexpr int kPThreads = 384;
+constexpr int kPProducers = 3;
+constexpr int kPEpiWarps = 8;
+
+template <int BN, bool kF8>
+struct PLayout {
+  static constexpr int kSfbAtoms = (BN + 127) / 128;
+  static constexpr size_t kA = 128 * kKTBytes;
+  static constexpr size_t kB = (size_t)BN * kKTBytes;
+  static constexpr size_t kSfa = kF8 ? 0 : 4 * 512;
+  static constexpr size_t kSfb = kF8 ? 0 : (size_t)4 * 512 * kSfbAtoms;
+  static constexpr size_t kStage = kA + kB + kSfa + kSfb;
+  static constexpr size_t kXchg = 64 * (size_t)BN * 2;   // GeGLU up half, bf16
+  struct Smem {
+    uint64_t full[kTcMaxStages], empty[kTcMaxStages], acc_full[2], acc_empty[2];
+    uint32_t tmem_base;
+    float colscale[256];
+  };
+  static constexpr size_t kFixed = 1024 + kXchg + sizeof(Smem) + 64;
+  static constexpr int kStages =
+      (int)((227 * 1024 - kFixed) / kStage) < kTcMaxStages ? (int)((227 * 1024 - kFixed) / kStage) : kTcMaxStages;
+  static_assert(kStages >= 2, "persistent tile too wide for the shared-memory ring");
+  static constexpr size_t kBytes = 1024 + kStages * kStage + kXchg + sizeof(Smem) + 64;
+  static constexpr uint32_t kAccStride = (uint32_t)((BN + 31) / 32 * 32);
+  static constexpr uint32_t kSfaCol = 2 * kAccStride;
+  static constexpr uint32_t kSfbCol = kSfaCol + 16;
+  static_assert(kSfbCol + 16 * kSfbAtoms <= 512, "two accumulators and the scale columns must fit in TMEM");
+  static constexpr uint32_t kTmemCols = (kF8 ? 2 * kAccStride : kSfbCol + 16 * kSfbAtoms) <= 256 ? 256u : 512u;
+};
+
+template <int BN, bool kF8>
+__global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                                          const __grid_constant__ CUtensorMap tmB,
+                                                                          const TcParams p) {
+  using L = PLayout<BN, kF8>;
+  using Smem = typename L::Smem;
+  constexpr int kStepK = kF8 ? 32 : 64;
+  extern __shared__ __align__(1024) uint8_t dsmem[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~uintptr_t(1023));
+  uint8_t* stage0 = base;
+  __nv_bfloat16* xchg = reinterpret_cast<__nv_bfloat16*>(base + L::kStages * L::kStage);
+  Smem* sh = reinterpret_cast<Smem*>(base + L::kStages * L::kStage + L::kXchg);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool geglu = (p.epi == kEpiGeglu);
+  const int num_kt = (int)((p.K + 4 * kStepK - 1) / (4 * kStepK));
+  const int kb_total = (int)(p.K / kStepK);
+  auto stA = [&](int s) { return stage0 + s * L::kStage; };
+  auto stB = [&](int s) { return stage0 + s * L::kStage + L::kA; };
+  auto stSFA = [&](int s) { return stage0 + s * L::kStage + L::kA + L::kB; };
+  auto stSFB = [&](int s) { return stage0 + s * L::kStage + L::kA + L::kB + L::kSfa; };
+
+  // the tile schedule: tile t -> (weight tile t % tiles_x, token tile, slot)
+  const int tx = p.tiles_x;
+  const int ty = p.mode == 1 ? p.tile_off[p.num_experts] : p.tiles_y;
+  const int64_t total = (int64_t)tx * ty * (p.mode == 1 ? 1 : p.tiles_z);
+  auto tile_of = [&](int64_t t, int64_t& m_tile) {
+    m_tile = t % tx;
+    const int64_t r = t / tx;
+    return p.mode == 1 ? resolve_tile_at<BN>(p, (int)r, 0) : resolve_tile_at<BN>(p, (int)(r % ty), (int)(r / ty));
+  };
+
+  if (tid == 0) {
+    for (int s = 0; s < L::kStages; ++s) {
+      sm100::mbar_init(&sh->full[s], 1);
+      sm100::mbar_init(&sh->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      sm100::mbar_init(&sh->acc_full[b], 1);
+      sm100::mbar_init(&sh->acc_empty[b], kPEpiWarps);
+    }
+    sm100::fence_barrier_init();
+    sm100::prefetch_tmap(&tmA);
+    sm100::prefetch_tmap(&tmB);
+  }
+  if (warp == 1) sm100::tmem_alloc(&sh->tmem_base, L::kTmemCols);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = sh->tmem_base;
+
+  if (warp == 0 || warp == 2 || warp == 3) {
+    // ------------------------------------------------------------ producers
+    const int pidx = warp == 0 ? 0 : warp - 1;
+    const bool leader = sm100::elect_one();
+    int64_t g = 0;   // stage counter over all of this CTA's tiles
+    bool alive = true;
+    for (int64_t t = blockIdx.x; t < total && alive; t += gridDim.x) {
+      int64_t m_tile;
+      const TileInfo ti = tile_of(t, m_tile);
+      if (!ti.active) continue;
+      const int64_t a_row_base = ti.expert * p.n_out;
+      const int64_t m_tiles = p.n_out / 128;
+      const uint8_t* sfa_base = kF8 ? nullptr : p.sfa + ((ti.expert * m_tiles + m_tile) * kb_total) * 512;
+      const uint8_t* sfb_base = kF8 ? nullptr : p.sfb + (ti.tile * kb_total) * (size_t)L::kSfbAtoms * 512;
+      for (int kt = 0; kt < num_kt; ++kt, ++g) {
+        const int s = (int)(g % L::kStages);
+        if (s % kPProducers != pidx) continue;
+        const uint32_t ph = (uint32_t)((g / L::kStages) & 1);
+        if (!sm100::mbar_wait(&sh->empty[s], ph ^ 1, p.err, 61)) { alive = false; break; }
+        const int nkb = min(4, kb_total - kt * 4);
+        const uint32_t sfa_bytes = kF8 ? 0u : (uint32_t)nkb * 512;
+        const uint32_t sfb_bytes = kF8 ? 0u : (uint32_t)nkb * L::kSfbAtoms * 512;
+        const int32_t x = kt * kKTBytes;
+        if (leader) {
+          sm100::mbar_arrive_expect_tx(&sh->full[s], (uint32_t)(L::kA + L::kB) + sfa_bytes + sfb_bytes);
+          if constexpr (!kF8) {
+            bulk_g2s(stSFA(s), sfa_base + (size_t)kt * 4 * 512, sfa_bytes, &sh->full[s]);
+            bulk_g2s(stSFB(s), sfb_base + (size_t)kt * 4 * L::kSfbAtoms * 512, sfb_bytes, &sh->full[s]);
+          }
+          if (geglu) {
+            const int64_t n0 = m_tile * 64;
+            sm100::tma_load_2d(stA(s), &tmA, x, (int32_t)(a_row_base + n0), &sh->full[s]);
+            sm100::tma_load_2d(stA(s) + 64 * kKTBytes, &tmA, x, (int32_t)(a_row_base + p.n_out / 2 + n0),
+                               &sh->full[s]);
+          } else {
+            sm100::tma_load_2d(stA(s), &tmA, x, (int32_t)(a_row_base + m_tile * 128), &sh->full[s]);
+          }
+          sm100::tma_load_2d(stB(s), &tmB, x, (int32_t)ti.b_row0, &sh->full[s]);
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    const bool leader = sm100::elect_one();
+    const uint32_t idesc = kF8 ? sm100::idesc_f8(BN) : sm100::idesc_nvf4(BN);
+    int64_t g = 0;
+    int it = 0;
+    bool alive = true;
+    for (int64_t t = blockIdx.x; t < total && alive; t += gridDim.x) {
+      int64_t m_tile;
+      const TileInfo ti = tile_of(t, m_tile);
+      if (!ti.active) continue;
+      const int b = it & 1;
+      const uint32_t accp = (uint32_t)((it >> 1) & 1);
+      if (!sm100::mbar_wait(&sh->acc_empty[b], accp ^ 1, p.err, 62)) break;
+      sm100::tc_fence_after();
+      const uint32_t dcol = tmem + (uint32_t)b * L::kAccStride;
+      for (int kt = 0; kt < num_kt; ++kt, ++g) {
+        const int s = (int)(g % L::kStages);
+        const uint32_t ph = (uint32_t)((g / L::kStages) & 1);
+        if (!sm100::mbar_wait(&sh->full[s], ph, p.err, 63)) { alive = false; break; }
+        sm100::tc_fence_after();
+        const int nkb = min(4, kb_total - kt * 4);
+        if (leader) {
+          if constexpr (!kF8) {
+            for (int kb = 0; kb < nkb; ++kb) {
+              sm100::tc_cp_32x128b_warpx4(tmem + L::kSfaCol + 4 * kb,
+                                          sm100::sdesc_sf_atom(sm100::smem_u32(stSFA(s) + kb * 512)));
+#pragma unroll
+              for (int a = 0; a < L::kSfbAtoms; ++a)
+                sm100::tc_cp_32x128b_warpx4(
+                    tmem + L::kSfbCol + 4 * (kb * L::kSfbAtoms + a),
+                    sm100::sdesc_sf_atom(sm100::smem_u32(stSFB(s) + (kb * L::kSfbAtoms + a) * 512)));
+            }
+          }
+          for (int kb = 0; kb < nkb; ++kb) {
+            const uint64_t ad = sm100::sdesc_k_sw128(sm100::smem_u32(stA(s)) + kb * 32);
+            const uint64_t bd = sm100::sdesc_k_sw128(sm100::smem_u32(stB(s)) + kb * 32);
+            if constexpr (kF8)
+              sm100::tc_mma_f8(dcol, ad, bd, idesc, (kt | kb) ? 1u : 0u);
+            else
+              sm100::tc_mma_nvf4(dcol, ad, bd, idesc, tmem + L::kSfaCol + 4 * kb,
+                                 tmem + L::kSfbCol + 4 * kb * L::kSfbAtoms, (kt | kb) ? 1u : 0u);
+          }
+          sm100::tc_commit(&sh->empty[s]);
+        }
+        __syncwarp();
+      }
+      if (leader) sm100::tc_commit(&sh->acc_full[b]);
+      __syncwarp();
+      ++it;
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int row = 32 * q + lane;
+    constexpr int kHalf = BN >= 16 ? BN / 2 : BN;
+    const int hseg = (warp - 4) >> 2;
+    const int tbeg = hseg * kHalf, tend = min(BN, tbeg + kHalf);
+    constexpr int kChunk = kHalf < 32 ? kHalf : 32;
+    const int ncol = geglu ? 64 : 128;
+    const int es = (p.epi == kEpiStore && p.c_dt == AEOQ_F32) ? 4 : 2;
+    float* colscale = sh->colscale;
+    int it = 0;
+    for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+      int64_t m_tile;
+      const TileInfo ti = tile_of(t, m_tile);
+      if (!ti.active) continue;
+      const int b = it & 1;
+      const uint32_t accp = (uint32_t)((it >> 1) & 1);
+      ++it;
+      // the previous tile's exchange and column scales are no longer read
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * kPEpiWarps) : "memory");
+      float alpha = 1.0f;
+      if constexpr (kF8) {
+        const int64_t wrow = geglu ? (row < 64 ? m_tile * 64 + row : p.n_out / 2 + m_tile * 64 + (row - 64))
+                                   : m_tile * 128 + row;
+        alpha = p.sb_rows[ti.expert * p.n_out + wrow];
+        for (int c = tid - 128; c < BN; c += 32 * kPEpiWarps)
+          colscale[c] = c < ti.n_valid ? p.sa_rows[ti.b_row0 + c] : 0.0f;
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * kPEpiWarps) : "memory");
+      } else {
+        if (p.epi == kEpiScaleRow) alpha = p.grp_alpha_ts[ti.expert] * load_scalar_f(p.w_ts, p.w_ts_dt);
+        else alpha = load_scalar_f(p.a_ts, p.a_ts_dt) * load_scalar_f(p.w_ts, p.w_ts_dt);
+      }
+      auto scaled = [&](float acc, int c) { return kF8 ? (acc * colscale[c]) * alpha : acc * alpha; };
+      const bool ok = sm100::mbar_wait(&sh->acc_full[b], accp, p.err, 64);
+      sm100::tc_fence_after();
+      const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)b * L::kAccStride;
+      char* cbase = reinterpret_cast<char*>(p.c) + ti.slot * p.c_slot_stride;
+      const int64_t col_w = (int64_t)m_tile * ncol + 32 * (q & (geglu ? 1 : 3));
+      char* cwarp = cbase + ti.c_row0 * p.ldc + col_w * es;
+      uint32_t hkey = 0;
+      if (!geglu) {
+        for (int c0 = tbeg; c0 < tend; c0 += kChunk) {
+          float v[kChunk < 16 ? 16 : kChunk];
+          tmem_chunk<kChunk>(tq + (uint32_t)c0, v);
+#pragma unroll
+          for (int g8 = 0; g8 < kChunk; g8 += 8) {
+            const int t0 = c0 + g8;
+            float y[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int c = t0 + j;
+              float val = (c < ti.n_valid) ? scaled(v[g8 + j], c) : 0.0f;
+              if (p.epi == kEpiScaleRow && c < ti.n_valid) val = bf16r(val) * __bfloat162float(p.row_w[ti.c_row0 + c]);
+              y[j] = val;
+            }
+            if (!ok) continue;
+            if (es == 2) {
+              store_8tok_bf16(y, cwarp + t0 * p.ldc, p.ldc, ti.n_valid - t0, lane);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                if (t0 + j < ti.n_valid) *reinterpret_cast<float*>(cwarp + (t0 + j) * p.ldc + 4 * lane) = y[j];
+            }
+          }
+        }
+        sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&sh->acc_empty[b]);
+      } else {
+        if (row >= 64) {
+          for (int c0 = tbeg; c0 < tend; c0 += kChunk) {
+            float v[kChunk < 16 ? 16 : kChunk];
+            tmem_chunk<kChunk>(tq + (uint32_t)c0, v);
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j)
+              xchg[(row - 64) * BN + c0 + j] = __float2bfloat16_rn(scaled(v[j], c0 + j));
+          }
+          sm100::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) sm100::mbar_arrive(&sh->acc_empty[b]);
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * kPEpiWarps) : "memory");
+        if (q < 2) {
+          for (int c0 = tbeg; c0 < tend; c0 += kChunk) {
+            float v[kChunk < 16 ? 16 : kChunk];
+            tmem_chunk<kChunk>(tq + (uint32_t)c0, v);
+#pragma unroll
+            for (int g8 = 0; g8 < kChunk; g8 += 8) {
+              const int t0 = c0 + g8;
+              float y[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int c = t0 + j;
+                float hvf = 0.0f;
+                if (c < ti.n_valid) {
+                  const float gv = bf16r(scaled(v[g8 + j], c));
+                  const float u = __bfloat162float(xchg[row * BN + c]);
+                  const __nv_bfloat16 hv = __float2bfloat16_rn(bf16r(gelu_tanh(gv)) * u);
+                  hkey = max(hkey, In<AEOQ_BF16>::abs_key(hv));
+                  hvf = __bfloat162float(hv);
+                }
+                y[j] = hvf;
+              }
+              if (ok) store_8tok_bf16(y, cwarp + t0 * p.ldc, p.ldc, ti.n_valid - t0, lane);
+            }
+          }
+          sm100::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) sm100::mbar_arrive(&sh->acc_empty[b]);
+        }
+        if (p.grp_amax) {
+          hkey = warp_umax(hkey);
+          if (lane == 0 && hkey) atomicMax(p.grp_amax + ti.expert, hkey);
+        }
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, L::kTmemCols);
+  }
+}
+
+template <int BN, bool kF8>
+static int launch_persistent(const uint8_t* a, int64_t a_rows, const uint8_t* b, TcParams p, int grid_ctas,
+                             cudaStream_t st) {
+  using L = PLayout<BN, kF8>;
+  CUtensorMap ta, tb;
+  const int64_t row_bytes = kF8 ? p.K : p.K / 2;
+  int rc = make_tmap(&ta, a, a_rows, row_bytes, row_bytes, p.epi == kEpiGeglu ? 64 : 128);
+  if (rc) return rc;
+  rc = make_tmap(&tb, b, p.b_rows, row_bytes, row_bytes, BN);
+  if (rc) return rc;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_persistent_kernel<BN, kF8>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kBytes);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(AEOQ_ERR_CUDA, "tc_gemm_persistent: smem attribute: %s", cudaGetErrorString(e));
+    }
+    attr_set = true;
+  }
+  tc_gemm_persistent_kernel<BN, kF8><<<grid_ctas, kPThreads, L::kBytes, st>>>(ta, tb, p);
+  return check_launch(kF8 ? "tc_gemm_persistent_kernel<fp8>" : "tc_gemm_persistent_kernel");
+}
+
+static int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  }
+  return n;
 }
 
 // ---------------------------------------------------------------- host side
@@ -563,6 +1005,21 @@ int tc_gemm_dispatch(int bn, const uint8_t* a, int64_t a_rows, const uint8_t* b,
   return tc_gemm_dispatch_kind<false>(bn, a, a_rows, b, p, grid, st);
 }
 
+// Persistent launch over the tile grid `grid` (x: weight tiles, y: token
+// tiles, z: slots; mode 1 reads the token-tile count on the device).
+template <bool kF8>
+int tc_gemm_persistent(int bn, const uint8_t* a, int64_t a_rows, const uint8_t* b, TcParams p, dim3 grid,
+                       cudaStream_t st) {
+  p.tiles_x = (int)grid.x;
+  p.tiles_y = (int)grid.y;
+  p.tiles_z = (int)grid.z;
+  const int64_t total = (int64_t)grid.x * grid.y * grid.z;
+  const int ctas = (int)std::min<int64_t>(sm_count(), std::max<int64_t>(1, total));
+  if (bn == 224) return launch_persistent<224, kF8>(a, a_rows, b, p, ctas, st);
+  if (bn == 128) return launch_persistent<128, kF8>(a, a_rows, b, p, ctas, st);
+  return set_error(AEOQ_ERR_INVALID, "tc_gemm_persistent: unsupported tile N %d", bn);
+}
+
 int pick_bn(int64_t M) {
   if (M <= 8) return 8;
   if (M <= 16) return 16;
@@ -580,6 +1037,9 @@ using namespace aeoq;
 // would leave SMs idle (each halving adds CTAs that re-read the weight tile
 // from L2, which is cheaper than idle HBM bandwidth).
 extern "C" int aeoq_nvfp4_tile_n(int64_t M, int64_t N, int64_t slots) {
+  // Problems of two or more waves of 224-token tiles take the persistent
+  // kernel (double-buffered accumulator, epilogue under the next main loop).
+  if ((N / 128) * (slots > 0 ? slots : 1) * ((M + 223) / 224) >= 2 * 148) return 224;
   int bn = pick_bn(M);
   const int64_t base = (N / 128) * (slots > 0 ? slots : 1);
   while (bn > 8 && base * ((M + bn - 1) / bn) < 148) bn >>= 1;
@@ -599,8 +1059,9 @@ extern "C" int aeoq_nvfp4_gemm_tc(const uint8_t* a, const uint8_t* a_sf_atoms, c
                (long long)K);
   AEOQ_REQUIRE((K / 2) % 16 == 0, AEOQ_ERR_INVALID, "nvfp4_gemm_tc: K/2 must be a multiple of 16");
   AEOQ_REQUIRE(c_dtype == AEOQ_BF16 || c_dtype == AEOQ_F32, AEOQ_ERR_INVALID, "nvfp4_gemm_tc: bad output dtype");
-  AEOQ_REQUIRE(tile_n == 8 || tile_n == 16 || tile_n == 32 || tile_n == 64 || tile_n == 128 || tile_n == 256,
-               AEOQ_ERR_INVALID, "nvfp4_gemm_tc: tile_n %d must be a power of two in [8, 256]", tile_n);
+  AEOQ_REQUIRE(tile_n == 8 || tile_n == 16 || tile_n == 32 || tile_n == 64 || tile_n == 128 || tile_n == 224 ||
+                   tile_n == 256,
+               AEOQ_ERR_INVALID, "nvfp4_gemm_tc: tile_n %d must be 224 or a power of two in [8, 256]", tile_n);
   if (slots * M * N == 0) return AEOQ_OK;
   AEOQ_REQUIRE(a && a_sf_atoms && a_ts && w && w_sf_atoms && w_ts && c && err_word, AEOQ_ERR_INVALID,
                "nvfp4_gemm_tc: null pointer");
@@ -630,6 +1091,7 @@ extern "C" int aeoq_nvfp4_gemm_tc(const uint8_t* a, const uint8_t* a_sf_atoms, c
   p.c_slot_stride = M * N * es;
   p.err = err_word;
   dim3 grid((unsigned)(N / 128), (unsigned)((M + tile_n - 1) / tile_n), (unsigned)slots);
+  if (tile_n == 224) return tc_gemm_persistent<false>(tile_n, w, num_experts * N, a, p, grid, (cudaStream_t)stream);
   return tc_gemm_dispatch(tile_n, w, num_experts * N, a, p, grid, (cudaStream_t)stream);
 }
 
@@ -678,6 +1140,7 @@ extern "C" int aeoq_nvfp4_gemm_grouped(const uint8_t* b, const uint8_t* b_sf, in
   const int64_t max_tiles = (max_rows + tile_n - 1) / tile_n + num_experts;
   const unsigned gx = (unsigned)(epi == kEpiGeglu ? (N / 2) / 64 : N / 128);
   dim3 grid(gx, (unsigned)max_tiles, 1);
+  if (tile_n == 128) return tc_gemm_persistent<false>(tile_n, w, num_experts * N, b, p, grid, (cudaStream_t)stream);
   return tc_gemm_dispatch(tile_n, w, num_experts * N, b, p, grid, (cudaStream_t)stream);
 }
 
@@ -710,6 +1173,7 @@ extern "C" int aeoq_fp8_gemm(const uint8_t* a, const float* sa, int64_t M, const
   p.sb_rows = sb;
   p.err = err_word;
   dim3 grid((unsigned)(N / 128), (unsigned)((M + tile_n - 1) / tile_n), 1);
+  if (tile_n == 224) return tc_gemm_persistent<true>(tile_n, w, N, a, p, grid, (cudaStream_t)stream);
   return tc_gemm_dispatch_kind<true>(tile_n, w, N, a, p, grid, (cudaStream_t)stream);
 }
 
@@ -752,5 +1216,6 @@ extern "C" int aeoq_fp8_gemm_grouped(const uint8_t* b, const float* sa_rows, int
   const int64_t max_tiles = (max_rows + tile_n - 1) / tile_n + num_experts;
   const unsigned gx = (unsigned)(epi == kEpiGeglu ? (N / 2) / 64 : N / 128);
   dim3 grid(gx, (unsigned)max_tiles, 1);
+  if (tile_n == 128) return tc_gemm_persistent<true>(tile_n, w, num_experts * N, b, p, grid, (cudaStream_t)stream);
   return tc_gemm_dispatch_kind<true>(tile_n, w, num_experts * N, b, p, grid, (cudaStream_t)stream);
 }
