@@ -578,10 +578,10 @@ int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int64_t row_bytes, 
 // lane quadrant) overlaps the main loop of tile i + 1.
 //   warps 0, 2, 3   producers (ring slot s is filled by producer s % 3)
 //   warp 1          TMEM owner + MMA issuer
-//   warps 4 .. 11   epilogue
-constexpr int kPThreads = 384;
+//   warps 4 .. 19   epilogue (four per TMEM lane quadrant)
+constexpr int kPEpiWarps = 16;
+constexpr int kPThreads = 128 + 32 * kPEpiWarps;
 constexpr int kPProducers = 3;
-constexpr int kPEpiWarps = 8;
 
 template <int BN, bool kF8>
 struct PLayout {
@@ -708,19 +708,35 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
     int64_t g = 0;
     int it = 0;
     bool alive = true;
+#ifdef AEOQ_TC_TRACE
+    long long w_acc = 0, w_full = 0, w_issue = 0;
+#endif
     for (int64_t t = blockIdx.x; t < total && alive; t += gridDim.x) {
       int64_t m_tile;
       const TileInfo ti = tile_of(t, m_tile);
       if (!ti.active) continue;
       const int b = it & 1;
       const uint32_t accp = (uint32_t)((it >> 1) & 1);
+#ifdef AEOQ_TC_TRACE
+      long long c0_ = clock64();
+#endif
       if (!sm100::mbar_wait(&sh->acc_empty[b], accp ^ 1, p.err, 62)) break;
+#ifdef AEOQ_TC_TRACE
+      w_acc += clock64() - c0_;
+#endif
       sm100::tc_fence_after();
       const uint32_t dcol = tmem + (uint32_t)b * L::kAccStride;
       for (int kt = 0; kt < num_kt; ++kt, ++g) {
         const int s = (int)(g % L::kStages);
         const uint32_t ph = (uint32_t)((g / L::kStages) & 1);
+#ifdef AEOQ_TC_TRACE
+        const long long c1_ = clock64();
+#endif
         if (!sm100::mbar_wait(&sh->full[s], ph, p.err, 63)) { alive = false; break; }
+#ifdef AEOQ_TC_TRACE
+        const long long c2_ = clock64();
+        w_full += c2_ - c1_;
+#endif
         sm100::tc_fence_after();
         const int nkb = min(4, kb_total - kt * 4);
         if (leader) {
@@ -747,23 +763,35 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
           sm100::tc_commit(&sh->empty[s]);
         }
         __syncwarp();
+#ifdef AEOQ_TC_TRACE
+        w_issue += clock64() - c2_;
+#endif
       }
       if (leader) sm100::tc_commit(&sh->acc_full[b]);
       __syncwarp();
       ++it;
     }
+#ifdef AEOQ_TC_TRACE
+    if (p.trace && lane == 0) { p.trace[blockIdx.x * 8 + 1] = w_acc; p.trace[blockIdx.x * 8 + 2] = w_full; p.trace[blockIdx.x * 8 + 3] = w_issue; p.trace[blockIdx.x * 8 + 4] = it; }
+#endif
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int row = 32 * q + lane;
-    constexpr int kHalf = BN >= 16 ? BN / 2 : BN;
+    // the four warps of a quadrant split the tile's tokens (segments of a
+    // multiple of 8 tokens)
+    constexpr int kSegs = kPEpiWarps / 4;
+    constexpr int kSeg = ((BN + 8 * kSegs - 1) / (8 * kSegs)) * 8;
     const int hseg = (warp - 4) >> 2;
-    const int tbeg = hseg * kHalf, tend = min(BN, tbeg + kHalf);
-    constexpr int kChunk = kHalf < 32 ? kHalf : 32;
+    const int tbeg = hseg * kSeg, tend = min(BN, tbeg + kSeg);
+    constexpr int kChunk = kSeg < 32 ? kSeg : 32;
     const int ncol = geglu ? 64 : 128;
     const int es = (p.epi == kEpiStore && p.c_dt == AEOQ_F32) ? 4 : 2;
     float* colscale = sh->colscale;
     int it = 0;
+#ifdef AEOQ_TC_TRACE
+    long long e_wait = 0, e_work = 0;
+#endif
     for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
       int64_t m_tile;
       const TileInfo ti = tile_of(t, m_tile);
@@ -786,7 +814,14 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
         else alpha = load_scalar_f(p.a_ts, p.a_ts_dt) * load_scalar_f(p.w_ts, p.w_ts_dt);
       }
       auto scaled = [&](float acc, int c) { return kF8 ? (acc * colscale[c]) * alpha : acc * alpha; };
+#ifdef AEOQ_TC_TRACE
+      const long long d0_ = clock64();
+#endif
       const bool ok = sm100::mbar_wait(&sh->acc_full[b], accp, p.err, 64);
+#ifdef AEOQ_TC_TRACE
+      const long long d1_ = clock64();
+      e_wait += d1_ - d0_;
+#endif
       sm100::tc_fence_after();
       const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)b * L::kAccStride;
       char* cbase = reinterpret_cast<char*>(p.c) + ti.slot * p.c_slot_stride;
@@ -800,6 +835,7 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
 #pragma unroll
           for (int g8 = 0; g8 < kChunk; g8 += 8) {
             const int t0 = c0 + g8;
+            if (t0 >= tend) break;
             float y[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -828,7 +864,7 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
             tmem_chunk<kChunk>(tq + (uint32_t)c0, v);
 #pragma unroll
             for (int j = 0; j < kChunk; ++j)
-              xchg[(row - 64) * BN + c0 + j] = __float2bfloat16_rn(scaled(v[j], c0 + j));
+              if (c0 + j < tend) xchg[(row - 64) * BN + c0 + j] = __float2bfloat16_rn(scaled(v[j], c0 + j));
           }
           sm100::tc_fence_before();
           __syncwarp();
@@ -842,6 +878,7 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
 #pragma unroll
             for (int g8 = 0; g8 < kChunk; g8 += 8) {
               const int t0 = c0 + g8;
+              if (t0 >= tend) break;
               float y[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
@@ -868,7 +905,13 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
           if (lane == 0 && hkey) atomicMax(p.grp_amax + ti.expert, hkey);
         }
       }
+#ifdef AEOQ_TC_TRACE
+      e_work += clock64() - d1_;
+#endif
     }
+#ifdef AEOQ_TC_TRACE
+    if (p.trace && tid == 128) { p.trace[blockIdx.x * 8 + 5] = e_wait; p.trace[blockIdx.x * 8 + 6] = e_work; }
+#endif
   }
   sm100::tc_fence_before();
   __syncthreads();
@@ -898,6 +941,9 @@ static int launch_persistent(const uint8_t* a, int64_t a_rows, const uint8_t* b,
     }
     attr_set = true;
   }
+#ifdef AEOQ_TC_TRACE
+  if (const char* tp = getenv("AEOQ_TC_TRACE_PTR")) p.trace = reinterpret_cast<uint64_t*>(strtoull(tp, nullptr, 10));
+#endif
   tc_gemm_persistent_kernel<BN, kF8><<<grid_ctas, kPThreads, L::kBytes, st>>>(ta, tb, p);
   return check_launch(kF8 ? "tc_gemm_persistent_kernel<fp8>" : "tc_gemm_persistent_kernel");
 }

@@ -57,6 +57,7 @@ def parse():
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
+    p.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM measurements")
     p.add_argument("--workload", default="decode", choices=["decode", "ep"],
                    help="decode: config 1 (default); ep: config 4, expert-parallel prefill stack")
     p.add_argument("--tokens", type=int, default=32 * 2048, help="ep: tokens over all ranks")
@@ -226,6 +227,73 @@ def run_reference(args, rank):
         "cpu_baseline": cb,
         "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+def _graph_time_us(torch, dev, fn, iters):
+    """Mean device time of fn over one CUDA graph of `iters` calls (after warm-up)."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    sg = torch.cuda.Stream(dev)
+    sg.wait_stream(torch.cuda.current_stream(dev))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(sg):
+        fn()
+        with torch.cuda.graph(g, stream=sg):
+            for _ in range(iters):
+                fn()
+    torch.cuda.current_stream(dev).wait_stream(sg)
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1000.0 / iters
+
+
+def measure_prefill(torch, dev, lib, A):
+    """Config 0 (NVFP4 linear N=1408, K=2816) at M = 128 and at prefill sizes,
+    and the config-2 FP8 expert prefill (4096 tokens, top-8), through the
+    public API, as CUDA-graph replays. FP4/FP8 fractions are of the nominal
+    dense peaks (9 / 4.5 PFLOP/s): no measured FP4/FP8 peak exists."""
+    from aeo_quant_b200.bridges.gemma4 import moe_ops
+    from aeo_quant_b200.gpu import nvfp4_matmul as NM
+    from aeo_quant_b200.gpu import quant as Q
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = (torch.randn(1408, 2816, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    wp, wsf, wts = Q.quantize_2d_to_nvfp4(w)
+    wts = wts.float()
+    out = {}
+    for M in (128, 8192, 32768):
+        x = torch.randn(M, 2816, generator=g, device=dev).to(torch.bfloat16)
+        ap, asf, ats = Q.quantize_2d_to_nvfp4(x)
+        us = _graph_time_us(torch, dev, lambda: NM.nvfp4_linear_prequantized(ap, asf, ats, wp, wsf, wts),
+                            20 if M < 32768 else 10)
+        tf = 2.0 * M * 1408 * 2816 / us / 1e6
+        out[f"config0_M{M}"] = {"us": round(us, 2), "tflops": round(tf, 1), "frac_fp4_nominal": round(tf / 9000, 4)}
+    T, k = 4096, TOPK
+    gq, gs = Q.quantize_3d_to_fp8((torch.randn(E, 2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+    dq, ds = Q.quantize_3d_to_fp8((torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+    gsb, dsb = gs.reshape(-1).float().contiguous(), ds.reshape(-1).float().contiguous()
+    h = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    logits = torch.randn(T, E, generator=g, device=dev)
+    wv, ids = torch.topk(torch.softmax(logits, -1), k, dim=-1)
+    wts8 = (wv / wv.sum(-1, keepdim=True)).to(torch.bfloat16)
+    us = _graph_time_us(torch, dev, lambda: moe_ops.fp8_experts_grouped(h, ids, wts8, gq, gsb, dq, dsb), 5)
+    tf = T * k * 11894784 / us / 1e6
+    out["config2_fp8_T4096"] = {"us": round(us, 1), "tflops": round(tf, 1), "frac_fp8_nominal": round(tf / 4500, 4)}
+    del gq, dq
+    gp, gsf, gt = Q.quantize_3d_to_nvfp4((torch.randn(E, 2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+    dp, dsf, dt = Q.quantize_3d_to_nvfp4((torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+    us = _graph_time_us(torch, dev, lambda: moe_ops.nvfp4_experts_grouped(h, ids, wts8, gp, gsf, gt.float(), dp, dsf,
+                                                                          dt.float()), 5)
+    tf = T * k * 11894784 / us / 1e6
+    out["config2_shapes_nvfp4_T4096"] = {"us": round(us, 1), "tflops": round(tf, 1),
+                                         "frac_fp4_nominal": round(tf / 9000, 4)}
+    return out
 
 
 def main_ep(args, rank, world, local):
@@ -454,6 +522,9 @@ def main():
         stage_ms["fused"] = time_graph(lib.aeoq_moe_nvfp4_decode_fused, fws, fws_n)
         stage_ms["unfused"] = time_graph(lib.aeoq_moe_nvfp4_decode, uws, uws_n)
 
+    # ---- prefill: config-0 GEMMs and the config-2 FP8 expert prefill ----
+    prefill = measure_prefill(torch, dev, lib, A) if (B == 1 and not args.no_prefill) else None
+
     # ---- end to end through the public module API with host buffers ----
     hid_h = hid.pin_memory()
     idx_h = idx.pin_memory()
@@ -525,6 +596,7 @@ def main():
                     "d2h_bytes_per_step": B * H * 2,
                     "path": "Gemma4TextExpertsNVFP4.forward eager, pinned host in/out, sync per step"},
             "roofline": roof,
+            "prefill": prefill,
         }
         if world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
