@@ -38,7 +38,9 @@
 //            The k CTAs of a row tile form a cluster; each sums a slice of
 //            the rows over the k CTAs' shared memory in f32 in expert order
 //            and rounds once (:184-186).
-// Every wait is bounded (sm100::mbar_wait); TMEM is freed on every path.
+// Every mbarrier wait is bounded (sm100::mbar_wait); TMEM is freed on every
+// path, and before any wait on another CTA (a cluster barrier), so that no
+// CTA blocked in tcgen05.alloc can be part of a wait cycle.
 #include <cuda.h>
 
 #include <algorithm>
@@ -50,6 +52,8 @@ namespace aeoq {
 
 int make_tmap_bytes(CUtensorMap* m, const void* ptr, int64_t rows, int64_t row_bytes, int64_t ld, int box_bytes,
                     int box_rows, bool swizzle128);
+int make_tmap_nd(CUtensorMap* m, const void* ptr, int rank, const int64_t* dims, const int64_t* strides,
+                 const int* box, bool swizzle128);
 
 namespace dtc {
 
@@ -73,8 +77,9 @@ __device__ uint64_t* g_dtrace = nullptr;
 #define TRACE_BASE(v)
 #endif
 
-constexpr int kThreads = 192;
-constexpr int kRing = 3;      // launch-1 weight ring depth
+constexpr int kThreads = 192;      // launch 2
+constexpr int kThreads1 = 256;     // launch 1: two more producer warps (6, 7)
+constexpr int kRing = 3;           // launch-1 weight ring depth (one producer warp per slot)
 
 __host__ __device__ constexpr int rup(int v, int m) { return (v + m - 1) / m * m; }
 
@@ -105,16 +110,16 @@ struct Args {
 
 // ---- shared-memory layouts (offsets from a 1024-aligned base)
 struct L1 {
-  int a, ring, stage, hid, sf, sfchunk, tok, dv, bars, bytes;
+  int a, ring, stage, hid, sf, sfrow, tok, dv, bars, bytes;
   __host__ __device__ explicit L1(const Plan& p) {
     const int nt = p.Q / 4;
     a = 0;                                   // nt token tiles of 1 KB
     ring = 1024 * nt;
     stage = 2 * p.T * 128;
     hid = ring + kRing * stage;
-    sfchunk = 2 * p.T * 16;                  // per 4 K steps: gate rows, then up rows, 16 B each
+    sfrow = 4 * p.Q;                         // scale rows: gate rows, then up rows, 4Q bytes each
     sf = rup(hid + 2 * p.H, 128);
-    tok = rup(sf + nt * sfchunk, 16);        // token scale bytes, 4 per K step
+    tok = rup(sf + 2 * p.T * sfrow, 16);     // token scale bytes, 4 per K step
     dv = rup(tok + 4 * p.Q, 16);             // 2T f32 accumulator row
     bars = rup(dv + 8 * p.T, 16);
     bytes = bars + 256;
@@ -208,6 +213,34 @@ __device__ __forceinline__ void st_weight_scales_chunked(uint32_t taddr, const u
   }
 }
 
+// Same, from row-major scale rows of row_bytes (a multiple of 16): each lane
+// reads a row's four steps with one 16-byte load.
+__device__ __forceinline__ void st_weight_scales_rows16(uint32_t taddr, const uint8_t* sf, int row_bytes, int n_rows,
+                                                        int nkb, int lane) {
+  for (int c = 0; c < (nkb + 3) / 4; ++c) {
+    uint4 v[2][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int row = 128 * a + 32 * i + lane;
+        v[a][i] = *reinterpret_cast<const uint4*>(sf + (row < n_rows ? row : 0) * row_bytes + 16 * c);
+        if (row >= n_rows) v[a][i] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    uint32_t r[32];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        r[0 * 8 + 4 * a + i] = v[a][i].x;
+        r[1 * 8 + 4 * a + i] = v[a][i].y;
+        r[2 * 8 + 4 * a + i] = v[a][i].z;
+        r[3 * 8 + 4 * a + i] = v[a][i].w;
+      }
+    sm100::tmem_st32(taddr + 32 * c, r);
+  }
+}
+
 // Same, from row-major scale rows of sfrow bytes (a multiple of 4; words
 // past a row's last K step are read but not used by any MMA).
 __device__ __forceinline__ void st_weight_scales_rows(uint32_t taddr, const uint8_t* sf, int sfrow, int n_rows,
@@ -256,7 +289,7 @@ __device__ __forceinline__ uint32_t block_max128(uint32_t key, int t, uint32_t* 
 }
 
 // ------------------------------------------------------------------ launch 1
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads1, 1)
     decode_gateup_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmS,
                             const Args a, const Plan pl) {
   TRACE_BASE(0);
@@ -297,21 +330,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_wait();        // inputs may come from the preceding kernel
   const int64_t e = load_index(a.ids, a.ids_dt, j);
   const bool valid = e >= 0 && e < pl.E;
-  const int32_t row_g = (int32_t)((valid ? e : 0) * 2 * I + (int64_t)T * m);
   float alpha = 0.0f;
 
-  if (warp == 0) {
+  if (warp == 0 || warp >= 6) {
+    // ---- producers: warp 0 (ring slot 0, plus the hidden vector, the
+    // scales and the weight scales' TMEM copy), warps 6 and 7 (slots 1, 2).
+    // One warp's copies complete one after another, so the slots go to
+    // different warps. Tensor maps: weights (H/2, I, gate|up, E) and scales
+    // (H/16, I, gate|up, E), so one box brings a stage's gate and up rows.
+    const int slot = warp == 0 ? 0 : warp - 5;
     const bool leader = sm100::elect_one();
-    if (leader) {
+    if (warp == 0 && leader) {
       // the hidden vector first: the quantization waits on it, the MMAs on that
       sm100::mbar_arrive_expect_tx(&sh->hid, (uint32_t)(2 * H));
       bulk_g2s(base + L.hid, a.hidden, (uint32_t)(2 * H), &sh->hid);
       if (valid) {
-        sm100::mbar_arrive_expect_tx(&sh->sf, (uint32_t)(nt * L.sfchunk));
-        for (int c = 0; c < nt; ++c) {
-          sm100::tma_load_2d(sfs + c * L.sfchunk, &tmS, 4 * kb0 + 16 * c, row_g, &sh->sf);
-          sm100::tma_load_2d(sfs + c * L.sfchunk + 16 * T, &tmS, 4 * kb0 + 16 * c, row_g + I, &sh->sf);
-        }
+        sm100::mbar_arrive_expect_tx(&sh->sf, (uint32_t)(2 * T * L.sfrow));
+        sm100::tma_load_4d(sfs, &tmS, 4 * kb0, T * m, 0, (int32_t)e, &sh->sf);
       }
     }
     __syncwarp();
@@ -320,32 +355,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the MMAs cannot start before the quantization they feed.
     bool go = sm100::mbar_wait(&sh->hid, 0, a.err, 47);
     if (valid) go = go && sm100::mbar_wait(&sh->sf, 0, a.err, 48);
-    bool triggered = false;
-    for (int kt = 0; kt < nt && valid && go; ++kt) {
-      const int s = kt % kRing;
+    bool done_first = false;
+    for (int kt = slot; kt < nt && valid && go; kt += kRing) {
       const uint32_t ph = (kt / kRing) & 1;
-      if (!sm100::mbar_wait(&sh->empty[s], ph ^ 1, a.err, 41)) break;
+      if (!sm100::mbar_wait(&sh->empty[slot], ph ^ 1, a.err, 41)) break;
       if (leader) {
-        const int32_t x = 32 * kb0 + 128 * kt;
-        sm100::mbar_arrive_expect_tx(&sh->full[s], (uint32_t)L.stage);
-        sm100::tma_load_2d(ring + s * L.stage, &tmW, x, row_g, &sh->full[s]);
-        sm100::tma_load_2d(ring + s * L.stage + T * 128, &tmW, x, row_g + I, &sh->full[s]);
+        sm100::mbar_arrive_expect_tx(&sh->full[slot], (uint32_t)L.stage);
+        sm100::tma_load_4d(ring + slot * L.stage, &tmW, 32 * kb0 + 128 * kt, T * m, 0, (int32_t)e, &sh->full[slot]);
       }
       __syncwarp();
-      if (!triggered && kt + 1 >= min(kRing, nt)) {
+      if (warp == 0 && !done_first) {
+        done_first = true;
         pdl_trigger();   // the down launch may start its prefetch now
-        triggered = true;
-        // Until the MMAs free a stage this warp is idle: it writes the
+        // Until the MMAs free its slot this warp is idle: it writes the
         // weight scales (lane quadrant 0, the only one accumulator row 0
         // reads), in parallel with the quantization of the hidden vector.
-        st_weight_scales_chunked(tmem + pl.sfb1, sfs, L.sfchunk, N1, nkb, lane);
+        st_weight_scales_rows16(tmem + pl.sfb1, sfs, L.sfrow, N1, nkb, lane);
         sm100::tmem_st_wait();
         sm100::tc_fence_before();
         __syncwarp();
         if (lane == 0) sm100::mbar_arrive(&sh->bready);
       }
     }
-    if (!triggered) {
+    if (warp == 0 && !done_first) {
       pdl_trigger();
       if (lane == 0) sm100::mbar_arrive(&sh->bready);
     }
@@ -375,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (leader) sm100::tc_commit(&sh->accum);
     __syncwarp();
   } else {
-    // ---- warps 2-5: quantize, scales into TMEM, then the epilogue
+    // ---- warps 2-5: quantize, token scales into TMEM, then the epilogue
     const int t = tid - 64;
     const uint32_t qaddr = (uint32_t)(32 * (warp & 3)) << 16;
     const bool hid_ok = sm100::mbar_wait(&sh->hid, 0, a.err, 44);
@@ -413,11 +445,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (t == 0) DT(3);
     if (warp == 4) read_row0(tmem, N1, ok && valid, dv, lane);
   }
+  // TMEM is released before any wait on another CTA: a CTA blocked in
+  // tcgen05.alloc behind this one must never be what this one waits for.
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, (uint32_t)pl.cols1);
+  }
   // The K parts of a tile form one cluster: rank 0 adds the parts' rows (in
   // part order, from each CTA's shared memory) and finishes the tile.
-  sm100::tc_fence_before();
   sm100::cluster_sync();
-  if (warp >= 2 && sm100::cluster_ctarank() == 0) {
+  if (warp >= 2 && warp < 6 && sm100::cluster_ctarank() == 0) {   // the four epilogue warps
     const int t = tid - 64;
     if (t == 0) DT(9);
     uint32_t hkey = 0;
@@ -441,11 +480,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   sm100::cluster_sync();   // every part's row has been read
-  __syncthreads();
-  if (warp == 1) {
-    sm100::tc_fence_after();
-    sm100::tmem_dealloc(tmem, (uint32_t)pl.cols1);
-  }
 }
 
 // ------------------------------------------------------------------ launch 2
@@ -477,11 +511,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   // The ids, the down weights and their scales do not depend on launch 1.
   const int64_t e = load_index(a.ids, a.ids_dt, j);
   const bool valid = e >= 0 && e < pl.E;
-  if (warp == 0 && valid && sm100::elect_one()) {
+  // Loads spread over warps 0, 2, 3, 4, 5 (one warp's copies complete one
+  // after another); warp 0 posts the expected bytes. A copy that completes
+  // first leaves the transaction count below zero until then.
+  if (valid && warp != 1) {
+    const int pw = warp == 0 ? 0 : warp - 1;   // 0..4
     const int32_t row0 = (int32_t)(e * H + (int64_t)N2 * t2);
-    sm100::mbar_arrive_expect_tx(&sh->full, (uint32_t)(nt * N2 * 128 + N2 * L.sfrow));
-    bulk_g2s(sfs, a.d_sf + (int64_t)row0 * L.sfrow, (uint32_t)(N2 * L.sfrow), &sh->full);
-    for (int kt = 0; kt < nt; ++kt) sm100::tma_load_2d(btile + kt * N2 * 128, &tmD, 128 * kt, row0, &sh->full);
+    if (sm100::elect_one()) {
+      if (pw == 0) {
+        sm100::mbar_arrive_expect_tx(&sh->full, (uint32_t)(nt * N2 * 128 + N2 * L.sfrow));
+        bulk_g2s(sfs, a.d_sf + (int64_t)row0 * L.sfrow, (uint32_t)(N2 * L.sfrow), &sh->full);
+      }
+      for (int kt = 0; kt < nt; ++kt)
+        if ((kt + 1) % 5 == pw) sm100::tma_load_2d(btile + kt * N2 * 128, &tmD, 128 * kt, row0, &sh->full);
+    }
+    __syncwarp();
   }
   // May wait until a launch-1 CTA on this SM releases its columns.
   if (warp == 1) sm100::tmem_alloc(&sh->tmem, (uint32_t)pl.cols2);
@@ -555,10 +599,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("bar.sync 2, 128;" ::: "memory");
     for (int i = t; i < N2; i += 128) dv[i] = bf16r(bf16r(dv[i] * alpha) * wj);
   }
+  // TMEM is released before any wait on another CTA (see launch 1).
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, (uint32_t)pl.cols2);
+  }
   // The k experts of a row tile form one cluster: CTA rank r sums rows
   // [r*R, r*R + R) over the k CTAs' shared memory in expert order (f32, one
   // rounding) and writes them.
-  sm100::tc_fence_before();
   sm100::cluster_sync();
   if (warp >= 2) {
     const int t = tid - 64;
@@ -572,11 +622,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (t == 0) DT(4);
   }
   sm100::cluster_sync();   // every CTA's rows have been read
-  __syncthreads();
-  if (warp == 1) {
-    sm100::tc_fence_after();
-    sm100::tmem_dealloc(tmem, (uint32_t)pl.cols2);
-  }
 }
 
 constexpr int kSmemLimit = 232448 - 1024;
@@ -679,10 +724,17 @@ extern "C" int aeoq_moe_nvfp4_decode_tc(const void* hidden, const void* top_k_in
   const int64_t E = num_experts, H = hidden_dim, I = inter_dim;
   cudaStream_t st = (cudaStream_t)stream;
   CUtensorMap tw, ts, td;
-  int rc = make_tmap_bytes(&tw, gate_up, E * 2 * I, H / 2, H / 2, 128, pl.T, true);
-  if (rc) return rc;
-  rc = make_tmap_bytes(&ts, gate_up_sf, E * 2 * I, H / 16, H / 16, 16, pl.T, false);
-  if (rc) return rc;
+  {
+    const int64_t dw[4] = {H / 2, I, 2, E}, sw[3] = {H / 2, I * (H / 2), 2 * I * (H / 2)};
+    const int bw[4] = {128, pl.T, 2, 1};
+    int rc = make_tmap_nd(&tw, gate_up, 4, dw, sw, bw, true);
+    if (rc) return rc;
+    const int64_t ds[4] = {H / 16, I, 2, E}, ss[3] = {H / 16, I * (H / 16), 2 * I * (H / 16)};
+    const int bs[4] = {4 * pl.Q, pl.T, 2, 1};
+    rc = make_tmap_nd(&ts, gate_up_sf, 4, ds, ss, bs, false);
+    if (rc) return rc;
+  }
+  int rc = 0;
   rc = make_tmap_bytes(&td, down, E * H, I / 2, I / 2, 128, pl.N2, true);
   if (rc) return rc;
   dtc::Ws w = dtc::layout(workspace, pl);
@@ -732,7 +784,7 @@ extern "C" int aeoq_moe_nvfp4_decode_tc(const void* hidden, const void* top_k_in
   attr2[1].val.clusterDim.z = 1;
   cudaLaunchConfig_t c1 = {};
   c1.gridDim = dim3((unsigned)pl.tiles, (unsigned)pl.parts, (unsigned)top_k);
-  c1.blockDim = dim3(dtc::kThreads);
+  c1.blockDim = dim3(dtc::kThreads1);
   c1.dynamicSmemBytes = s1;
   c1.stream = st;
   c1.attrs = attr1;
@@ -744,6 +796,7 @@ extern "C" int aeoq_moe_nvfp4_decode_tc(const void* hidden, const void* top_k_in
   }
   cudaLaunchConfig_t c2 = c1;
   c2.gridDim = dim3((unsigned)(H / pl.N2), (unsigned)top_k);
+  c2.blockDim = dim3(dtc::kThreads);
   c2.dynamicSmemBytes = s2;
   c2.attrs = attr2;
   e = cudaLaunchKernelEx(&c2, dtc::decode_down_tc_kernel, td, a, pl);

@@ -43,7 +43,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Spin limit for every wait in the tensor-core kernels. A healthy wait
 // completes in well under a millisecond; the limit corresponds to seconds.
-constexpr uint32_t kSpinLimit = 1u << 26;
+#ifndef AEOQ_SPIN_LIMIT
+#define AEOQ_SPIN_LIMIT (1u << 26)
+#endif
+constexpr uint32_t kSpinLimit = AEOQ_SPIN_LIMIT;
 
 // Bounded wait: returns false (and records `code` in *err) on timeout.
 // mbarrier.try_wait already suspends the thread for a hardware-chosen
@@ -102,6 +105,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+// 4D tile load (coordinates innermost first).
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int32_t c0, int32_t c1, int32_t c2,
+                                            int32_t c3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
       : "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {

@@ -1000,6 +1000,27 @@ int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int64_t row_bytes, 
   return make_tmap_bytes(m, ptr, rows, row_bytes, ld, kKTBytes, box_rows, true);
 }
 
+// Byte tensor map of rank 2..5: dims[0] innermost (bytes), strides[i] the
+// byte pitch of dims[i + 1], box[] the tile extents.
+int make_tmap_nd(CUtensorMap* m, const void* ptr, int rank, const int64_t* dims, const int64_t* strides,
+                 const int* box, bool swizzle128) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(AEOQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = (cuuint64_t)dims[i];
+    b[i] = (cuuint32_t)box[i];
+    e[i] = 1;
+    if (i + 1 < rank) st[i] = (cuuint64_t)strides[i];
+  }
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, (cuuint32_t)rank, const_cast<void*>(ptr), d, st, b, e,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(AEOQ_ERR_INVALID, "tensor map (rank %d) encode failed (%d)", rank, (int)r);
+  return AEOQ_OK;
+}
+
 template <int BN, bool kF8>
 static int launch_tc(const uint8_t* a, int64_t a_rows, const uint8_t* b, const TcParams& p, dim3 grid,
                      cudaStream_t st) {
