@@ -39,19 +39,31 @@ __global__ void sf_to_atoms_kernel(const uint8_t* __restrict__ sf, int64_t group
   }
 }
 
-// Activation rows (slot s = r / M, j = r % M) -> token-tile atoms.
-__global__ void rows_to_tile_atoms_kernel(const uint8_t* __restrict__ sf, int64_t rows, int64_t M, int64_t kbc,
+// Activation rows (slot s = r / M, j = r % M) -> token-tile atoms. One warp
+// per output atom (token tile, K step, 128-row group): lane l gathers the
+// four scale words of rows l, l+32, l+64, l+96 of the group (zero past the
+// slot's M rows) and writes its 16 bytes, so each atom is one contiguous
+// 512-byte store.
+__global__ void rows_to_tile_atoms_kernel(const uint8_t* __restrict__ sf, int64_t slots, int64_t M, int64_t kbc,
                                           int tile_n, uint8_t* __restrict__ out) {
   const int natoms = (tile_n + 127) / 128;
   const int64_t tps = (M + tile_n - 1) / tile_n;
-  const int64_t total = rows * kbc;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / kbc, kb = i - r * kbc;
-    const int64_t s = r / M, j = r - s * M;
-    const int64_t tile = s * tps + j / tile_n;
-    const int rit = (int)(j % tile_n);
-    const uint32_t v = *reinterpret_cast<const uint32_t*>(sf + r * (kbc * 4) + kb * 4);
-    *reinterpret_cast<uint32_t*>(out + ((tile * kbc + kb) * natoms + (rit >> 7)) * 512 + atom_byte(rit & 127)) = v;
+  const int64_t total = slots * tps * kbc * natoms;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t w = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
+    const int a = (int)(w % natoms);
+    const int64_t tk = w / natoms;              // tile * kbc + kb
+    const int64_t kb = tk % kbc, tile = tk / kbc;
+    const int64_t s = tile / tps, jt = tile - s * tps;
+    uint32_t v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rit = 128 * a + 32 * i + lane;   // row in the token tile
+      const int64_t j = jt * tile_n + rit;
+      v[i] = (rit < tile_n && j < M) ? *reinterpret_cast<const uint32_t*>(sf + (s * M + j) * (kbc * 4) + kb * 4) : 0u;
+    }
+    *reinterpret_cast<uint4*>(out + w * 512 + 16 * lane) = make_uint4(v[0], v[1], v[2], v[3]);
   }
 }
 
@@ -91,6 +103,6 @@ extern "C" int aeoq_nvfp4_rows_to_tile_atoms(const uint8_t* sf, int64_t rows, in
   const int64_t total = rows * (K / 64);
   if (total == 0) return AEOQ_OK;
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
-  rows_to_tile_atoms_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(sf, rows, M, K / 64, tile_n, out);
+  rows_to_tile_atoms_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(sf, rows / M, M, K / 64, tile_n, out);
   return check_launch("rows_to_tile_atoms_kernel");
 }

@@ -58,8 +58,10 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     p.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM measurements")
-    p.add_argument("--workload", default="decode", choices=["decode", "ep"],
-                   help="decode: config 1 (default); ep: config 4, expert-parallel prefill stack")
+    p.add_argument("--workload", default="decode", choices=["decode", "ep", "gemm"],
+                   help="decode: config 1 (default); ep: config 4, expert-parallel prefill stack; "
+                        "gemm: config-0 NVFP4 linear at --gemm-m rows (profiling)")
+    p.add_argument("--gemm-m", type=int, default=32768)
     p.add_argument("--tokens", type=int, default=32 * 2048, help="ep: tokens over all ranks")
     p.add_argument("--ep-layers", type=int, default=4)
     return p.parse_args()
@@ -296,6 +298,39 @@ def measure_prefill(torch, dev, lib, A):
     return out
 
 
+def main_gemm(args, local):
+    """Config-0 weights (N=1408, K=2816) against --gemm-m activation rows
+    through nvfp4_linear_prequantized: W warm-up calls, then K timed calls
+    (CUDA events). Used for the GEMM profiles."""
+    import torch
+    from aeo_quant_b200.gpu import nvfp4_matmul as NM
+    from aeo_quant_b200.gpu import quant as Q
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = (torch.randn(1408, 2816, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    wp, wsf, wts = Q.quantize_2d_to_nvfp4(w)
+    wts = wts.float()
+    M = args.gemm_m
+    x = torch.randn(M, 2816, generator=g, device=dev).to(torch.bfloat16)
+    ap, asf, ats = Q.quantize_2d_to_nvfp4(x)
+    for _ in range(max(3, args.warmup)):
+        NM.nvfp4_linear_prequantized(ap, asf, ats, wp, wsf, wts)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        NM.nvfp4_linear_prequantized(ap, asf, ats, wp, wsf, wts)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / args.steps
+    tf = 2.0 * M * 1408 * 2816 / us / 1e6
+    print(json.dumps({"metric": "NVFP4 prefill TFLOPS (config-0 shapes)", "value": round(tf, 1), "unit": "TFLOP/s",
+                      "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": us / 1000.0,
+                      "higher_is_better": True, "config": {"workload": f"config0 GEMM M={M} N=1408 K=2816"},
+                      "frac_fp4_nominal": round(tf / 9000, 4)}), flush=True)
+
+
 def main_ep(args, rank, world, local):
     """Config 4: a stack of NVFP4 MoE layers (config-2 shapes), experts
     sharded E/world per GPU, tokens sharded by sequence, NCCL all-to-all
@@ -412,6 +447,9 @@ def main():
         return
     if args.workload == "ep":
         main_ep(args, rank, world, local)
+        return
+    if args.workload == "gemm":
+        main_gemm(args, local)
         return
     import torch
     import torch.distributed as dist
