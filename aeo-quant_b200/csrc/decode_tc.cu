@@ -79,7 +79,8 @@ __device__ uint64_t* g_dtrace = nullptr;
 
 constexpr int kThreads = 192;      // launch 2
 constexpr int kThreads1 = 256;     // launch 1: two more producer warps (6, 7)
-constexpr int kRing = 3;           // launch-1 weight ring depth (one producer warp per slot)
+constexpr int kRing = 6;           // launch-1 weight ring: every K stage of a CTA in flight at once
+constexpr int kProducers1 = 3;     // launch-1 producer warps 0, 6, 7 (slot s -> producer s % 3)
 
 __host__ __device__ constexpr int rup(int v, int m) { return (v + m - 1) / m * m; }
 
@@ -242,19 +243,22 @@ __device__ __forceinline__ void st_weight_scales_rows16(uint32_t taddr, const ui
 }
 
 // Same, from row-major scale rows of sfrow bytes (a multiple of 4; words
-// past a row's last K step are read but not used by any MMA).
+// past a row's last K step are read but not used by any MMA), for an N-row
+// operand of kAtoms 128-row groups: 4 * kAtoms columns per K step.
+template <int kAtoms>
 __device__ __forceinline__ void st_weight_scales_rows(uint32_t taddr, const uint8_t* sf, int sfrow, int n_rows,
                                                       int nkb, int lane) {
-  for (int c = 0; c < (nkb + 3) / 4; ++c) {
+  constexpr int kPer = 8 / kAtoms;   // K steps per 32-column store
+  for (int c = 0; c < (nkb + kPer - 1) / kPer; ++c) {
     uint32_t r[32];
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
+    for (int a = 0; a < kAtoms; ++a)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int row = 128 * a + 32 * i + lane;
-        const uint32_t* src = reinterpret_cast<const uint32_t*>(sf + (row < n_rows ? row : 0) * sfrow) + 4 * c;
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(sf + (row < n_rows ? row : 0) * sfrow) + kPer * c;
 #pragma unroll
-        for (int kbi = 0; kbi < 4; ++kbi) r[8 * kbi + 4 * a + i] = row < n_rows ? src[kbi] : 0u;
+        for (int kbi = 0; kbi < kPer; ++kbi) r[4 * kAtoms * kbi + 4 * a + i] = row < n_rows ? src[kbi] : 0u;
       }
     sm100::tmem_st32(taddr + 32 * c, r);
   }
@@ -338,10 +342,11 @@ __global__ void __launch_bounds__(kThreads1, 1)
     // One warp's copies complete one after another, so the slots go to
     // different warps. Tensor maps: weights (H/2, I, gate|up, E) and scales
     // (H/16, I, gate|up, E), so one box brings a stage's gate and up rows.
-    const int slot = warp == 0 ? 0 : warp - 5;
+    const int pidx = warp == 0 ? 0 : warp - 5;
     const bool leader = sm100::elect_one();
     if (warp == 0 && leader) {
-      // the hidden vector first: the quantization waits on it, the MMAs on that
+      // the hidden vector and the scales first: the quantization and the
+      // scale copy into TMEM wait on them, the MMAs on those
       sm100::mbar_arrive_expect_tx(&sh->hid, (uint32_t)(2 * H));
       bulk_g2s(base + L.hid, a.hidden, (uint32_t)(2 * H), &sh->hid);
       if (valid) {
@@ -350,35 +355,30 @@ __global__ void __launch_bounds__(kThreads1, 1)
       }
     }
     __syncwarp();
-    // The weight stream starts once the hidden vector and the scales have
-    // landed: issued together, the small copies would queue behind it, and
-    // the MMAs cannot start before the quantization they feed.
-    bool go = sm100::mbar_wait(&sh->hid, 0, a.err, 47);
-    if (valid) go = go && sm100::mbar_wait(&sh->sf, 0, a.err, 48);
-    bool done_first = false;
-    for (int kt = slot; kt < nt && valid && go; kt += kRing) {
+    // Every stage of the CTA's K range is issued at once (the ring holds
+    // them all for the configured shapes; a slot's later uses wait for its
+    // empty barrier).
+    for (int kt = 0; kt < nt && valid; ++kt) {
+      const int s = kt % kRing;
+      if (s % kProducers1 != pidx) continue;
       const uint32_t ph = (kt / kRing) & 1;
-      if (!sm100::mbar_wait(&sh->empty[slot], ph ^ 1, a.err, 41)) break;
+      if (!sm100::mbar_wait(&sh->empty[s], ph ^ 1, a.err, 41)) break;
       if (leader) {
-        sm100::mbar_arrive_expect_tx(&sh->full[slot], (uint32_t)L.stage);
-        sm100::tma_load_4d(ring + slot * L.stage, &tmW, 32 * kb0 + 128 * kt, T * m, 0, (int32_t)e, &sh->full[slot]);
+        sm100::mbar_arrive_expect_tx(&sh->full[s], (uint32_t)L.stage);
+        sm100::tma_load_4d(ring + s * L.stage, &tmW, 32 * kb0 + 128 * kt, T * m, 0, (int32_t)e, &sh->full[s]);
       }
       __syncwarp();
-      if (warp == 0 && !done_first) {
-        done_first = true;
-        pdl_trigger();   // the down launch may start its prefetch now
-        // Until the MMAs free its slot this warp is idle: it writes the
-        // weight scales (lane quadrant 0, the only one accumulator row 0
-        // reads), in parallel with the quantization of the hidden vector.
-        st_weight_scales_rows16(tmem + pl.sfb1, sfs, L.sfrow, N1, nkb, lane);
-        sm100::tmem_st_wait();
-        sm100::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) sm100::mbar_arrive(&sh->bready);
-      }
     }
-    if (warp == 0 && !done_first) {
-      pdl_trigger();
+    if (warp == 0) {
+      pdl_trigger();   // the down launch may start its prefetch now
+      // The weight scales into TMEM (lane quadrant 0, the only one
+      // accumulator row 0 reads), in parallel with the quantization of the
+      // hidden vector by the epilogue warps.
+      if (valid && sm100::mbar_wait(&sh->sf, 0, a.err, 48))
+        st_weight_scales_rows16(tmem + pl.sfb1, sfs, L.sfrow, N1, nkb, lane);
+      sm100::tmem_st_wait();
+      sm100::tc_fence_before();
+      __syncwarp();
       if (lane == 0) sm100::mbar_arrive(&sh->bready);
     }
   } else if (warp == 1) {
@@ -546,7 +546,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < kb2; ++kb) {
         const uint64_t ad = sm100::sdesc_k_sw128(sm100::smem_u32(tokA + (kb >> 2) * 1024) + (kb & 3) * 32);
         const uint64_t bd = sm100::sdesc_k_sw128(sm100::smem_u32(btile + (kb >> 2) * N2 * 128) + (kb & 3) * 32);
-        sm100::tc_mma_nvf4(tmem, ad, bd, idesc, tmem + pl.sfa2 + 4 * kb, tmem + pl.sfb2 + 8 * kb, kb ? 1u : 0u);
+        sm100::tc_mma_nvf4(tmem, ad, bd, idesc, tmem + pl.sfa2 + 4 * kb, tmem + pl.sfb2 + (N2 > 128 ? 8 : 4) * kb,
+                           kb ? 1u : 0u);
       }
     }
     if (leader) sm100::tc_commit(&sh->accum);
@@ -556,7 +557,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t qaddr = (uint32_t)(32 * (warp & 3)) << 16;
     if (valid && sm100::mbar_wait(&sh->full, 0, a.err, 53)) {
       if (t == 0) DT(5);
-      if (warp == 4) st_weight_scales_rows(tmem + qaddr + pl.sfb2, sfs, L.sfrow, N2, kb2, lane);
+      if (warp == 4) {
+        if (pl.N2 > 128) st_weight_scales_rows<2>(tmem + qaddr + pl.sfb2, sfs, L.sfrow, N2, kb2, lane);
+        else st_weight_scales_rows<1>(tmem + qaddr + pl.sfb2, sfs, L.sfrow, N2, kb2, lane);
+      }
     }
     pdl_wait();   // launch 1 complete: h and the maxima are visible
     if (t == 0) DT(1);
@@ -648,9 +652,13 @@ bool plan_for(int64_t k, int64_t H, int64_t I, Plan& p) {
   }
   p.cols1 = (p.sfb1 + 8 * p.Q <= 256) ? 256 : 512;
   const int kb2 = (int)(I / 64);
-  p.N2 = (H % 256 == 0) ? 256 : 128;
-  auto need2 = [&](int n2) { return n2 + rup(4 * kb2, 32) + 8 * rup(kb2, 4); };
-  if (need2(p.N2) > 512) p.N2 = 128;
+  // 128-row down tiles: a launch-2 CTA (about 58 KB of shared memory, at
+  // most 256 TMEM columns) fits beside a launch-1 CTA and prefetches its
+  // weights while launch 1 runs; two of them share an SM afterwards.
+  p.N2 = 128;
+  auto need2 = [&](int n2) {
+    return n2 + rup(4 * kb2, 32) + (n2 > 128 ? 8 * rup(kb2, 4) : 4 * rup(kb2, 8));
+  };
   if (need2(p.N2) > 512) return false;
   p.sfa2 = p.N2;
   p.sfb2 = p.sfa2 + rup(4 * kb2, 32);
