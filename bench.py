@@ -44,7 +44,7 @@ FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one tensor-core decode
 # (both launches) at this workload, from the ncu capture summarised in
 # profiles/moe_decode_tc_b1.md (None until captured).
-NCU_TRAFFIC_TC = 26983424
+NCU_TRAFFIC_TC = 27048448
 
 
 def parse():
