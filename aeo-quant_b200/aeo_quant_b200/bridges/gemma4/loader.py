@@ -71,3 +71,51 @@ def load_gemma4_nvfp4(model_id_or_path, **from_pretrained_kwargs):
     with _gemma4_experts_nvfp4_class_swap():
         model = AutoModelForCausalLM.from_pretrained(model_id_or_path, **from_pretrained_kwargs)
     return model
+
+
+@torch.no_grad()
+def quantize_experts_to_nvfp4(model):
+    """Replace every bf16 ``Gemma4TextExperts`` in ``model`` by a
+    ``Gemma4TextExpertsNVFP4`` holding its NVFP4 quantization, on the
+    experts' device.
+
+    This is the expert step of the reference's checkpoint builder
+    (``examples/build_checkpoint_nvfp4.py:133-151``): each fused 3-D expert
+    tensor goes through ``quantize_3d_to_nvfp4`` and becomes ``<proj>``
+    (packed E2M1), ``<proj>_scale`` (e4m3 block scales) and ``<proj>_scale_2``
+    (the tensor scale, held as a 0-d fp32 buffer as after loading). Here it
+    runs on the GPU kernels, one layer at a time, and each layer's bf16
+    weights are released as soon as its NVFP4 copy exists. Returns the
+    number of modules converted."""
+    from ...gpu.quant import quantize_3d_to_nvfp4
+
+    targets = []
+    for name, mod in model.named_modules():
+        for child_name, child in mod.named_children():
+            if type(child) is modeling_gemma4.Gemma4TextExperts:
+                targets.append((mod, child_name, child))
+    for parent, child_name, old in targets:
+        dev = old.gate_up_proj.device
+        cfg = _ExpertShape(old)
+        new = Gemma4TextExpertsNVFP4(cfg).to(dev)
+        for proj in ("gate_up_proj", "down_proj"):
+            packed, block_scale, tensor_scale = quantize_3d_to_nvfp4(getattr(old, proj).detach().to(torch.bfloat16))
+            getattr(new, proj).copy_(packed)
+            getattr(new, f"{proj}_scale").copy_(block_scale)
+            getattr(new, f"{proj}_scale_2").copy_(tensor_scale.float())
+            del packed, block_scale, tensor_scale
+        setattr(parent, child_name, new)
+        del old
+    return len(targets)
+
+
+class _ExpertShape:
+    """The config fields ``Gemma4TextExpertsNVFP4.__init__`` reads, taken
+    from an existing bf16 expert module."""
+
+    def __init__(self, experts):
+        E, two_i, H = experts.gate_up_proj.shape
+        self.num_experts = E
+        self.hidden_size = H
+        self.moe_intermediate_size = two_i // 2
+        self.hidden_activation = "gelu_pytorch_tanh"

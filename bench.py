@@ -58,12 +58,14 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     p.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM measurements")
-    p.add_argument("--workload", default="decode", choices=["decode", "ep", "gemm"],
+    p.add_argument("--workload", default="decode", choices=["decode", "ep", "gemm", "stack"],
                    help="decode: config 1 (default); ep: config 4, expert-parallel prefill stack; "
                         "gemm: config-0 NVFP4 linear at --gemm-m rows (profiling)")
     p.add_argument("--gemm-m", type=int, default=32768)
     p.add_argument("--tokens", type=int, default=32 * 2048, help="ep: tokens over all ranks")
     p.add_argument("--ep-layers", type=int, default=4)
+    p.add_argument("--stack-layers", type=int, default=30, help="stack: decoder layers")
+    p.add_argument("--prompt", type=int, default=2048, help="stack: prefill tokens")
     return p.parse_args()
 
 
@@ -439,6 +441,128 @@ def main_ep(args, rank, world, local):
     dist.destroy_process_group()
 
 
+def stack_config(layers):
+    """Config 3: a Gemma-4-26B-A4B-shaped text decoder. Pinned: hidden 2816,
+    128 experts top-8, expert intermediate 704, vocab 262144, 30 layers with
+    a sliding window of 1024 on 5 of every 6. Chosen (the real config.json
+    is not available): 16 query heads and 8 KV heads of 256 (512 on
+    full-attention layers), dense MLP 2112, no per-layer input embedding."""
+    from transformers.models.gemma4.configuration_gemma4 import Gemma4TextConfig
+    types_ = [("full_attention" if (i + 1) % 6 == 0 else "sliding_attention") for i in range(layers)]
+    return Gemma4TextConfig(
+        hidden_size=H, num_hidden_layers=layers, num_attention_heads=16, num_key_value_heads=8, head_dim=256,
+        global_head_dim=512, intermediate_size=2112, moe_intermediate_size=I, num_experts=E, top_k_experts=TOPK,
+        enable_moe_block=True, vocab_size=262144, vocab_size_per_layer_input=262144,
+        hidden_size_per_layer_input=0, sliding_window=1024, layer_types=types_, max_position_embeddings=8192)
+
+
+def _our_kernel_launches(torch, fn):
+    """Kernels of this library launched by one call of ``fn`` (profiler
+    pass outside any timed region); None if the profiler is unavailable."""
+    try:
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        n = 0
+        for ev in prof.events():
+            name = ev.name or ""
+            if ev.device_type == torch.autograd.DeviceType.CUDA and ("aeoq::" in name or "dtc::" in name):
+                n += 1
+        return n
+    except Exception:
+        return None
+
+
+def main_stack(args, local):
+    """Config 3: random-init Gemma-4-shaped stack, experts converted to NVFP4
+    on the GPU and run through the swapped ``Gemma4TextExpertsNVFP4``; HF
+    transformers (eager PyTorch) for everything else. Prefill 2048 tokens,
+    then K greedy decode steps, batch 1. value = decode tok/s."""
+    import torch
+    from transformers.models.gemma4.modeling_gemma4 import Gemma4ForCausalLM
+    from aeo_quant_b200.bridges.gemma4.loader import quantize_experts_to_nvfp4
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    L, P, K, W = args.stack_layers, args.prompt, args.steps, max(3, args.warmup)
+    torch.manual_seed(0)
+    old = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    with torch.device(dev):
+        model = Gemma4ForCausalLM(stack_config(L)).eval()
+    torch.set_default_dtype(old)
+    n_conv = quantize_experts_to_nvfp4(model)
+    torch.cuda.empty_cache()
+    g = torch.Generator().manual_seed(1)
+    ids = torch.randint(10, 262144, (1, P), generator=g).to(dev)
+
+    def prefill():
+        out = model(ids, use_cache=True)
+        return out.past_key_values, out.logits[:, -1:].argmax(-1)
+
+    def decode(pkv, nxt, n):
+        for _ in range(n):
+            out = model(nxt, past_key_values=pkv, use_cache=True)
+            pkv, nxt = out.past_key_values, out.logits[:, -1:].argmax(-1)
+        return pkv, nxt
+
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    with torch.no_grad():
+        pkv, nxt = prefill()           # warm-up
+        decode(pkv, nxt, W)
+        del pkv
+        torch.cuda.synchronize()
+        with ClockSampler(local) as clk:
+            ev[0].record()
+            pkv, nxt = prefill()
+            ev[1].record()
+            ev[2].record()
+            pkv, nxt = decode(pkv, nxt, K)
+            ev[3].record()
+            torch.cuda.synchronize()
+        t_pre = ev[0].elapsed_time(ev[1])
+        t_dec = ev[2].elapsed_time(ev[3])
+        n_dec = _our_kernel_launches(torch, lambda: decode(pkv, nxt, 1))
+        # e2e: each step's token id goes up from pinned host memory and the
+        # greedy token comes back before the next step is issued
+        tok_h = torch.empty(1, 1, dtype=torch.int64).pin_memory()
+        tok_h.copy_(nxt.cpu())
+        x = torch.empty(1, 1, dtype=torch.int64, device=dev)
+        pkv2, _ = prefill()
+        torch.cuda.synchronize()
+        ev[0].record()
+        for _ in range(K):
+            x.copy_(tok_h, non_blocking=True)
+            out = model(x, past_key_values=pkv2, use_cache=True)
+            pkv2 = out.past_key_values
+            tok_h.copy_(out.logits[:, -1:].argmax(-1), non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+        ev[1].record()
+        torch.cuda.synchronize()
+        t_e2e = ev[0].elapsed_time(ev[1])
+    value = K / (t_dec / 1000.0)
+    print(json.dumps({
+        "metric": "Gemma-4 stack greedy decode tok/s (batch 1)", "value": round(value, 2), "unit": "tok/s",
+        "n_gpus": 1, "steps": K, "warmup": W, "ms_per_step": t_dec / K, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "NVFP4 experts (fp32 accumulate), bf16 elsewhere",
+        "data": "synthetic (random-init weights N(0,0.02), experts quantized to NVFP4 on device; random prompt)",
+        "config": {"workload": f"config3: random-init Gemma-4-26B-A4B-shaped stack, {L} layers, "
+                               f"prefill {P} tokens then {K} greedy decode steps, batch 1",
+                   "experts_converted": n_conv, "hidden": H, "experts": E, "top_k": TOPK, "intermediate": I,
+                   "non_expert": "HF transformers eager (attention, router, dense MLP, lm_head)",
+                   "l2": "inputs larger than L2 (12.8 GB of expert weights per decode step)",
+                   "timing": "CUDA events around the prefill and around K decode steps"},
+        "prefill": {"tokens": P, "ms": round(t_pre, 3), "tok_s": round(P / (t_pre / 1000.0), 1)},
+        "gpu_launches": None if n_dec is None else n_dec * K,
+        "gpu_launches_per_decode_step": n_dec,
+        "clocks": clk.summary(),
+        "e2e": {"value": round(K / (t_e2e / 1000.0), 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                "d2h_bytes_per_step": 8, "path": "model forward per token, token id from pinned host, "
+                                                 "greedy token read back each step"},
+    }), flush=True)
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
@@ -450,6 +574,9 @@ def main():
         return
     if args.workload == "gemm":
         main_gemm(args, local)
+        return
+    if args.workload == "stack":
+        main_stack(args, local)
         return
     import torch
     import torch.distributed as dist
