@@ -19,7 +19,7 @@ FP8_WEIGHT, FP8_ACTIVATION = 0, 1
 _DT = {torch.bfloat16: BF16, torch.float16: F16, torch.float32: F32, torch.int32: I32,
        torch.int64: I64}
 
-_P, _I, _L, _Z = C.c_void_p, C.c_int, C.c_int64, C.c_size_t
+_P, _I, _L, _Z, _F = C.c_void_p, C.c_int, C.c_int64, C.c_size_t, C.c_float
 
 # name -> argtypes (every entry point returns int status unless listed in _RESTYPE)
 _SIGS = {
@@ -52,6 +52,7 @@ _SIGS["aeoq_selftest_div_rn"] = [_I, _P, _P, _P]
 _SIGS["aeoq_fp8_gemm"] = [_P, _P, _L, _P, _P, _L, _L, _P, _P, _P]
 _SIGS["aeoq_fp8_gemm_grouped"] = [_P, _P, _L, _P, _P, _I, _P, _P, _L, _L, _L, _I, _P, _P, _L, _P, _P]
 _SIGS["aeoq_fp8_quantize_rows_gather"] = [_P, _L, _P, _P, _L, _L, _P, _L, _P, _P]
+_SIGS["aeoq_gemma4_router"] = [_P, _L, _P, _P, _P, _L, _L, _L, _L, _F, _F, _P, _P, _P, _P]
 _SIGS["aeoq_moe_nvfp4_decode_tc_supported"] = [_L, _L, _L]
 _SIGS["aeoq_moe_nvfp4_decode_tc_workspace_size"] = [_L, _L, _L]
 _SIGS["aeoq_moe_nvfp4_decode_tc"] = [_P, _P, _I, _P, _L, _P, _P, _P, _I, _P, _P, _P, _I, _L, _L, _L, _P, _P, _Z, _P, _P]

@@ -119,3 +119,31 @@ class _ExpertShape:
         self.hidden_size = H
         self.moe_intermediate_size = two_i // 2
         self.hidden_activation = "gelu_pytorch_tanh"
+
+
+def gemma4_router_class_swap():
+    """Swap in ``Gemma4TextRouterB200`` for ``Gemma4TextRouter`` while a
+    model is built (same parameters, fused forward)."""
+    from .router import Gemma4TextRouterB200
+
+    @contextlib.contextmanager
+    def _cm():
+        original = modeling_gemma4.Gemma4TextRouter
+        modeling_gemma4.Gemma4TextRouter = Gemma4TextRouterB200
+        try:
+            yield
+        finally:
+            modeling_gemma4.Gemma4TextRouter = original
+    return _cm()
+
+
+def swap_routers(model):
+    """Give every ``Gemma4TextRouter`` in a built model the fused forward
+    (its parameters stay where they are). Returns the number swapped."""
+    from .router import Gemma4TextRouterB200
+    n = 0
+    for mod in model.modules():
+        if type(mod) is modeling_gemma4.Gemma4TextRouter:
+            mod.__class__ = Gemma4TextRouterB200
+            n += 1
+    return n

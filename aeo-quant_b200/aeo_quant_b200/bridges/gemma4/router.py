@@ -1,0 +1,50 @@
+"""Gemma-4 router on one fused kernel.
+
+``Gemma4TextRouterB200`` is HF transformers' ``Gemma4TextRouter`` (5.5.0,
+``models/gemma4/modeling_gemma4.py:1283-1316``) with the same parameters
+(``proj.weight``, ``scale``, ``per_expert_scale``) and the same outputs
+``(router_probabilities, top_k_weights, top_k_index)``. Its forward is
+``aeoq_gemma4_router``: RMS norm, scale, projection, softmax, top-k,
+renormalisation and per-expert scale in one launch, in place of about ten
+eager launches. The router sits in front of the swapped expert modules in
+every ``Gemma4TextDecoderLayer`` (:1379-1383); ``loader.swap_routers``
+installs it on a built model and ``loader.gemma4_router_class_swap`` during
+``from_pretrained``.
+"""
+from __future__ import annotations
+
+import torch
+from transformers.models.gemma4.modeling_gemma4 import Gemma4TextRouter
+
+from ... import _capi as A
+
+
+class Gemma4TextRouterB200(Gemma4TextRouter):
+    """Gemma4TextRouter with a fused CUDA forward (bf16 only)."""
+
+    def forward(self, hidden_states: torch.Tensor):
+        x = hidden_states
+        if x.dim() != 2:
+            raise ValueError(f"router expects (tokens, hidden), got shape {tuple(x.shape)}")
+        w = self.proj.weight
+        for name, t in (("hidden_states", x), ("proj.weight", w), ("scale", self.scale),
+                        ("per_expert_scale", self.per_expert_scale)):
+            if t.dtype != torch.bfloat16:
+                raise ValueError(f"{name} must be bfloat16, got {t.dtype}")
+            if not t.is_cuda:
+                raise ValueError(f"{name} must be a CUDA tensor")
+        if x.stride(-1) != 1 or x.stride(0) % 8 or x.data_ptr() % 16:
+            x = x.contiguous() if x.stride(-1) != 1 else x.clone()
+        T, H = x.shape
+        E = w.shape[0]
+        k = self.config.top_k_experts
+        dev = x.device
+        probs = torch.empty(T, E, dtype=torch.bfloat16, device=dev)
+        top_w = torch.empty(T, k, dtype=torch.bfloat16, device=dev)
+        top_i = torch.empty(T, k, dtype=torch.int64, device=dev)
+        lib = A.load()
+        A.check(lib.aeoq_gemma4_router(x.data_ptr(), x.stride(0), self.scale.contiguous().data_ptr(),
+                                       w.contiguous().data_ptr(), self.per_expert_scale.contiguous().data_ptr(),
+                                       T, H, E, k, float(self.eps), float(self.scalar_root_size),
+                                       probs.data_ptr(), top_w.data_ptr(), top_i.data_ptr(), A.stream_ptr(dev)))
+        return probs, top_w, top_i

@@ -58,7 +58,7 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     p.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM measurements")
-    p.add_argument("--workload", default="decode", choices=["decode", "ep", "gemm", "stack"],
+    p.add_argument("--workload", default="decode", choices=["decode", "ep", "gemm", "stack", "router"],
                    help="decode: config 1 (default); ep: config 4, expert-parallel prefill stack; "
                         "gemm: config-0 NVFP4 linear at --gemm-m rows (profiling)")
     p.add_argument("--gemm-m", type=int, default=32768)
@@ -474,6 +474,32 @@ def _our_kernel_launches(torch, fn):
         return None
 
 
+def main_router(args, local):
+    """The Gemma-4 router alone (config-3 shapes: H 2816, 128 experts,
+    top-8): the fused kernel and HF's eager forward, one token and
+    ``--prompt`` tokens, each timed as one CUDA graph of repeated calls."""
+    import torch
+    from transformers.models.gemma4.modeling_gemma4 import Gemma4TextRouter
+    from aeo_quant_b200.bridges.gemma4.loader import swap_routers
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    torch.manual_seed(0)
+    r = Gemma4TextRouter(stack_config(6)).to(device=dev, dtype=torch.bfloat16).eval()
+    with torch.no_grad():
+        r.proj.weight.normal_(0.0, 0.5)
+    swap_routers(torch.nn.Sequential(r))
+    out = {}
+    with torch.no_grad():
+        for T in (1, args.prompt):
+            x = torch.randn(T, H, device=dev).to(torch.bfloat16)
+            out[f"fused_T{T}_us"] = round(_graph_time_us(torch, dev, lambda: r(x), 200 if T == 1 else 50), 2)
+            out[f"hf_eager_T{T}_us"] = round(
+                _graph_time_us(torch, dev, lambda: Gemma4TextRouter.forward(r, x), 200 if T == 1 else 50), 2)
+    print(json.dumps({"metric": "Gemma-4 router latency", "unit": "us", "higher_is_better": False,
+                      "config": {"workload": "router alone, H 2816, 128 experts, top-8, bf16"}, **out}), flush=True)
+
+
 def main_stack(args, local):
     """Config 3: random-init Gemma-4-shaped stack, experts converted to NVFP4
     on the GPU and run through the swapped ``Gemma4TextExpertsNVFP4``; HF
@@ -507,9 +533,13 @@ def main_stack(args, local):
             pkv, nxt = out.past_key_values, out.logits[:, -1:].argmax(-1)
         return pkv, nxt
 
+    from aeo_quant_b200.bridges.gemma4.loader import swap_routers
+
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-    with torch.no_grad():
-        pkv, nxt = prefill()           # warm-up
+
+    def timed(clk_holder):
+        """Warm-up, then one timed prefill and K timed decode steps."""
+        pkv, nxt = prefill()
         decode(pkv, nxt, W)
         del pkv
         torch.cuda.synchronize()
@@ -521,9 +551,28 @@ def main_stack(args, local):
             pkv, nxt = decode(pkv, nxt, K)
             ev[3].record()
             torch.cuda.synchronize()
-        t_pre = ev[0].elapsed_time(ev[1])
-        t_dec = ev[2].elapsed_time(ev[3])
+        clk_holder.append(clk.summary())
+        return ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3]), pkv, nxt
+
+    clocks = []
+    with torch.no_grad():
+        # experts swapped, HF's eager router
+        t_pre_x, t_dec_x, _, _ = timed(clocks)
+        # experts and router swapped (the product configuration)
+        n_routers = swap_routers(model)
+        t_pre, t_dec, pkv, nxt = timed(clocks)
         n_dec = _our_kernel_launches(torch, lambda: decode(pkv, nxt, 1))
+        # router alone, one token and the prefill's tokens
+        lay = model.model.layers[0]
+        xr1 = torch.randn(1, H, device=dev).to(torch.bfloat16)
+        xrp = torch.randn(P, H, device=dev).to(torch.bfloat16)
+        from transformers.models.gemma4.modeling_gemma4 import Gemma4TextRouter
+        router_us = {
+            "fused_T1": round(_graph_time_us(torch, dev, lambda: lay.router(xr1), 200), 2),
+            "hf_eager_T1": round(_graph_time_us(torch, dev, lambda: Gemma4TextRouter.forward(lay.router, xr1), 200), 2),
+            f"fused_T{P}": round(_graph_time_us(torch, dev, lambda: lay.router(xrp), 50), 2),
+            f"hf_eager_T{P}": round(_graph_time_us(torch, dev, lambda: Gemma4TextRouter.forward(lay.router, xrp), 50), 2),
+        }
         # e2e: each step's token id goes up from pinned host memory and the
         # greedy token comes back before the next step is issued
         tok_h = torch.empty(1, 1, dtype=torch.int64).pin_memory()
@@ -549,14 +598,17 @@ def main_stack(args, local):
         "data": "synthetic (random-init weights N(0,0.02), experts quantized to NVFP4 on device; random prompt)",
         "config": {"workload": f"config3: random-init Gemma-4-26B-A4B-shaped stack, {L} layers, "
                                f"prefill {P} tokens then {K} greedy decode steps, batch 1",
-                   "experts_converted": n_conv, "hidden": H, "experts": E, "top_k": TOPK, "intermediate": I,
-                   "non_expert": "HF transformers eager (attention, router, dense MLP, lm_head)",
+                   "experts_converted": n_conv, "routers_swapped": n_routers, "hidden": H, "experts": E, "top_k": TOPK, "intermediate": I,
+                   "non_expert": "HF transformers eager (attention, dense MLP, lm_head)",
                    "l2": "inputs larger than L2 (12.8 GB of expert weights per decode step)",
                    "timing": "CUDA events around the prefill and around K decode steps"},
         "prefill": {"tokens": P, "ms": round(t_pre, 3), "tok_s": round(P / (t_pre / 1000.0), 1)},
+        "experts_only_swap": {"decode_tok_s": round(K / (t_dec_x / 1000.0), 2), "prefill_ms": round(t_pre_x, 3),
+                              "note": "HF eager router in front of the swapped experts"},
+        "router_us": router_us,
         "gpu_launches": None if n_dec is None else n_dec * K,
         "gpu_launches_per_decode_step": n_dec,
-        "clocks": clk.summary(),
+        "clocks": clocks[-1],
         "e2e": {"value": round(K / (t_e2e / 1000.0), 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": 8, "path": "model forward per token, token id from pinned host, "
                                                  "greedy token read back each step"},
@@ -577,6 +629,9 @@ def main():
         return
     if args.workload == "stack":
         main_stack(args, local)
+        return
+    if args.workload == "router":
+        main_router(args, local)
         return
     import torch
     import torch.distributed as dist

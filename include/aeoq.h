@@ -193,6 +193,20 @@ AEOQ_API int aeoq_fp8_quantize_rows_gather(const void* x, int64_t ld, const int*
                                            int64_t max_rows, int64_t K, uint8_t* q, int64_t q_ld,
                                            float* scale_out, void* stream);
 
+/* Gemma-4 router for T tokens (HF transformers 5.5.0 Gemma4TextRouter.forward,
+ * models/gemma4/modeling_gemma4.py:1296-1316): probs = softmax(proj(
+ * bf16(bf16(rmsnorm(x)) * scale) * root_scale)), top_k of probs (descending,
+ * equal values by lower expert id), renormalised and multiplied by
+ * per_expert_scale. x (T, H) bf16 with row stride ldx; scale (H,), proj_w
+ * (E, H), per_expert_scale (E,) bf16. Outputs probs (T, E) bf16, top_w
+ * (T, top_k) bf16, top_i (T, top_k) int64. H and ldx multiples of 8, H <=
+ * 6144 and >= 2 E + 128, E a multiple of 8 and <= 256, top_k <= min(E, 32). One launch,
+ * one 8-CTA cluster per 16 tokens. */
+AEOQ_API int aeoq_gemma4_router(const void* x, int64_t ldx, const void* scale, const void* proj_w,
+                                const void* per_expert_scale, int64_t T, int64_t H, int64_t E, int64_t top_k,
+                                float eps, float root_scale, void* probs, void* top_w, int64_t* top_i,
+                                void* stream);
+
 /* Device-side grouping of (token, slot) pairs by expert (replaces the
  * one_hot / nonzero / where scaffolding, modeling_nvfp4.py:208-222, and
  * modeling.py:111-121): counts, row offsets, token-tile offsets for tile_n,

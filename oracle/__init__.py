@@ -20,4 +20,4 @@ package against them. The GEMM arithmetic itself lives in third-party code
 hold the reference forwards with the GEMM call restated, so the GEMM
 contract is pinned by its published definition, not by reference outputs.
 """
-from . import gemm, moe, numerics, quant  # noqa: F401
+from . import gemm, moe, numerics, quant, router  # noqa: F401

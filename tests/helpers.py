@@ -64,3 +64,37 @@ def within_tol_or_ulp(out, ref, tol=TOL) -> bool:
     ref = np.asarray(ref, np.float64)
     lim = np.maximum(tol * np.max(np.abs(ref)), bf16_ulp(ref))
     return bool(np.all(np.abs(out - ref) <= lim))
+
+
+def check_router(probs, w, idx, ref_probs, ref_w, ref_idx, ulps=2, w_tol=1e-2):
+    """Router outputs against a reference: probabilities within one bf16 ulp
+    of max|ref| ... (``ulps`` ulps); per token the top-k sets agree except
+    for experts whose reference probability lies within ``ulps`` bf16 ulps
+    of the reference's k-th value (near-ties, where the order of equal
+    values or a last-place rounding decides); where the sets agree, the
+    weights of each expert agree within ``w_tol`` of the row's max weight.
+    Returns the number of tokens whose sets differ."""
+    probs, ref_probs = np.asarray(probs, np.float64), np.asarray(ref_probs, np.float64)
+    assert np.max(np.abs(probs - ref_probs)) <= ulps * float(bf16_ulp(ref_probs.max()))
+    idx, ref_idx = np.asarray(idx), np.asarray(ref_idx)
+    w, ref_w = np.asarray(w, np.float64), np.asarray(ref_w, np.float64)
+    k = idx.shape[1]
+    differ = 0
+    for t in range(idx.shape[0]):
+        kth = np.sort(ref_probs[t])[::-1][k - 1]
+        s, r = set(idx[t].tolist()), set(ref_idx[t].tolist())
+        assert len(s) == k
+        if s != r:
+            differ += 1
+            for e in s ^ r:
+                assert abs(ref_probs[t, e] - kth) <= ulps * float(bf16_ulp(kth)), (t, e, ref_probs[t, e], kth)
+            continue
+        a = dict(zip(idx[t].tolist(), w[t].tolist()))
+        b = dict(zip(ref_idx[t].tolist(), ref_w[t].tolist()))
+        m = max(abs(v) for v in b.values())
+        for e in s:
+            assert abs(a[e] - b[e]) <= w_tol * m, (t, e, a[e], b[e])
+        # descending order of the probabilities behind the weights
+        pv = ref_probs[t, idx[t]]
+        assert np.all(np.diff(pv) <= ulps * float(bf16_ulp(pv[0])))
+    return differ

@@ -119,3 +119,22 @@ def test_every_expert_call_in_the_stack_vs_oracle(stack):
         om = oracles.setdefault(id(mod), OracleExperts(mod).om)
         ref = OM.nvfp4_experts_forward(om, bf16_to_np(h), idx.cpu().numpy(), bf16_to_np(w))
         assert max_rel_err(bf16_to_np(y), ref) <= TOL
+
+
+def test_fused_router_in_stack(stack):
+    """The stack with every router on the fused kernel generates the same
+    greedy tokens as with HF's eager routers, logits within 2e-2."""
+    from transformers.models.gemma4.modeling_gemma4 import Gemma4TextRouter
+    from aeo_quant_b200.bridges.gemma4.loader import swap_routers
+    ids = torch.randint(10, 4096, (1, PROMPT), generator=torch.Generator().manual_seed(9)).cuda()
+    tok_ref, logits_ref = _greedy(stack, ids)
+    try:
+        assert swap_routers(stack) == 2
+        tok, logits = _greedy(stack, ids)
+    finally:
+        for l in stack.model.layers:
+            l.router.__class__ = Gemma4TextRouter
+    assert tok.tolist() == tok_ref.tolist()
+    for i in range(NEW):
+        err = float((logits[i] - logits_ref[i]).abs().max() / logits_ref[i].abs().max())
+        assert err <= 2e-2, (i, err)
