@@ -17,15 +17,17 @@
 // The reduction orders of the sums differ from cuBLAS / ATen, so logits can
 // differ from the eager ones in the last bf16 place.
 //
-// Layout: one 8-CTA cluster per tile of 8 tokens (1 for a single token).
-// CTA rank r computes the logits of experts [r*E/8, (r+1)*E/8) for the
-// tile's tokens: a warp takes two expert rows at a time, reads them once
-// with four 16-byte loads per row in flight per lane (the first of them
-// issued before the tokens are normalised) and dots them with every
-// token's normalised row in shared memory; the 0.7 MB projection is read
-// once per tile and stays in L2. Warp w of every CTA normalises token w of
-// the tile; warp w of rank 0 gathers token w's E logits through
-// distributed shared memory and finishes it.
+// Layout: one 8-CTA cluster per tile of 16 tokens (1 for a single token).
+// Every CTA copies the tile's token rows into shared memory with cp.async,
+// all pieces in flight at once. CTA rank r computes the logits of experts
+// [r*E/8, (r+1)*E/8) for the tile's tokens: a warp takes two expert rows at
+// a time, reads them once with 16-byte loads (twelve per row and lane in
+// flight for one token, the first of them issued before the copy) and dots
+// them with every token's normalised row in shared memory; the 0.7 MB
+// projection is read once per tile and stays in L2. Warp w of every CTA
+// normalises tokens w, w + 8 of the tile. Token q is finished by warp q / 8
+// of rank q % 8, which gathers its E logits through distributed shared
+// memory; top-k is k rounds of a warp argmax.
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -55,6 +57,10 @@ __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
   return v;
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sm100::smem_u32(dst)), "l"(src) : "memory");
 }
 
 __device__ __forceinline__ void unpack8(const uint4& u, float* f) {
@@ -95,17 +101,19 @@ __global__ void __launch_bounds__(kRouterThreads) gemma4_router_kernel(const Rou
       wb[u] = eb < rows && i < h8 ? __ldg(wbase + (int64_t)eb * h8 + i) : make_uint4(0u, 0u, 0u, 0u);
     }
   }
-  // 0. the tile's token rows and the norm scale into shared memory (rows
-  //    past T are zero)
-#pragma unroll 4
-  for (int i = tid; i < h8; i += kRouterThreads)
-    reinterpret_cast<uint4*>(scs)[i] = __ldg(reinterpret_cast<const uint4*>(a.scale) + i);
-  for (int q = 0; q < NT; ++q) {
-    uint4* yq = reinterpret_cast<uint4*>(y + (size_t)q * H);
-    const uint4* xq = reinterpret_cast<const uint4*>(a.x + (t0 + q) * a.ldx);
-#pragma unroll 4
-    for (int i = tid; i < h8; i += kRouterThreads) yq[i] = q < nt ? xq[i] : make_uint4(0u, 0u, 0u, 0u);
+  // 0. the tile's token rows and the norm scale into shared memory, every
+  //    16-byte piece in flight at once (cp.async); rows past T are zero
+  for (int i = tid; i < h8; i += kRouterThreads) cp_async16(reinterpret_cast<uint4*>(scs) + i,
+                                                           reinterpret_cast<const uint4*>(a.scale) + i);
+  for (int j = tid; j < NT * h8; j += kRouterThreads) {
+    const int q = j / h8, i = j - q * h8;
+    uint4* dst = reinterpret_cast<uint4*>(y + (size_t)q * H) + i;
+    if (q < nt)
+      cp_async16(dst, reinterpret_cast<const uint4*>(a.x + (t0 + q) * a.ldx) + i);
+    else
+      *dst = make_uint4(0u, 0u, 0u, 0u);
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
   // 1. warp w: tokens t0 + w, t0 + w + 8, ... r = rsqrt(mean(x^2) + eps);
   //    y = bf16(bf16(bf16(x * r) * scale) * root), in place
@@ -176,14 +184,13 @@ __global__ void __launch_bounds__(kRouterThreads) gemma4_router_kernel(const Rou
     }
   }
   sm100::cluster_sync();
-  // 3. rank 0, warp w: tokens w, w + 8, ...: softmax, top-k,
-  //    renormalisation, per-expert scale. The token rows are no longer
-  //    needed: token q's probabilities and its selection live there.
-  for (int q = warp; rank == 0 && q < nt; q += kRouterThreads / 32) {
+  // 3. token q is finished by warp q / 8 of cluster rank q % 8: softmax,
+  //    top-k, renormalisation, per-expert scale. Top-k is k rounds of a
+  //    warp argmax over 64-bit keys (probability bits above the inverted
+  //    expert id): probabilities are >= +0, so the key order is descending
+  //    probability, equal values by lower expert id.
+  for (int q = (int)rank + kRouterCluster * warp; q < nt; q += kRouterCluster * (kRouterThreads / 32)) {
     const int64_t t = t0 + q;
-    float* pq = reinterpret_cast<float*>(smem) + (size_t)q * (E + 64);   // E probabilities
-    int* sidx = reinterpret_cast<int*>(pq + E);                         // 32 selected ids
-    float* sval = pq + E + 32;                                          // 32 selected values
     constexpr int kPer = kRouterMaxE / 32;
     float l[kPer], p[kPer];
     float mx = -INFINITY;
@@ -202,47 +209,47 @@ __global__ void __launch_bounds__(kRouterThreads) gemma4_router_kernel(const Rou
       sum += p[i];
     }
     sum = warp_sum(sum);
+    unsigned long long key[kPer];
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
       const int e = lane + 32 * i;
       p[i] = bf16r(p[i] / sum);
+      key[i] = 0ull;
       if (e < E) {
         a.probs[t * E + e] = __float2bfloat16_rn(p[i]);
-        pq[e] = p[i];
+        key[i] = ((unsigned long long)__float_as_uint(p[i]) << 32) | (0xFFFFFFFFu - (uint32_t)e);
       }
     }
-    __syncwarp();
-    // rank of each expert: how many probabilities beat it (larger value, or
-    // equal value and lower id); ranks below k are the top-k in order
+    float tot = 0.0f, myval = 0.0f;
+    int myidx = 0;
+    for (int j = 0; j < a.k; ++j) {
+      unsigned long long m = key[0];
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int e = lane + 32 * i;
-      if (e < E) {
-        int rk = 0;
-#pragma unroll 8
-        for (int f = 0; f < E; ++f) {
-          const float v = pq[f];
-          rk += (v > p[i]) | ((v == p[i]) & (f < e));
-        }
-        if (rk < a.k) {
-          sidx[rk] = e;
-          sval[rk] = p[i];
-        }
+      for (int i = 1; i < kPer; ++i) m = key[i] > m ? key[i] : m;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long v = __shfl_xor_sync(0xFFFFFFFFu, m, o);
+        m = v > m ? v : m;
+      }
+      const int e = (int)(0xFFFFFFFFu - (uint32_t)m);
+      const float v = __uint_as_float((uint32_t)(m >> 32));
+#pragma unroll
+      for (int i = 0; i < kPer; ++i)
+        if (key[i] == m) key[i] = 0ull;
+      tot += v;
+      if (lane == j) {
+        myidx = e;
+        myval = v;
       }
     }
-    __syncwarp();
-    float tot = 0.0f;
-    for (int j = 0; j < a.k; ++j) tot += sval[j];
     const float den = bf16r(tot);
     if (lane < a.k) {
-      const int isel = sidx[lane];
-      const float wj = bf16r(sval[lane] / den);
-      a.topw[t * a.k + lane] = __float2bfloat16_rn(wj * __bfloat162float(a.pes[isel]));
-      a.topi[t * a.k + lane] = isel;
+      const float wj = bf16r(myval / den);
+      a.topw[t * a.k + lane] = __float2bfloat16_rn(wj * __bfloat162float(a.pes[myidx]));
+      a.topi[t * a.k + lane] = myidx;
     }
-    __syncwarp();
   }
-  sm100::cluster_sync();   // rank 0 has read every CTA's logits
+  sm100::cluster_sync();   // every CTA's logits have been read
 }
 
 }  // namespace
