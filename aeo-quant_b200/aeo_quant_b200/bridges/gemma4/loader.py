@@ -45,6 +45,39 @@ def _preconvert_fp8_scales(model):
             module.down_proj_scale = module.down_proj_scale.squeeze(-1).unsqueeze(1).float().contiguous()
 
 
+def _from_pretrained(model_id_or_path, kwargs):
+    """``AutoModelForCausalLM.from_pretrained`` with the reference's
+    defaults (bf16, ``device_map="cuda"``, loader.py:87-88, :125-126).
+    ``device_map`` needs the ``accelerate`` package; without it, a
+    single-device map (a string or ``torch.device``) is honoured by loading
+    on the host and moving the model, and any other map is an error."""
+    from transformers import AutoModelForCausalLM
+    kwargs.setdefault("dtype", torch.bfloat16)
+    kwargs.setdefault("device_map", "cuda")
+    dev = kwargs.get("device_map")
+    move_to = None
+    if dev is not None:
+        try:
+            import accelerate  # noqa: F401
+        except ImportError:
+            if not isinstance(dev, (str, torch.device)) or str(dev) == "auto":
+                raise ValueError(f"device_map={dev!r} needs the accelerate package; pass a single device") from None
+            kwargs.pop("device_map")
+            move_to = torch.device(dev)
+    model = AutoModelForCausalLM.from_pretrained(model_id_or_path, **kwargs)
+    if move_to is not None:
+        model = model.to(move_to)
+    return model
+
+
+def _install_fused_routers(model):
+    """Fused router forward on a model whose weights are on a GPU."""
+    p = next(model.parameters(), None)
+    if p is not None and p.is_cuda:
+        swap_routers(model)
+    return model
+
+
 def load_gemma4(model_id_or_path, *, quant_format="fp8", **from_pretrained_kwargs):
     """Dispatch by format (loader.py:67-76)."""
     if quant_format == "nvfp4":
@@ -53,24 +86,23 @@ def load_gemma4(model_id_or_path, *, quant_format="fp8", **from_pretrained_kwarg
 
 
 def load_gemma4_fp8(model_id_or_path, **from_pretrained_kwargs):
-    """Load an FP8 checkpoint under the class swap (loader.py:79-92)."""
-    from transformers import AutoModelForCausalLM
-    from_pretrained_kwargs.setdefault("dtype", torch.bfloat16)
-    from_pretrained_kwargs.setdefault("device_map", "cuda")
+    """Load an FP8 checkpoint under the class swap (loader.py:79-92). On a
+    GPU the routers get the fused forward as well."""
     with gemma4_experts_fp8_class_swap():
-        model = AutoModelForCausalLM.from_pretrained(model_id_or_path, **from_pretrained_kwargs)
+        model = _from_pretrained(model_id_or_path, from_pretrained_kwargs)
     _preconvert_fp8_scales(model)
-    return model
+    return _install_fused_routers(model)
 
 
 def load_gemma4_nvfp4(model_id_or_path, **from_pretrained_kwargs):
-    """Load an NVFP4 checkpoint under the class swap (loader.py:111-138)."""
-    from transformers import AutoModelForCausalLM
-    from_pretrained_kwargs.setdefault("dtype", torch.bfloat16)
-    from_pretrained_kwargs.setdefault("device_map", "cuda")
+    """Load an NVFP4 checkpoint (``checkpoint.build_checkpoint_nvfp4``'s
+    output, or the reference builder's) under the class swap
+    (loader.py:111-138). The 0-d bf16 ``*_scale_2`` tensors load into the
+    modules' fp32 buffers. On a GPU the routers get the fused forward as
+    well."""
     with _gemma4_experts_nvfp4_class_swap():
-        model = AutoModelForCausalLM.from_pretrained(model_id_or_path, **from_pretrained_kwargs)
-    return model
+        model = _from_pretrained(model_id_or_path, from_pretrained_kwargs)
+    return _install_fused_routers(model)
 
 
 @torch.no_grad()
