@@ -18,8 +18,11 @@ the union of all ranks' tokens, bit for bit:
   them per token in ascending expert order with bf16 rounding after each
   add (``index_add_``, :250-253).
 
-Rank r owns experts [r * E/world, (r+1) * E/world). Pairs whose expert id
-is outside [0, E) are dropped (:209-211). ``ep_moe_forward`` is the
+By default rank r owns experts [r * E/world, (r+1) * E/world). A placement
+(``owner[e]`` = the rank holding expert e, E/world experts per rank, e.g.
+from ``balanced_placement`` for skewed routing) may replace that; a rank
+then holds its experts in ascending id order. Results do not depend on the
+placement. Pairs whose expert id is outside [0, E) are dropped (:209-211). ``ep_moe_forward`` is the
 orchestration shared by every backend; the expert arithmetic, the payload
 codec and the combine are supplied by an ``ops`` object (``NVFP4EpOps``
 for the CUDA library).
@@ -40,8 +43,59 @@ def _all_to_all_rows(rows: torch.Tensor, send_counts, recv_counts, group) -> tor
     return out
 
 
-def plan_dispatch(top_k_index: torch.Tensor, num_experts: int, world: int):
-    """Send order of the (token, slot) pairs, grouped by owning rank.
+def contiguous_placement(num_experts: int, world: int) -> torch.Tensor:
+    """owner[e] = e // (E/world): rank r holds experts [r*E/world, (r+1)*E/world)."""
+    if num_experts % world:
+        raise ValueError(f"num_experts ({num_experts}) must be divisible by the world size ({world})")
+    return torch.arange(num_experts) // (num_experts // world)
+
+
+def balanced_placement(load, world: int) -> torch.Tensor:
+    """A placement with E/world experts per rank that evens out the ranks'
+    expected rows: experts by descending ``load`` (ties by id) each go to
+    the least-loaded rank that still has room (ties by rank). ``load`` is
+    any per-expert weight, e.g. a routing histogram. Returns owner (E,)
+    int64 on the host."""
+    load = torch.as_tensor(load, dtype=torch.float64).reshape(-1).cpu()
+    E = load.numel()
+    if E % world:
+        raise ValueError(f"num_experts ({E}) must be divisible by the world size ({world})")
+    cap = E // world
+    order = sorted(range(E), key=lambda e: (-float(load[e]), e))
+    owner = torch.empty(E, dtype=torch.int64)
+    tot = [0.0] * world
+    room = [cap] * world
+    for e in order:
+        r = min((r for r in range(world) if room[r]), key=lambda r: (tot[r], r))
+        owner[e] = r
+        tot[r] += float(load[e])
+        room[r] -= 1
+    return owner
+
+
+def local_index(owner: torch.Tensor, world: int) -> torch.Tensor:
+    """local[e] = position of expert e among its owner's experts (ascending
+    id). Raises ValueError unless every rank owns E/world experts."""
+    owner = torch.as_tensor(owner, dtype=torch.int64).reshape(-1).cpu()
+    E = owner.numel()
+    if E % world or bool(((owner < 0) | (owner >= world)).any()):
+        raise ValueError("placement must map every expert to a rank in [0, world)")
+    counts = torch.bincount(owner, minlength=world)
+    if bool((counts != E // world).any()):
+        raise ValueError(f"placement must give every rank {E // world} experts, got {counts.tolist()}")
+    local = torch.empty(E, dtype=torch.int64)
+    seen = [0] * world
+    for e in range(E):
+        r = int(owner[e])
+        local[e] = seen[r]
+        seen[r] += 1
+    return local
+
+
+def plan_dispatch(top_k_index: torch.Tensor, num_experts: int, world: int, owner: torch.Tensor | None = None):
+    """Send order of the (token, slot) pairs, grouped by owning rank
+    (``owner`` (E,) as from ``balanced_placement``; contiguous blocks when
+    None).
 
     Returns ``(send_pairs, send_counts, dest)``: pair indices (t * k + j) in
     send order (by destination rank, then pair index), pairs per destination
@@ -52,7 +106,11 @@ def plan_dispatch(top_k_index: torch.Tensor, num_experts: int, world: int):
     ids = top_k_index.reshape(-1).to(torch.int64)
     n = ids.numel()
     valid = (ids >= 0) & (ids < num_experts)
-    dest = torch.where(valid, torch.div(ids, e_loc, rounding_mode="floor"), torch.full_like(ids, world))
+    if owner is None:
+        dest = torch.where(valid, torch.div(ids, e_loc, rounding_mode="floor"), torch.full_like(ids, world))
+    else:
+        owner = owner.to(ids.device)
+        dest = torch.where(valid, owner[ids.clamp(0, num_experts - 1)], torch.full_like(ids, world))
     key = dest * n + torch.arange(n, device=ids.device)
     order = torch.argsort(key)
     counts = torch.bincount(dest, minlength=world + 1)[:world]
@@ -60,14 +118,22 @@ def plan_dispatch(top_k_index: torch.Tensor, num_experts: int, world: int):
     return order[:n_send], counts, dest
 
 
-def ep_moe_forward(hidden, top_k_index, top_k_weights, *, num_experts: int, group, ops):
-    """One expert-parallel MoE layer over ``group`` (see module docstring)."""
+def ep_moe_forward(hidden, top_k_index, top_k_weights, *, num_experts: int, group, ops, owner=None):
+    """One expert-parallel MoE layer over ``group`` (see module docstring).
+    ``owner``: optional placement (E,) of experts on ranks."""
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     e_loc = num_experts // world
     T, k = top_k_index.shape
     dev = hidden.device
-    send_pairs, send_counts, _ = plan_dispatch(top_k_index, num_experts, world)
+    if owner is None:
+        my_experts = torch.arange(rank * e_loc, (rank + 1) * e_loc)
+        local_of = None
+    else:
+        owner = torch.as_tensor(owner, dtype=torch.int64).reshape(-1).cpu()
+        local_of = local_index(owner, world).to(dev)
+        my_experts = torch.nonzero(owner == rank).reshape(-1)
+    send_pairs, send_counts, _ = plan_dispatch(top_k_index, num_experts, world, owner)
 
     # counts: one small all-to-all, then the split sizes on the host
     recv_counts_t = torch.empty_like(send_counts)
@@ -80,13 +146,16 @@ def ep_moe_forward(hidden, top_k_index, top_k_weights, *, num_experts: int, grou
     send_tok = torch.div(send_pairs, k, rounding_mode="floor")
     ids = top_k_index.reshape(-1).to(torch.int64)
     wbits = top_k_weights.reshape(-1).to(torch.bfloat16).view(torch.int16).to(torch.int32)
-    local_id = (ids[send_pairs] - torch.div(ids[send_pairs], e_loc, rounding_mode="floor") * e_loc).to(torch.int32)
+    if local_of is None:
+        local_id = (ids[send_pairs] - torch.div(ids[send_pairs], e_loc, rounding_mode="floor") * e_loc).to(torch.int32)
+    else:
+        local_id = local_of[ids[send_pairs]].to(torch.int32)
     meta = torch.stack([local_id, wbits[send_pairs]], dim=1)
 
     recv_payload = [_all_to_all_rows(p[send_tok], sc, rc, group) for p in payload]
     recv_meta = _all_to_all_rows(meta, sc, rc, group)
     recv_w = recv_meta[:, 1].to(torch.int16).view(torch.bfloat16)
-    out_rows = ops.experts(recv_payload, recv_meta[:, 0], recv_w, ts, rank * e_loc)   # (n_recv, H)
+    out_rows = ops.experts(recv_payload, recv_meta[:, 0], recv_w, ts, my_experts)   # (n_recv, H)
 
     back = _all_to_all_rows(out_rows, rc, sc, group)     # in this rank's send order
     pair_row = torch.full((T * k,), -1, dtype=torch.int32, device=dev)
@@ -114,7 +183,7 @@ class NVFP4EpOps:
         packed, sf, _ = _nvfp4_quantize_rows(hidden.contiguous(), ts)
         return [packed, sf.view(torch.uint8)]
 
-    def experts(self, payload, local_ids, weights, ts, first_expert):
+    def experts(self, payload, local_ids, weights, ts, my_experts):
         packed, sf = payload
         n = packed.shape[0]
         H = self.dw.shape[1]
@@ -141,15 +210,17 @@ class NVFP4EpOps:
 class ExpertParallelNVFP4(torch.nn.Module):
     """One rank's share of an expert-parallel ``Gemma4TextExpertsNVFP4``.
 
-    Holds experts [rank * E/world, (rank+1) * E/world) with the reference's
-    buffer names (first dimension E/world); ``forward`` takes this rank's
-    tokens and returns their outputs."""
+    Holds experts [rank * E/world, (rank+1) * E/world), or with ``owner``
+    the experts e with owner[e] == rank in ascending id order, with the
+    reference's buffer names (first dimension E/world); ``forward`` takes
+    this rank's tokens and returns their outputs."""
 
-    def __init__(self, local_experts, num_experts: int, group=None):
+    def __init__(self, local_experts, num_experts: int, group=None, owner=None):
         super().__init__()
         self.local = local_experts
         self.num_experts = num_experts
         self.group = group
+        self.owner = None if owner is None else torch.as_tensor(owner, dtype=torch.int64).reshape(-1).cpu()
 
     def forward(self, hidden_states, top_k_index, top_k_weights):
         m = self.local
@@ -158,4 +229,4 @@ class ExpertParallelNVFP4(torch.nn.Module):
         ops = NVFP4EpOps(m.gate_up_proj, m.gate_up_proj_scale, m.gate_up_proj_scale_2,
                          m.down_proj, m.down_proj_scale, m.down_proj_scale_2)
         return ep_moe_forward(hidden_states, top_k_index, top_k_weights, num_experts=self.num_experts,
-                              group=self.group, ops=ops)
+                              group=self.group, ops=ops, owner=self.owner)

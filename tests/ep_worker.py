@@ -21,7 +21,10 @@ from oracle.gemm import nvfp4_gemm, nvfp4_linear  # noqa: E402
 
 
 def case_inputs(case):
-    """Deterministic layer and tokens shared by the workers and the test."""
+    """Deterministic layer and tokens shared by the workers and the test.
+    Case 2 is case 1's skewed routing, run with a balanced placement."""
+    if case == 2:
+        return case_inputs(1)
     g = np.load(os.path.join(HERE, "golden", "moe_golden.npz"))
     m = OM.NVFP4Experts(g["nv/gate_up_proj"], g["nv/gate_up_proj_scale"], g["nv/gate_up_proj_scale_2"][0],
                         g["nv/down_proj"], g["nv/down_proj_scale"], g["nv/down_proj_scale_2"][0])
@@ -53,7 +56,7 @@ class OracleEpOps:
         p, s, _ = OQ.quantize_nvfp4(hidden.to(torch.float32).numpy(), "bf16", ts=ts)
         return [torch.from_numpy(p), torch.from_numpy(s)]
 
-    def experts(self, payload, local_ids, weights, ts, first):
+    def experts(self, payload, local_ids, weights, ts, my_experts):
         p, s = (t.numpy() for t in payload)
         lid = local_ids.numpy()
         w = weights.to(torch.float32).numpy()
@@ -61,7 +64,7 @@ class OracleEpOps:
         out = np.zeros((p.shape[0], H), np.float32)
         for le in np.unique(lid):
             rows = np.nonzero(lid == le)[0]
-            e = first + le
+            e = int(my_experts[le])
             gu = nvfp4_gemm(p[rows], s[rows], ts, self.m.gate_up_proj[e], self.m.gate_up_proj_scale[e],
                             self.m.gate_up_proj_scale_2)
             d = nvfp4_linear(OM.geglu(gu), self.m.down_proj[e], self.m.down_proj_scale[e], self.m.down_proj_scale_2)
@@ -86,15 +89,20 @@ def main():
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = port
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    from aeo_quant_b200.bridges.gemma4.expert_parallel import ep_moe_forward
+    from aeo_quant_b200.bridges.gemma4.expert_parallel import balanced_placement, ep_moe_forward
     m, hidden, ids, w = case_inputs(case)
     E = m.num_experts
     T = hidden.shape[0]
     lo, hi = rank * T // world, (rank + 1) * T // world
     e_loc = E // world
     ops = OracleEpOps(m, rank * e_loc, e_loc)
+    owner = None
+    if case == 2:
+        load = np.bincount(ids[(ids >= 0) & (ids < E)], minlength=E)
+        owner = balanced_placement(torch.from_numpy(load), world)
     y = ep_moe_forward(torch.from_numpy(hidden[lo:hi]).to(torch.bfloat16), torch.from_numpy(ids[lo:hi]),
-                       torch.from_numpy(w[lo:hi]).to(torch.bfloat16), num_experts=E, group=None, ops=ops)
+                       torch.from_numpy(w[lo:hi]).to(torch.bfloat16), num_experts=E, group=None, ops=ops,
+                       owner=owner)
     np.savez(out_path, y=y.numpy(), lo=lo, hi=hi)
     dist.destroy_process_group()
 

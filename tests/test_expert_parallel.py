@@ -21,7 +21,7 @@ def _free_port():
         return str(s.getsockname()[1])
 
 
-@pytest.mark.parametrize("case", [0, 1])
+@pytest.mark.parametrize("case", [0, 1, 2])
 def test_ep_two_ranks_match_one_process(tmp_path, case):
     sys.path.insert(0, HERE)
     from ep_worker import case_inputs
@@ -57,3 +57,32 @@ def test_plan_dispatch_groups_pairs_by_rank():
     assert dest.tolist() == [1, 0, 1, 0, 2, 1]          # id 8 (== E) is dropped
     with pytest.raises(ValueError, match="divisible by the world size"):
         plan_dispatch(ids, 8, 3)
+
+
+def test_balanced_placement_and_local_index():
+    sys.path.insert(0, os.path.join(os.path.dirname(HERE), "aeo-quant_b200"))
+    from aeo_quant_b200.bridges.gemma4.expert_parallel import (balanced_placement, contiguous_placement,
+                                                               local_index, plan_dispatch)
+    # Zipf-like load over 16 experts, hot experts at the low ids
+    load = torch.tensor([1.0 / (e + 1) ** 1.2 for e in range(16)])
+    owner = balanced_placement(load, 4)
+    assert torch.bincount(owner, minlength=4).tolist() == [4, 4, 4, 4]
+    per_rank = torch.zeros(4, dtype=torch.float64).index_add_(0, owner, load.double())
+    contig = torch.zeros(4, dtype=torch.float64).index_add_(0, contiguous_placement(16, 4), load.double())
+    assert per_rank.max() < contig.max()
+    # the hottest expert's rank is filled up with the coldest ones
+    assert per_rank.max() <= load.double().max() + load.double().sort().values[:3].sum() + 1e-9
+    assert owner[:4].tolist() == [0, 1, 2, 3]          # the four hottest go to different ranks
+    local = local_index(owner, 4)
+    for r in range(4):
+        mine = torch.nonzero(owner == r).reshape(-1)
+        assert local[mine].tolist() == list(range(4))
+    ids = torch.tensor([[0, 5], [16, 1]])               # 16 == E: dropped
+    send, counts, dest = plan_dispatch(ids, 16, 4, owner)
+    assert dest.tolist() == [int(owner[0]), int(owner[5]), 4, int(owner[1])]
+    assert counts.sum().item() == 3
+    assert torch.equal(local_index(contiguous_placement(16, 4), 4), torch.arange(16) % 4)
+    with pytest.raises(ValueError, match="every rank"):
+        local_index(torch.zeros(16, dtype=torch.int64), 4)
+    with pytest.raises(ValueError, match="divisible"):
+        balanced_placement(load, 3)
