@@ -53,6 +53,11 @@ _SIGS["aeoq_fp8_gemm"] = [_P, _P, _L, _P, _P, _L, _L, _P, _P, _P]
 _SIGS["aeoq_fp8_gemm_grouped"] = [_P, _P, _L, _P, _P, _I, _P, _P, _L, _L, _L, _I, _P, _P, _L, _P, _P]
 _SIGS["aeoq_fp8_quantize_rows_gather"] = [_P, _L, _P, _P, _L, _L, _P, _L, _P, _P]
 _SIGS["aeoq_gemma4_router"] = [_P, _L, _P, _P, _P, _L, _L, _L, _L, _F, _F, _P, _P, _P, _P]
+_SIGS["aeoq_moe_nvfp4_forward_workspace_size"] = [_L, _L, _L, _L, _L]
+_SIGS["aeoq_moe_nvfp4_forward"] = [_P, _L, _P, _I, _P, _L, _P, _P, _P, _I, _P, _P, _P, _I, _L, _L, _L, _I, _P, _P,
+                                   _Z, _P, _P]
+_SIGS["aeoq_moe_fp8_forward_workspace_size"] = [_L, _L, _L, _L, _L]
+_SIGS["aeoq_moe_fp8_forward"] = [_P, _L, _P, _I, _P, _L, _P, _P, _P, _P, _L, _L, _L, _P, _P, _Z, _P, _P]
 _SIGS["aeoq_moe_nvfp4_decode_tc_supported"] = [_L, _L, _L]
 _SIGS["aeoq_moe_nvfp4_decode_tc_workspace_size"] = [_L, _L, _L]
 _SIGS["aeoq_moe_nvfp4_decode_tc"] = [_P, _P, _I, _P, _L, _P, _P, _P, _I, _P, _P, _P, _I, _L, _L, _L, _P, _P, _Z, _P, _P]
@@ -70,7 +75,9 @@ _RESTYPE = {"aeoq_moe_nvfp4_decode_tc_workspace_size": C.c_size_t,
             "aeoq_last_error": C.c_char_p, "aeoq_nvfp4_quantize_workspace_size": C.c_size_t,
             "aeoq_moe_nvfp4_decode_workspace_size": C.c_size_t,
             "aeoq_moe_nvfp4_decode_fused_workspace_size": C.c_size_t,
-            "aeoq_moe_nvfp4_decode_fused_noalloc_max_scratch": C.c_size_t}
+            "aeoq_moe_nvfp4_decode_fused_noalloc_max_scratch": C.c_size_t,
+            "aeoq_moe_nvfp4_forward_workspace_size": C.c_size_t,
+            "aeoq_moe_fp8_forward_workspace_size": C.c_size_t}
 
 _lib = None
 

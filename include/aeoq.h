@@ -240,6 +240,44 @@ AEOQ_API int aeoq_moe_combine(const void* c_sorted, const int* pair_row, const v
                               int64_t T, int64_t k, int64_t H, int mode, void* out, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Whole expert-layer forwards, one call each (the launch sequence of the
+ * Python layer over one caller-provided workspace; nothing is allocated,
+ * nothing synchronises with the host). hidden (T, H) bf16 contiguous;
+ * top_k_index (T, k) int32/int64 (idx_dtype), ids outside [0, E) dropped;
+ * top_k_weights (T, k) bf16; out (T, H) bf16. err_word: device int that a
+ * tensor-core wait which times out sets nonzero.
+ *
+ * aeoq_moe_nvfp4_forward replaces Gemma4TextExpertsNVFP4._forward_prefill
+ * (src/aeo_quant/bridges/gemma4/modeling_nvfp4.py:188-255): one global
+ * activation tensor scale, per-expert re-quantized down input, bf16
+ * index_add_ fold. one_token_semantics = 1 gives the rounding of
+ * _forward_decode_3d (:132-186): one shared down-input scale, f32 combine.
+ * gate_up (E, 2I, H/2) / down (E, H, I/2) packed E2M1; their scales as
+ * weight atoms from aeoq_nvfp4_sf_to_atoms (gate_up with geglu_inter = I,
+ * down with 0); *_ts 0-d tensor scales (f32 or bf16 per *_ts_dtype).
+ *
+ * aeoq_moe_fp8_forward replaces Gemma4TextExpertsFP8.forward
+ * (src/aeo_quant/bridges/gemma4/modeling.py:110-146): gate_up (E, 2I, H) and
+ * down (E, H, I) e4m3, per-output-channel scales flat f32 (E * 2I), (E * H).
+ * ------------------------------------------------------------------------ */
+AEOQ_API size_t aeoq_moe_nvfp4_forward_workspace_size(int64_t T, int64_t top_k, int64_t num_experts,
+                                                      int64_t hidden, int64_t inter);
+AEOQ_API int aeoq_moe_nvfp4_forward(const void* hidden, int64_t T, const void* top_k_index, int idx_dtype,
+                                    const void* top_k_weights, int64_t top_k, const uint8_t* gate_up,
+                                    const uint8_t* gate_up_atoms, const void* gate_up_ts, int gate_up_ts_dtype,
+                                    const uint8_t* down, const uint8_t* down_atoms, const void* down_ts,
+                                    int down_ts_dtype, int64_t num_experts, int64_t hidden_size, int64_t inter,
+                                    int one_token_semantics, void* out, void* workspace, size_t workspace_bytes,
+                                    int* err_word, void* stream);
+AEOQ_API size_t aeoq_moe_fp8_forward_workspace_size(int64_t T, int64_t top_k, int64_t num_experts, int64_t hidden,
+                                                    int64_t inter);
+AEOQ_API int aeoq_moe_fp8_forward(const void* hidden, int64_t T, const void* top_k_index, int idx_dtype,
+                                  const void* top_k_weights, int64_t top_k, const uint8_t* gate_up,
+                                  const float* gate_up_scale, const uint8_t* down, const float* down_scale,
+                                  int64_t num_experts, int64_t hidden_size, int64_t inter, void* out,
+                                  void* workspace, size_t workspace_bytes, int* err_word, void* stream);
+
+/* ------------------------------------------------------------------------
  * One-token NVFP4 MoE expert forward, fully fused (two launches).
  * Replaces Gemma4TextExpertsNVFP4._forward_decode_3d
  * (src/aeo_quant/bridges/gemma4/modeling_nvfp4.py:132-186): hidden quant ->

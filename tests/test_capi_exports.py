@@ -64,6 +64,23 @@ def test_workspace_sizes(lib):
     assert lib.aeoq_nvfp4_quantize_workspace_size(1, 2816) == 0
     assert lib.aeoq_nvfp4_quantize_workspace_size(1408, 2816) > 0
     assert lib.aeoq_moe_nvfp4_decode_workspace_size(8, 2816, 704) >= 8 * 704 * 2
+    # whole-layer forwards: at least the sorted (pairs, H) bf16 outputs, growing with T, 0 for no tokens
+    for fn in (lib.aeoq_moe_nvfp4_forward_workspace_size, lib.aeoq_moe_fp8_forward_workspace_size):
+        assert fn(0, 8, 128, 2816, 704) == 0
+        assert fn(64, 8, 128, 2816, 704) >= 64 * 8 * 2816 * 2
+        assert fn(4096, 8, 128, 2816, 704) > fn(64, 8, 128, 2816, 704)
+
+
+def test_whole_layer_forward_validation(lib):
+    # no tokens: nothing to do, no pointer touched
+    assert lib.aeoq_moe_nvfp4_forward(None, 0, None, 4, None, 8, None, None, None, 2, None, None, None, 2,
+                                      128, 2816, 704, 0, None, None, 0, None, None) == 0
+    rc = lib.aeoq_moe_nvfp4_forward(None, 4, None, 4, None, 99, None, None, None, 2, None, None, None, 2,
+                                    128, 2816, 704, 0, None, None, 0, None, None)
+    assert rc == -1 and b"bad shape" in lib.aeoq_last_error()
+    rc = lib.aeoq_moe_fp8_forward(None, 4, None, 4, None, 8, None, None, None, None, 128, 2816, 704, None,
+                                  None, 0, None, None)
+    assert rc == -1 and b"null pointer" in lib.aeoq_last_error()
 
 
 def test_python_api_refuses_cpu_tensors():
