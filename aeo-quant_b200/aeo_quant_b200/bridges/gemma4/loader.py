@@ -71,10 +71,11 @@ def _from_pretrained(model_id_or_path, kwargs):
 
 
 def _install_fused_routers(model):
-    """Fused router forward on a model whose weights are on a GPU."""
+    """Fused router forward on a model whose weights are on a GPU, for every
+    router whose shapes the kernel takes (the others keep HF's forward)."""
     p = next(model.parameters(), None)
     if p is not None and p.is_cuda:
-        swap_routers(model)
+        swap_routers(model, only_supported=True)
     return model
 
 
@@ -169,13 +170,15 @@ def gemma4_router_class_swap():
     return _cm()
 
 
-def swap_routers(model):
+def swap_routers(model, only_supported: bool = False):
     """Give every ``Gemma4TextRouter`` in a built model the fused forward
-    (its parameters stay where they are). Returns the number swapped."""
-    from .router import Gemma4TextRouterB200
+    (its parameters stay where they are). With ``only_supported``, routers
+    whose shapes the kernel does not take are left as they are. Returns the
+    number swapped."""
+    from .router import Gemma4TextRouterB200, router_supported
     n = 0
     for mod in model.modules():
-        if type(mod) is modeling_gemma4.Gemma4TextRouter:
+        if type(mod) is modeling_gemma4.Gemma4TextRouter and (not only_supported or router_supported(mod)):
             mod.__class__ = Gemma4TextRouterB200
             n += 1
     return n

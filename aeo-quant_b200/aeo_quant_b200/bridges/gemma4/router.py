@@ -19,6 +19,15 @@ from transformers.models.gemma4.modeling_gemma4 import Gemma4TextRouter
 from ... import _capi as A
 
 
+def router_supported(router) -> bool:
+    """True if the fused kernel takes this router's shapes: hidden size H a
+    multiple of 8 with 2E + 128 <= H <= 6144, E a multiple of 8 up to 256,
+    top_k <= min(E, 32) (the limits ``aeoq_gemma4_router`` checks)."""
+    E, H = router.proj.weight.shape
+    k = int(router.config.top_k_experts)
+    return (H % 8 == 0 and 2 * E + 128 <= H <= 6144 and E % 8 == 0 and E <= 256 and 1 <= k <= min(E, 32))
+
+
 class Gemma4TextRouterB200(Gemma4TextRouter):
     """Gemma4TextRouter with a fused CUDA forward (bf16 only)."""
 

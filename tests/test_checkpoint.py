@@ -154,3 +154,16 @@ def test_device_map_without_accelerate():
     from aeo_quant_b200.bridges.gemma4.loader import load_gemma4_nvfp4
     with pytest.raises(ValueError, match="accelerate"):
         load_gemma4_nvfp4("/nonexistent", device_map="auto")
+
+
+def test_router_swap_only_supported_shapes():
+    import torch.nn as nn
+    from test_router_oracle import hf_router
+    from aeo_quant_b200.bridges.gemma4.loader import swap_routers
+    from aeo_quant_b200.bridges.gemma4.router import Gemma4TextRouterB200, router_supported
+    ok, odd, narrow = hf_router(2816, 128, 8, 1, 0.02), hf_router(2816, 12, 4, 1, 0.02), hf_router(256, 128, 8, 1, 0.02)
+    assert router_supported(ok) and not router_supported(odd) and not router_supported(narrow)
+    seq = nn.Sequential(ok, odd, narrow)
+    assert swap_routers(seq, only_supported=True) == 1
+    assert type(ok) is Gemma4TextRouterB200 and type(odd) is not Gemma4TextRouterB200
+    assert swap_routers(seq) == 2          # an explicit swap takes every router
