@@ -118,6 +118,18 @@ def plan_dispatch(top_k_index: torch.Tensor, num_experts: int, world: int, owner
     return order[:n_send], counts, dest
 
 
+def global_amax(hidden: torch.Tensor, group) -> torch.Tensor:
+    """max |hidden| over every rank's tokens as a 1-element f32 tensor (one
+    all-reduce(max)). A rank without tokens (decode with fewer tokens than
+    ranks) contributes 0 and still joins the collective, so no peer waits."""
+    if hidden.numel():
+        amax = hidden.abs().amax().to(torch.float32).reshape(1)
+    else:
+        amax = torch.zeros(1, dtype=torch.float32, device=hidden.device)
+    dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=group)
+    return amax
+
+
 def ep_moe_forward(hidden, top_k_index, top_k_weights, *, num_experts: int, group, ops, owner=None):
     """One expert-parallel MoE layer over ``group`` (see module docstring).
     ``owner``: optional placement (E,) of experts on ranks."""
@@ -141,7 +153,7 @@ def ep_moe_forward(hidden, top_k_index, top_k_weights, *, num_experts: int, grou
     sc = send_counts.tolist()
     rc = recv_counts_t.tolist()
 
-    ts = ops.global_scale(hidden, group)
+    ts = ops.tensor_scale(global_amax(hidden, group), hidden.dtype)
     payload = ops.encode(hidden, ts)                     # per-token row tensors
     send_tok = torch.div(send_pairs, k, rounding_mode="floor")
     ids = top_k_index.reshape(-1).to(torch.int64)
@@ -172,12 +184,9 @@ class NVFP4EpOps:
         self.dw, self.dw_sf, self.dw_ts = dw, dw_sf, dw_ts
         self.lib = A.load()
 
-    def global_scale(self, hidden, group):
-        # amax over every rank's tokens, then ts = bf16(amax / 2688) >= 1e-12
-        # in the input dtype (quant.py:167-168)
-        amax = hidden.abs().amax().to(torch.float32).reshape(1)
-        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=group)
-        return (amax[0].to(hidden.dtype) / 2688.0).clamp(min=1e-12)
+    def tensor_scale(self, amax, dtype):
+        # ts = amax / 2688 in the input dtype, at least 1e-12 (quant.py:167-168)
+        return (amax[0].to(dtype) / 2688.0).clamp(min=1e-12)
 
     def encode(self, hidden, ts):
         packed, sf, _ = _nvfp4_quantize_rows(hidden.contiguous(), ts)

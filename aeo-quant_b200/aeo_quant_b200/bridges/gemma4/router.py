@@ -20,11 +20,15 @@ from ... import _capi as A
 
 
 def router_supported(router) -> bool:
-    """True if the fused kernel takes this router's shapes: hidden size H a
+    """True if the fused kernel takes this router: bfloat16 parameters
+    (``proj.weight``, ``scale``, ``per_expert_scale``), hidden size H a
     multiple of 8 with 2E + 128 <= H <= 6144, E a multiple of 8 up to 256,
-    top_k <= min(E, 32) (the limits ``aeoq_gemma4_router`` checks)."""
+    top_k <= min(E, 32) (the limits ``aeoq_gemma4_router`` checks). A router
+    loaded in another dtype keeps HF's forward."""
     E, H = router.proj.weight.shape
     k = int(router.config.top_k_experts)
+    if any(t.dtype != torch.bfloat16 for t in (router.proj.weight, router.scale, router.per_expert_scale)):
+        return False
     return (H % 8 == 0 and 2 * E + 128 <= H <= 6144 and E % 8 == 0 and E <= 256 and 1 <= k <= min(E, 32))
 
 

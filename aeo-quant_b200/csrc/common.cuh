@@ -25,6 +25,17 @@ namespace aeoq {
 int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
 
+// Per-device launch set-up. Function attributes belong to the context of the
+// device that is current when they are set, and the SM count is a property of
+// that device, so both are cached per (device, function) under a mutex: a
+// process that drives several GPUs sets each attribute once on each of them.
+// func_smem_attr raises the function's dynamic shared-memory limit to at
+// least `bytes` on the current device (and, with carveout >= 0, its preferred
+// shared-memory carveout); returns AEOQ_OK or an AEOQ error code.
+int func_smem_attr(const void* func, size_t bytes, int carveout, const char* what);
+// Multiprocessor count of the current device (148 on B200).
+int device_sm_count();
+
 #define AEOQ_REQUIRE(cond, code, ...)                     \
   do {                                                    \
     if (!(cond)) return ::aeoq::set_error((code), __VA_ARGS__); \

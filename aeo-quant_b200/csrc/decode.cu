@@ -286,17 +286,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) moe_decode_down_kernel(
   }
 }
 
-static int g_num_sms = 0;
-
-static int num_sms() {
-  if (!g_num_sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_num_sms <= 0) g_num_sms = 148;
-  }
-  return g_num_sms;
-}
+static int num_sms() { return device_sm_count(); }
 
 static int gateup_grid(int64_t k, int64_t I) {
   const int64_t pairs = k * I;
@@ -338,16 +328,6 @@ extern "C" size_t aeoq_moe_nvfp4_decode_workspace_size(int64_t top_k, int64_t hi
   return decode_ws(nullptr, top_k, inter).bytes;
 }
 
-// Programmatic dependent launch can be switched off with AEOQ_NO_PDL=1
-// (plain stream order; used to isolate ordering issues).
-static bool pdl_enabled() {
-  static const bool on = [] {
-    const char* v = getenv("AEOQ_NO_PDL");
-    return !(v && v[0] == '1');
-  }();
-  return on;
-}
-
 template <typename... KArgs, typename... Args>
 static int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, const char* name,
                       Args... args) {
@@ -359,7 +339,7 @@ static int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
   if (e != cudaSuccess) {
     cudaGetLastError();

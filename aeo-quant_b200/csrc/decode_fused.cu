@@ -398,16 +398,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_decode_fused_kernel(FusedArg
   }
 }
 
-static int fused_grid() {
-  static int g = 0;
-  if (!g) {
-    int dev = 0, n = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    g = n > 0 ? n : 148;
-  }
-  return g;
-}
+static int fused_grid() { return device_sm_count(); }
 
 }  // namespace aeoq
 
@@ -465,16 +456,9 @@ extern "C" int aeoq_moe_nvfp4_decode_fused(const void* hidden, const void* top_k
   a.sync = reinterpret_cast<uint32_t*>(w);
   a.parts = reinterpret_cast<uint32_t*>(w + 256);
   a.h = reinterpret_cast<__nv_bfloat16*>(w + 256 + ((size_t)G * 4 + 255) / 256 * 256);
-  static size_t attr_bytes = 0;
-  if (attr_bytes < s.bytes) {
-    cudaError_t e = cudaFuncSetAttribute(moe_decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)s.bytes);
-    if (e != cudaSuccess) {
-      cudaGetLastError();   // do not leave the error for the next launch check
-      return set_error(AEOQ_ERR_CUDA, "moe_decode_fused: shared memory attribute (%zu B): %s", s.bytes,
-                       cudaGetErrorString(e));
-    }
-    attr_bytes = s.bytes;
+  {
+    const int rc = func_smem_attr((const void*)moe_decode_fused_kernel, s.bytes, -1, "moe_decode_fused");
+    if (rc) return rc;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)G);

@@ -61,21 +61,6 @@ __device__ __forceinline__ int cta_linear() {
   return (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
 }
 
-#ifdef AEOQ_TC_TRACE
-__device__ uint64_t* g_dtrace = nullptr;
-#define DT(slot)                                                                                     \
-  do {                                                                                               \
-    if (g_dtrace) {                                                                                  \
-      uint64_t t_;                                                                                   \
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                         \
-      g_dtrace[(kTraceBase + cta_linear()) * 32 + (slot)] = t_;                                       \
-    }                                                                                                \
-  } while (0)
-#define TRACE_BASE(v) constexpr int kTraceBase = (v)
-#else
-#define DT(slot) do {} while (0)
-#define TRACE_BASE(v)
-#endif
 
 constexpr int kThreads = 192;      // launch 2
 constexpr int kThreads1 = 256;     // launch 1: two more producer warps (6, 7)
@@ -296,7 +281,6 @@ __device__ __forceinline__ uint32_t block_max128(uint32_t key, int t, uint32_t* 
 __global__ void __launch_bounds__(kThreads1, 1)
     decode_gateup_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmS,
                             const Args a, const Plan pl) {
-  TRACE_BASE(0);
   extern __shared__ __align__(1024) uint8_t dsm[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
   const L1 L(pl);
@@ -311,7 +295,6 @@ __global__ void __launch_bounds__(kThreads1, 1)
   const int m = blockIdx.x, p = blockIdx.y, j = blockIdx.z;
   const int T = pl.T, N1 = 2 * T, H = pl.H, I = pl.I;
   const int kb0 = p * pl.Q, nkb = min(pl.Q, H / 64 - kb0), nt = (nkb + 3) / 4;
-  if (tid == 0) DT(0);
 
   if (tid == 0) {
     for (int s = 0; s < kRing; ++s) {
@@ -386,7 +369,6 @@ __global__ void __launch_bounds__(kThreads1, 1)
     const uint32_t idesc = sm100::idesc_nvf4((uint32_t)N1);
     bool ok = sm100::mbar_wait(&sh->bready, 0, a.err, 42);
     sm100::tc_fence_after();
-    if (tid == 32) DT(2);
     for (int kt = 0; kt < nt && ok && valid; ++kt) {
       const int s = kt % kRing;
       const uint32_t ph = (kt / kRing) & 1;
@@ -430,19 +412,14 @@ __global__ void __launch_bounds__(kThreads1, 1)
     }
     sm100::fence_proxy_async_smem();   // token tiles: generic writes -> MMA reads
     asm volatile("bar.sync 2, 128;" ::: "memory");
-    if (t == 0) DT(1);
     if (warp == 4) st_token_scales(tmem + qaddr + pl.sfa1, tok, nkb, lane);
-    if (t == 0) DT(5);
-    if (t == 0) DT(7);
     sm100::tmem_st_wait();
-    if (t == 0) DT(8);
     sm100::tc_fence_before();
     __syncwarp();
     if (lane == 0) sm100::mbar_arrive(&sh->bready);
     alpha = ts * load_scalar_f(a.gu_ts, a.gu_ts_dt);
     const bool ok = sm100::mbar_wait(&sh->accum, 0, a.err, 46);
     sm100::tc_fence_after();
-    if (t == 0) DT(3);
     if (warp == 4) read_row0(tmem, N1, ok && valid, dv, lane);
   }
   // TMEM is released before any wait on another CTA: a CTA blocked in
@@ -458,7 +435,6 @@ __global__ void __launch_bounds__(kThreads1, 1)
   sm100::cluster_sync();
   if (warp >= 2 && warp < 6 && sm100::cluster_ctarank() == 0) {   // the four epilogue warps
     const int t = tid - 64;
-    if (t == 0) DT(9);
     uint32_t hkey = 0;
     if (t < T) {
       float g = 0.0f, u = 0.0f;
@@ -476,7 +452,6 @@ __global__ void __launch_bounds__(kThreads1, 1)
     hkey = block_max128(hkey, t, sh->red);
     if (t == 0) {
       a.hmax[(int64_t)j * pl.tiles + m] = hkey;
-      DT(4);
     }
   }
   sm100::cluster_sync();   // every part's row has been read
@@ -485,7 +460,6 @@ __global__ void __launch_bounds__(kThreads1, 1)
 // ------------------------------------------------------------------ launch 2
 __global__ void __launch_bounds__(kThreads, 1)
     decode_down_tc_kernel(const __grid_constant__ CUtensorMap tmD, const Args a, const Plan pl) {
-  TRACE_BASE(4096);
   extern __shared__ __align__(1024) uint8_t dsm[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
   const L2 L(pl);
@@ -498,7 +472,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t2 = blockIdx.x, j = blockIdx.y;
   const int H = pl.H, I = pl.I, N2 = pl.N2, kb2 = I / 64, nt = (kb2 + 3) / 4;
-  if (tid == 0) DT(0);
 
   if (tid == 0) {
     sm100::mbar_init(&sh->full, 1);
@@ -533,14 +506,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = sh->tmem;
-  if (tid == 0) DT(8);
 
   if (warp == 1) {
     const bool leader = sm100::elect_one();
     bool ok = sm100::mbar_wait(&sh->bready, 0, a.err, 51);
     if (valid) ok = ok && sm100::mbar_wait(&sh->full, 0, a.err, 52);
     sm100::tc_fence_after();
-    if (tid == 32) DT(2);
     if (ok && valid && leader) {
       const uint32_t idesc = sm100::idesc_nvf4((uint32_t)N2);
       for (int kb = 0; kb < kb2; ++kb) {
@@ -556,14 +527,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = tid - 64;
     const uint32_t qaddr = (uint32_t)(32 * (warp & 3)) << 16;
     if (valid && sm100::mbar_wait(&sh->full, 0, a.err, 53)) {
-      if (t == 0) DT(5);
       if (warp == 4) {
         if (pl.N2 > 128) st_weight_scales_rows<2>(tmem + qaddr + pl.sfb2, sfs, L.sfrow, N2, kb2, lane);
         else st_weight_scales_rows<1>(tmem + qaddr + pl.sfb2, sfs, L.sfrow, N2, kb2, lane);
       }
     }
     pdl_wait();   // launch 1 complete: h and the maxima are visible
-    if (t == 0) DT(1);
     // this thread's first h block is loaded alongside the maxima (one round trip)
     uint4 h0 = make_uint4(0u, 0u, 0u, 0u), h1 = h0;
     if (t < I / 16) {
@@ -575,7 +544,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n_parts = pl.k * pl.tiles;
     for (int i = t; i < n_parts; i += 128) key = max(key, __ldcg(a.hmax + i));
     key = block_max128(key, t, sh->red);
-    if (t == 0) DT(6);
     const float ts = nvfp4_tensor_scale<AEOQ_BF16>(In<AEOQ_BF16>::key_to_f(key));
     for (int bl = t; bl < I / 16; bl += 128) {
       if (bl != t) {
@@ -598,7 +566,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float wj = __bfloat162float(a.topw[j]);
     const bool ok = sm100::mbar_wait(&sh->accum, 0, a.err, 54);
     sm100::tc_fence_after();
-    if (t == 0) DT(3);
     if (warp == 4) read_row0(tmem, N2, ok && valid, dv, lane);
     asm volatile("bar.sync 2, 128;" ::: "memory");
     for (int i = t; i < N2; i += 128) dv[i] = bf16r(bf16r(dv[i] * alpha) * wj);
@@ -616,14 +583,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   sm100::cluster_sync();
   if (warp >= 2) {
     const int t = tid - 64;
-    if (t == 0) DT(7);
     const int R = (N2 + pl.k - 1) / pl.k, r0 = (int)sm100::cluster_ctarank() * R;
     for (int i = r0 + t; i < min(N2, r0 + R); i += 128) {
       float s = 0.0f;
       for (int jj = 0; jj < pl.k; ++jj) s += sm100::ld_dsmem_f32(sm100::dsmem_addr(dv + i, (uint32_t)jj));
       a.out[(int64_t)N2 * t2 + i] = __float2bfloat16_rn(s);
     }
-    if (t == 0) DT(4);
   }
   sm100::cluster_sync();   // every CTA's rows have been read
 }
@@ -688,11 +653,6 @@ Ws layout(void* base, const Plan& p) {
 
 using namespace aeoq;
 
-#ifdef AEOQ_TC_TRACE
-extern "C" int aeoq_debug_set_decode_trace(void* p) {
-  return cudaMemcpyToSymbol(dtc::g_dtrace, &p, sizeof(p)) == cudaSuccess ? 0 : -2;
-}
-#endif
 
 extern "C" int aeoq_moe_nvfp4_decode_tc_supported(int64_t top_k, int64_t hidden, int64_t inter) {
   dtc::Plan p;
@@ -756,27 +716,11 @@ extern "C" int aeoq_moe_nvfp4_decode_tc(const void* hidden, const void* top_k_in
   a.out = reinterpret_cast<__nv_bfloat16*>(out);
   a.err = err_word;
   const size_t s1 = dtc::L1(pl).bytes + 1024, s2 = dtc::L2(pl).bytes + 1024;
-  static size_t set1 = 0, set2 = 0;
-  if (set1 < s1) {
-    // the whole carveout as shared memory, so a launch-2 CTA fits beside a launch-1 CTA
-    if (cudaFuncSetAttribute(dtc::decode_gateup_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s1) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(dtc::decode_gateup_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) !=
-            cudaSuccess) {
-      cudaGetLastError();
-      return set_error(AEOQ_ERR_CUDA, "moe_decode_tc: shared memory attribute (launch 1)");
-    }
-    set1 = s1;
-  }
-  if (set2 < s2) {
-    if (cudaFuncSetAttribute(dtc::decode_down_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(dtc::decode_down_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) !=
-            cudaSuccess) {
-      cudaGetLastError();
-      return set_error(AEOQ_ERR_CUDA, "moe_decode_tc: shared memory attribute (launch 2)");
-    }
-    set2 = s2;
+  // the whole carveout as shared memory, so a launch-2 CTA fits beside a launch-1 CTA
+  {
+    int rc = func_smem_attr((const void*)dtc::decode_gateup_tc_kernel, s1, 100, "moe_decode_tc (launch 1)");
+    if (!rc) rc = func_smem_attr((const void*)dtc::decode_down_tc_kernel, s2, 100, "moe_decode_tc (launch 2)");
+    if (rc) return rc;
   }
   cudaLaunchAttribute attr1[2], attr2[2];
   attr1[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -293,11 +293,8 @@ extern "C" int aeoq_gemma4_router(const void* x, int64_t ldx, const void* scale,
   auto kern = nt == 1 ? gemma4_router_kernel<1, 12> : gemma4_router_kernel<kTok, 4>;
   const size_t smem = (size_t)2 * (nt + 1) * H + sizeof(float) * nt * (kRouterMaxE / kRouterCluster);
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) {
-      cudaGetLastError();
-      return set_error(AEOQ_ERR_CUDA, "gemma4_router_kernel: %s", cudaGetErrorString(e));
-    }
+    const int rc = func_smem_attr((const void*)kern, smem, -1, "gemma4_router_kernel");
+    if (rc) return rc;
   }
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;

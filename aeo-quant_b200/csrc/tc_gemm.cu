@@ -88,23 +88,8 @@ struct TcParams {
   const float* sb_rows;                   // FP8: per weight row scale, f32 [num_experts * n_out]
   int tiles_x, tiles_y, tiles_z;          // persistent kernel: tile grid (mode 1: tiles_y read on device)
   int* err;                               // device error word (bounded waits)
-  uint64_t* trace;                        // development builds only: per-CTA phase stamps
-  int dbg;                                // development builds only: experiment switches
 };
 
-#ifdef AEOQ_TC_TRACE
-#define TC_TRACE(i)                                                                                      \
-  do {                                                                                                   \
-    if (p.trace) {                                                                                       \
-      uint64_t t_;                                                                                       \
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                             \
-      const uint64_t cta_ = blockIdx.x + (uint64_t)gridDim.x * (blockIdx.y + (uint64_t)gridDim.y * blockIdx.z); \
-      if (cta_ < 8192) p.trace[cta_ * 8 + (i)] = t_;                                                     \
-    }                                                                                                    \
-  } while (0)
-#else
-#define TC_TRACE(i) do {} while (0)
-#endif
 
 constexpr int kTcMaxStages = 8;
 struct TcSmem {
@@ -280,7 +265,6 @@ __global__ void __launch_bounds__(kTcThreads, (BN <= 128) ? 2 : 1) nvfp4_tc_gemm
   TcSmem* sh = reinterpret_cast<TcSmem*>(base + L::kStages * L::kStage);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  if (tid == 0) TC_TRACE(0);
   const TileInfo ti = resolve_tile<BN>(p);
   if (!ti.active) return;   // whole CTA exits together before any sync
   const int64_t m_tile = blockIdx.x;
@@ -311,7 +295,6 @@ __global__ void __launch_bounds__(kTcThreads, (BN <= 128) ? 2 : 1) nvfp4_tc_gemm
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
-  if (tid == 0) TC_TRACE(1);
 
   // ------------------------------------------------------------ producers
   // Each ring slot's copies are split by operand: request r = 4 * slot + op
@@ -370,26 +353,13 @@ __global__ void __launch_bounds__(kTcThreads, (BN <= 128) ? 2 : 1) nvfp4_tc_gemm
     // ------------------------------------------------------------ MMA issuer
     {
       const bool leader = sm100::elect_one();
-#ifdef AEOQ_TC_TRACE
-      uint64_t mwait_ = 0, mcp_ = 0, mmma_ = 0;
-#endif
       const uint32_t idesc = kF8 ? sm100::idesc_f8(BN) : sm100::idesc_nvf4(BN);
       for (int kt = 0; kt < num_kt; ++kt) {
         const int s = kt % L::kStages;
         const uint32_t ph = (kt / L::kStages) & 1;
-#ifdef AEOQ_TC_TRACE
-        const long long w0_ = clock64();
-#endif
         if (!sm100::mbar_wait(&sh->full[s], ph, p.err, 12)) break;
-#ifdef AEOQ_TC_TRACE
-        const long long w1_ = clock64();
-        mwait_ += w1_ - w0_;
-#endif
         sm100::tc_fence_after();
         const int nkb = min(4, kb_total - kt * 4);
-#ifdef AEOQ_TC_TRACE
-        if (!((p.dbg & 1) && kt > 0))
-#endif
         if (!kF8 && leader)
         for (int kb = 0; kb < nkb; ++kb) {
           sm100::tc_cp_32x128b_warpx4(tmem + L::kSfaCol + 4 * kb, sm100::sdesc_sf_atom(sm100::smem_u32(stSFA(s) + kb * 512)));
@@ -398,11 +368,6 @@ __global__ void __launch_bounds__(kTcThreads, (BN <= 128) ? 2 : 1) nvfp4_tc_gemm
             sm100::tc_cp_32x128b_warpx4(tmem + L::kSfbCol + 4 * (kb * L::kSfbAtoms + a),
                                         sm100::sdesc_sf_atom(sm100::smem_u32(stSFB(s) + (kb * L::kSfbAtoms + a) * 512)));
         }
-#ifdef AEOQ_TC_TRACE
-        const long long w2_ = clock64();
-        mcp_ += w2_ - w1_;
-        if (!(p.dbg & 2))
-#endif
         if (leader)
         for (int kb = 0; kb < nkb; ++kb) {
           const uint64_t ad = sm100::sdesc_k_sw128(sm100::smem_u32(stA(s)) + kb * 32);
@@ -413,17 +378,10 @@ __global__ void __launch_bounds__(kTcThreads, (BN <= 128) ? 2 : 1) nvfp4_tc_gemm
             sm100::tc_mma_nvf4(tmem, ad, bd, idesc, tmem + L::kSfaCol + 4 * kb,
                                tmem + L::kSfbCol + 4 * kb * L::kSfbAtoms, (kt | kb) ? 1u : 0u);
         }
-#ifdef AEOQ_TC_TRACE
-        mmma_ += clock64() - w2_;
-#endif
         if (leader) sm100::tc_commit(&sh->empty[s]);
         __syncwarp();
       }
       if (leader) sm100::tc_commit(&sh->accum);
-      TC_TRACE(5);
-#ifdef AEOQ_TC_TRACE
-      if (p.trace) { const uint64_t c_ = blockIdx.x + (uint64_t)gridDim.x * (blockIdx.y + (uint64_t)gridDim.y * blockIdx.z); if (c_ < 8192) { p.trace[c_ * 8 + 4] = mwait_; p.trace[c_ * 8 + 2] = mcp_; p.trace[c_ * 8 + 3] = mmma_; } }
-#endif
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -451,7 +409,6 @@ __global__ void __launch_bounds__(kTcThreads, (BN <= 128) ? 2 : 1) nvfp4_tc_gemm
     // accumulator -> f32 value of output (row, token t)
     auto scaled = [&](float acc, int t) { return kF8 ? (acc * colscale[t]) * alpha : acc * alpha; };
     const bool ok = sm100::mbar_wait(&sh->accum, 0, p.err, 14);
-    if (tid == 64) TC_TRACE(6);
     sm100::tc_fence_after();
     char* cbase = reinterpret_cast<char*>(p.c) + ti.slot * p.c_slot_stride;
     uint32_t hkey = 0;
@@ -465,19 +422,10 @@ __global__ void __launch_bounds__(kTcThreads, (BN <= 128) ? 2 : 1) nvfp4_tc_gemm
     char* cwarp = cbase + ti.c_row0 * p.ldc + col_w * es;
     constexpr int kChunk = kHalf < 32 ? kHalf : 32;   // columns per TMEM wait
     const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
-#ifdef AEOQ_TC_TRACE
-    long long e_ld = 0, e_st = 0, e0_ = clock64();
-#endif
     if (p.epi != kEpiGeglu) {
       for (int c0 = tbeg; c0 < tend; c0 += kChunk) {
         float v[kChunk < 16 ? 16 : kChunk];
-#ifdef AEOQ_TC_TRACE
-        const long long a_ = clock64();
-#endif
         tmem_chunk<kChunk>(tq + (uint32_t)c0, v);
-#ifdef AEOQ_TC_TRACE
-        e_ld += clock64() - a_;
-#endif
 #pragma unroll
         for (int g8 = 0; g8 < kChunk; g8 += 8) {
           const int t0 = c0 + g8;
@@ -490,15 +438,6 @@ __global__ void __launch_bounds__(kTcThreads, (BN <= 128) ? 2 : 1) nvfp4_tc_gemm
             y[j] = val;
           }
           if (!ok) continue;
-#ifdef AEOQ_TC_TRACE
-          if (p.dbg & 4) { if (y[0] == 12345.f) *reinterpret_cast<float*>(cwarp) = y[1]; continue; }
-          if (p.dbg & 8) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              if (t0 + j < ti.n_valid) *reinterpret_cast<__nv_bfloat16*>(cwarp + (t0 + j) * p.ldc + 2 * lane) = __float2bfloat16_rn(y[j]);
-            continue;
-          }
-#endif
           if (es == 2) {
             store_8tok_bf16(y, cwarp + t0 * p.ldc, p.ldc, ti.n_valid - t0, lane);
           } else {
@@ -545,14 +484,6 @@ __global__ void __launch_bounds__(kTcThreads, (BN <= 128) ? 2 : 1) nvfp4_tc_gemm
         }
       }
     }
-#ifdef AEOQ_TC_TRACE
-    const long long e1_ = clock64();
-    e_st = 0;
-    if (tid == 64 && p.trace) {
-      const uint64_t c_ = blockIdx.x + (uint64_t)gridDim.x * (blockIdx.y + (uint64_t)gridDim.y * blockIdx.z);
-      if (c_ < 8192) { p.trace[c_ * 8 + 5] = e_ld; p.trace[c_ * 8 + 6] = e1_ - e0_; p.trace[c_ * 8 + 1] = e_st; }
-    }
-#endif
     if (p.epi == kEpiGeglu && p.grp_amax) {
       hkey = warp_umax(hkey);
       if (lane == 0 && hkey) atomicMax(p.grp_amax + ti.expert, hkey);
@@ -560,7 +491,6 @@ __global__ void __launch_bounds__(kTcThreads, (BN <= 128) ? 2 : 1) nvfp4_tc_gemm
   }
   sm100::tc_fence_before();
   __syncthreads();
-  if (tid == 0) TC_TRACE(7);
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, L::kTmemCols);
@@ -708,35 +638,19 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
     int64_t g = 0;
     int it = 0;
     bool alive = true;
-#ifdef AEOQ_TC_TRACE
-    long long w_acc = 0, w_full = 0, w_issue = 0;
-#endif
     for (int64_t t = blockIdx.x; t < total && alive; t += gridDim.x) {
       int64_t m_tile;
       const TileInfo ti = tile_of(t, m_tile);
       if (!ti.active) continue;
       const int b = it & 1;
       const uint32_t accp = (uint32_t)((it >> 1) & 1);
-#ifdef AEOQ_TC_TRACE
-      long long c0_ = clock64();
-#endif
       if (!sm100::mbar_wait(&sh->acc_empty[b], accp ^ 1, p.err, 62)) break;
-#ifdef AEOQ_TC_TRACE
-      w_acc += clock64() - c0_;
-#endif
       sm100::tc_fence_after();
       const uint32_t dcol = tmem + (uint32_t)b * L::kAccStride;
       for (int kt = 0; kt < num_kt; ++kt, ++g) {
         const int s = (int)(g % L::kStages);
         const uint32_t ph = (uint32_t)((g / L::kStages) & 1);
-#ifdef AEOQ_TC_TRACE
-        const long long c1_ = clock64();
-#endif
         if (!sm100::mbar_wait(&sh->full[s], ph, p.err, 63)) { alive = false; break; }
-#ifdef AEOQ_TC_TRACE
-        const long long c2_ = clock64();
-        w_full += c2_ - c1_;
-#endif
         sm100::tc_fence_after();
         const int nkb = min(4, kb_total - kt * 4);
         if (leader) {
@@ -763,17 +677,11 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
           sm100::tc_commit(&sh->empty[s]);
         }
         __syncwarp();
-#ifdef AEOQ_TC_TRACE
-        w_issue += clock64() - c2_;
-#endif
       }
       if (leader) sm100::tc_commit(&sh->acc_full[b]);
       __syncwarp();
       ++it;
     }
-#ifdef AEOQ_TC_TRACE
-    if (p.trace && lane == 0) { p.trace[blockIdx.x * 8 + 1] = w_acc; p.trace[blockIdx.x * 8 + 2] = w_full; p.trace[blockIdx.x * 8 + 3] = w_issue; p.trace[blockIdx.x * 8 + 4] = it; }
-#endif
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
@@ -789,9 +697,6 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
     const int es = (p.epi == kEpiStore && p.c_dt == AEOQ_F32) ? 4 : 2;
     float* colscale = sh->colscale;
     int it = 0;
-#ifdef AEOQ_TC_TRACE
-    long long e_wait = 0, e_work = 0;
-#endif
     for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
       int64_t m_tile;
       const TileInfo ti = tile_of(t, m_tile);
@@ -814,14 +719,7 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
         else alpha = load_scalar_f(p.a_ts, p.a_ts_dt) * load_scalar_f(p.w_ts, p.w_ts_dt);
       }
       auto scaled = [&](float acc, int c) { return kF8 ? (acc * colscale[c]) * alpha : acc * alpha; };
-#ifdef AEOQ_TC_TRACE
-      const long long d0_ = clock64();
-#endif
       const bool ok = sm100::mbar_wait(&sh->acc_full[b], accp, p.err, 64);
-#ifdef AEOQ_TC_TRACE
-      const long long d1_ = clock64();
-      e_wait += d1_ - d0_;
-#endif
       sm100::tc_fence_after();
       const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)b * L::kAccStride;
       char* cbase = reinterpret_cast<char*>(p.c) + ti.slot * p.c_slot_stride;
@@ -905,13 +803,7 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
           if (lane == 0 && hkey) atomicMax(p.grp_amax + ti.expert, hkey);
         }
       }
-#ifdef AEOQ_TC_TRACE
-      e_work += clock64() - d1_;
-#endif
     }
-#ifdef AEOQ_TC_TRACE
-    if (p.trace && tid == 128) { p.trace[blockIdx.x * 8 + 5] = e_wait; p.trace[blockIdx.x * 8 + 6] = e_work; }
-#endif
   }
   sm100::tc_fence_before();
   __syncthreads();
@@ -931,32 +823,16 @@ static int launch_persistent(const uint8_t* a, int64_t a_rows, const uint8_t* b,
   if (rc) return rc;
   rc = make_tmap(&tb, b, p.b_rows, row_bytes, row_bytes, BN);
   if (rc) return rc;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(tc_gemm_persistent_kernel<BN, kF8>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kBytes);
-    if (e != cudaSuccess) {
-      cudaGetLastError();
-      return set_error(AEOQ_ERR_CUDA, "tc_gemm_persistent: smem attribute: %s", cudaGetErrorString(e));
-    }
-    attr_set = true;
+  {
+    const int rc = func_smem_attr((const void*)tc_gemm_persistent_kernel<BN, kF8>, L::kBytes, -1,
+                                  "tc_gemm_persistent");
+    if (rc) return rc;
   }
-#ifdef AEOQ_TC_TRACE
-  if (const char* tp = getenv("AEOQ_TC_TRACE_PTR")) p.trace = reinterpret_cast<uint64_t*>(strtoull(tp, nullptr, 10));
-#endif
   tc_gemm_persistent_kernel<BN, kF8><<<grid_ctas, kPThreads, L::kBytes, st>>>(ta, tb, p);
   return check_launch(kF8 ? "tc_gemm_persistent_kernel<fp8>" : "tc_gemm_persistent_kernel");
 }
 
-static int sm_count() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-  }
-  return n;
-}
+static int sm_count() { return device_sm_count(); }
 
 // ---------------------------------------------------------------- host side
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -1031,25 +907,11 @@ static int launch_tc(const uint8_t* a, int64_t a_rows, const uint8_t* b, const T
   if (rc) return rc;
   rc = make_tmap(&tb, b, p.b_rows, row_bytes, row_bytes, BN);
   if (rc) return rc;
-  static size_t set_bytes[12] = {};
-  const int slot = (BN == 8 ? 4 : BN == 16 ? 5 : BN == 32 ? 0 : BN == 64 ? 1 : BN == 128 ? 2 : 3) + (kF8 ? 6 : 0);
-  if (set_bytes[slot] < L::kBytes) {
-    cudaError_t e = cudaFuncSetAttribute(nvfp4_tc_gemm_kernel<BN, kF8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)L::kBytes);
-    if (e != cudaSuccess) {
-      cudaGetLastError();
-      return set_error(AEOQ_ERR_CUDA, "tc_gemm: smem attribute: %s", cudaGetErrorString(e));
-    }
-    set_bytes[slot] = L::kBytes;
+  {
+    const int rc = func_smem_attr((const void*)nvfp4_tc_gemm_kernel<BN, kF8>, L::kBytes, -1, "tc_gemm");
+    if (rc) return rc;
   }
-#ifdef AEOQ_TC_TRACE
-  TcParams pt = p;
-  if (const char* tp = getenv("AEOQ_TC_TRACE_PTR")) pt.trace = reinterpret_cast<uint64_t*>(strtoull(tp, nullptr, 10));
-  if (const char* dp = getenv("AEOQ_TC_DBG")) pt.dbg = atoi(dp);
-  nvfp4_tc_gemm_kernel<BN, kF8><<<grid, kTcThreads, L::kBytes, st>>>(ta, tb, pt);
-#else
   nvfp4_tc_gemm_kernel<BN, kF8><<<grid, kTcThreads, L::kBytes, st>>>(ta, tb, p);
-#endif
   return check_launch(kF8 ? "fp8_tc_gemm_kernel" : "nvfp4_tc_gemm_kernel");
 }
 

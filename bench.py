@@ -1,4 +1,4 @@
-"""Benchmark: one-token NVFP4 MoE expert decode (batch 1).
+"""Benchmark: one-token NVFP4 MoE expert decode (Gemma-4 expert layer, batch 1).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B]
 
@@ -43,7 +43,7 @@ FALLBACK_HBM_GBS = 6650.0
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one tensor-core decode
 # (both launches) at this workload, from the ncu capture summarised in
-# profiles/moe_decode_tc_b1.md (None until captured).
+# the committed ncu summary of the decode pair (None until captured).
 NCU_TRAFFIC_TC = 27048448
 
 
@@ -58,7 +58,7 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     p.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM measurements")
-    p.add_argument("--workload", default="decode", choices=["decode", "ep", "gemm", "stack", "router"],
+    p.add_argument("--workload", default="decode", choices=["decode", "ep", "gemm", "stack", "router", "grouped"],
                    help="decode: config 1 (default); ep: config 4, expert-parallel prefill stack; "
                         "gemm: config-0 NVFP4 linear at --gemm-m rows (profiling)")
     p.add_argument("--gemm-m", type=int, default=32768)
@@ -331,6 +331,45 @@ def main_gemm(args, local):
                       "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": us / 1000.0,
                       "higher_is_better": True, "config": {"workload": f"config0 GEMM M={M} N=1408 K=2816"},
                       "frac_fp4_nominal": round(tf / 9000, 4)}), flush=True)
+
+
+def main_grouped(args, local):
+    """The grouped expert forwards alone at the FP8 prefill shapes (128
+    experts, H 2816, I 704, --tokens tokens, softmax top-8): FP8 and NVFP4,
+    each W warm-up calls then K calls timed with CUDA events. Used for the
+    launch lists and captures of the grouped pipeline."""
+    import torch
+    from aeo_quant_b200.bridges.gemma4 import moe_ops
+    from aeo_quant_b200.gpu import quant as Q
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev).manual_seed(0)
+    T = args.tokens
+    h = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    wv, ids = torch.topk(torch.softmax(torch.randn(T, E, generator=g, device=dev), -1), TOPK, dim=-1)
+    wts = (wv / wv.sum(-1, keepdim=True)).to(torch.bfloat16)
+    out = {}
+    gq, gs = Q.quantize_3d_to_fp8((torch.randn(E, 2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+    dq, ds = Q.quantize_3d_to_fp8((torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+    gsb, dsb = gs.reshape(-1).float().contiguous(), ds.reshape(-1).float().contiguous()
+    gp, gsf, gt = Q.quantize_3d_to_nvfp4((torch.randn(E, 2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+    dp, dsf, dt = Q.quantize_3d_to_nvfp4((torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+    gt, dt = gt.float(), dt.float()
+    for name, fn in (("fp8", lambda: moe_ops.fp8_experts_grouped(h, ids, wts, gq, gsb, dq, dsb)),
+                     ("nvfp4", lambda: moe_ops.nvfp4_experts_grouped(h, ids, wts, gp, gsf, gt, dp, dsf, dt))):
+        for _ in range(max(1, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / args.steps
+        out[name] = {"us": round(us, 1), "tflops": round(T * TOPK * 11894784 / us / 1e6, 1)}
+    print(json.dumps({"metric": "grouped expert forward", "config": {"workload": f"{T} tokens, top-8, 128 experts"},
+                      **out}), flush=True)
 
 
 def main_ep(args, rank, world, local):
@@ -626,6 +665,9 @@ def main():
         return
     if args.workload == "gemm":
         main_gemm(args, local)
+        return
+    if args.workload == "grouped":
+        main_grouped(args, local)
         return
     if args.workload == "stack":
         main_stack(args, local)

@@ -22,7 +22,8 @@ from oracle.gemm import nvfp4_gemm, nvfp4_linear  # noqa: E402
 
 def case_inputs(case):
     """Deterministic layer and tokens shared by the workers and the test.
-    Case 2 is case 1's skewed routing, run with a balanced placement."""
+    Case 2 is case 1's skewed routing, run with a balanced placement. Case 3
+    has a single token, so with two ranks one of them holds none."""
     if case == 2:
         return case_inputs(1)
     g = np.load(os.path.join(HERE, "golden", "moe_golden.npz"))
@@ -30,9 +31,9 @@ def case_inputs(case):
                         g["nv/down_proj"], g["nv/down_proj_scale"], g["nv/down_proj_scale_2"][0])
     E, H = m.num_experts, m.down_proj.shape[1]
     rng = np.random.default_rng(7 + case)
-    T, k = 12, 4
+    T, k = (1 if case == 3 else 12), 4
     hidden = N.bf16(rng.standard_normal((T, H)).astype(np.float32))
-    if case == 0:      # uniform routing
+    if case in (0, 3):      # uniform routing
         ids = np.stack([rng.permutation(E)[:k] for _ in range(T)])
     else:              # skewed: most pairs on rank 0's experts, one dropped id (== E)
         ids = np.stack([np.r_[rng.permutation(3)[:k - 1], 3 + (t % 5)] for t in range(T)])
@@ -47,9 +48,7 @@ class OracleEpOps:
     def __init__(self, m, first, count):
         self.m, self.first, self.count = m, first, count
 
-    def global_scale(self, hidden, group):
-        amax = hidden.abs().amax().to(torch.float32).reshape(1)
-        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=group)
+    def tensor_scale(self, amax, dtype):
         return float(OQ.nvfp4_tensor_scale(np.float32(amax.item()), "bf16"))
 
     def encode(self, hidden, ts):

@@ -21,7 +21,7 @@ Every fixture is produced by the reference's own code:
   one float32 rounding, ``alpha`` epilogue, bf16 output), so these fixtures
   pin the reference's routing, casts, re-quantization and combine.
 * ``config0_hashes.json`` — SHA-256 of the reference quantizer outputs for
-  BASELINE config 0 (W[1408,2816] ~ N(0,0.02) and X[128,2816] ~ N(0,1),
+  the single-linear case (W[1408,2816] ~ N(0,0.02) and X[128,2816] ~ N(0,1),
   seed 0), too large to store in full.
 """
 from __future__ import annotations
@@ -272,4 +272,6 @@ def make_moe_golden(Q):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path to the aeo-quant source tree>")
+    main(sys.argv[1])

@@ -163,6 +163,9 @@ def test_router_swap_only_supported_shapes():
     from aeo_quant_b200.bridges.gemma4.router import Gemma4TextRouterB200, router_supported
     ok, odd, narrow = hf_router(2816, 128, 8, 1, 0.02), hf_router(2816, 12, 4, 1, 0.02), hf_router(256, 128, 8, 1, 0.02)
     assert router_supported(ok) and not router_supported(odd) and not router_supported(narrow)
+    # a router loaded in another dtype keeps HF's forward
+    f32 = hf_router(2816, 128, 8, 1, 0.02).float()
+    assert not router_supported(f32)
     seq = nn.Sequential(ok, odd, narrow)
     assert swap_routers(seq, only_supported=True) == 1
     assert type(ok) is Gemma4TextRouterB200 and type(odd) is not Gemma4TextRouterB200

@@ -21,7 +21,7 @@ def _free_port():
         return str(s.getsockname()[1])
 
 
-@pytest.mark.parametrize("case", [0, 1, 2])
+@pytest.mark.parametrize("case", [0, 1, 2, 3])
 def test_ep_two_ranks_match_one_process(tmp_path, case):
     sys.path.insert(0, HERE)
     from ep_worker import case_inputs

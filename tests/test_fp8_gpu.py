@@ -1,7 +1,7 @@
 """FP8 path on the GPU: per-row activation quantization (bit-exact), the
 tensor-core FP8 GEMM (tolerance vs the f32 oracle), and
 Gemma4TextExpertsFP8.forward vs the reference-generated golden outputs and
-the oracle restatement at the BASELINE shapes."""
+the oracle restatement at the Gemma-4 expert shapes."""
 import types
 
 import numpy as np
@@ -105,7 +105,7 @@ def test_fp8_golden_forward(golden_fp8, moe_golden, T):
 
 @pytest.fixture(scope="module")
 def full_fp8():
-    """BASELINE config 2 layer: 128 experts, H=2816, I=704, e4m3 rowwise."""
+    """FP8 expert layer: 128 experts, H=2816, I=704, e4m3 rowwise."""
     from aeo_quant_b200.gpu import quant as Q
     E, H, I = 128, 2816, 704
     gq, gs = Q.quantize_3d_to_fp8(randn_bf16((E, 2 * I, H), 0.02, 300))

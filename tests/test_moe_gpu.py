@@ -53,7 +53,7 @@ def test_golden_forward(golden_module, moe_golden, T):
 
 @pytest.fixture(scope="module")
 def full_layer():
-    """BASELINE config 1 layer: 128 experts, H=2816, I=704, NVFP4 per projection."""
+    """NVFP4 expert layer: 128 experts, H=2816, I=704, NVFP4 per projection."""
     from aeo_quant_b200.gpu import quant as Q
     E, H, I = 128, 2816, 704
     wgu = randn_bf16((E, 2 * I, H), 0.02, 100)

@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import TOL, bf16_to_np, max_rel_err, randn_bf16, routing
+from helpers import bf16_to_np, randn_bf16, routing
 
 pytestmark = pytest.mark.gpu
 
@@ -46,7 +46,9 @@ def test_noalloc_decode_matches_workspace_entry_point():
         A.check(lib.aeoq_moe_nvfp4_decode_fused_noalloc(*common(h, idx, w, got), st))
         torch.cuda.synchronize()
         assert np.all(np.isfinite(bf16_to_np(got)))
-        assert max_rel_err(bf16_to_np(got), bf16_to_np(ref)) <= TOL
+        # the same kernel on the same inputs: identical bits, so a stale
+        # value left in the shared scratch by the previous call would show
+        assert torch.equal(got, ref)
 
 
 def test_noalloc_rejects_oversized_shape():
