@@ -180,54 +180,65 @@ def routing(torch, S, B, seed):
     return idx, w, h
 
 
-def cpu_baseline(seconds, kind_note="port"):
-    """Time the numpy port of the reference decode (oracle/) on the host."""
-    import numpy as np
+def decode_config(B, L, world):
+    """The ``config`` object of the decode line, shared by both arms."""
+    return {"workload": f"config1: M=1 NVFP4 expert-gather decode, one MoE layer, batch {B}",
+            "experts": E, "hidden": H, "intermediate": I, "top_k": TOPK, "batch": B,
+            "resident_layers": L, "l2": f"inputs larger than L2: {L} layers cycled, "
+            f"{L * 428} MB resident, 26.8 MB streamed per step",
+            "parallelism": f"replicas x{world}", "timing": "one CUDA graph of K steps, CUDA events"}
+
+
+def cpu_baseline(seconds, batch=1):
+    """Time the reference's CPU arithmetic for the decode on the host: the
+    torch restatement in ``oracle/torch_port.py`` (quantize the hidden
+    vector, dequantize the 8 routed experts' NVFP4 weights to f32, f32
+    matmuls, every bf16 rounding of ``_forward_decode_3d``), one process
+    using every host thread, over a 128-expert layer of random packed
+    weights (the time per token does not depend on the values). Tokens run
+    back to back for about ``seconds``; value = tokens / elapsed."""
     import torch
-    from concurrent.futures import ThreadPoolExecutor
-    from oracle import moe as OM
-    from oracle import quant as OQ
-    pool_e = TOPK
-    g = torch.Generator().manual_seed(7)
-    wgu = (torch.randn(pool_e, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
-    wd = (torch.randn(pool_e, H, I, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
-    gp, gs, gt = OQ.quantize_nvfp4(wgu)
-    dp, ds, dt = OQ.quantize_nvfp4(wd)
-    m = OM.NVFP4Experts(gp, gs, gt, dp, ds, dt)
+    from oracle import torch_port as TP
     threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(7)
+    gu = torch.randint(0, 256, (E, 2 * I, H // 2), generator=g, dtype=torch.uint8)
+    dw = torch.randint(0, 256, (E, H, I // 2), generator=g, dtype=torch.uint8)
+    # e4m3 block scales 0x20..0x3f (2^-3 .. ~0.94): finite, no NaN codes
+    gs = torch.randint(0x20, 0x40, (E, 2 * I, H // 16), generator=g, dtype=torch.uint8)
+    ds = torch.randint(0x20, 0x40, (E, H, I // 16), generator=g, dtype=torch.uint8)
+    m = TP.Experts(gu, gs, 1e-3, dw, ds, 1e-3)
 
     def one(i):
-        rng = np.random.default_rng(i)
-        h = np.asarray(torch.randn(1, H, generator=torch.Generator().manual_seed(i)).to(torch.bfloat16).float())
-        idx = rng.permutation(pool_e)[None, :TOPK]
-        w = np.full((1, TOPK), 1.0 / TOPK, np.float32)
-        OM.nvfp4_experts_forward(m, h, idx, w)
+        gi = torch.Generator().manual_seed(100 + i)
+        h = torch.randn(batch, H, generator=gi).to(torch.bfloat16)
+        idx = torch.stack([torch.randperm(E, generator=gi)[:TOPK] for _ in range(batch)])
+        w = torch.softmax(torch.randn(batch, TOPK, generator=gi), -1).to(torch.bfloat16)
+        TP.forward(m, h, idx, w)
 
-    one(0)  # warm-up
+    one(0)   # warm-up
     done, t0 = 0, time.perf_counter()
-    with ThreadPoolExecutor(threads) as ex:
-        while time.perf_counter() - t0 < seconds:
-            list(ex.map(one, range(done + 1, done + 1 + threads)))
-            done += threads
+    while time.perf_counter() - t0 < seconds or done < 3:
+        one(done + 1)
+        done += 1
     dt_s = time.perf_counter() - t0
-    return {"value": done / dt_s, "unit": "tok/s", "cores": threads, "kind": kind_note,
-            "sample": f"{done} tokens x 1 layer of the numpy port (oracle/moe.py nvfp4_decode_3d), "
-                      f"top-8 over an 8-expert pool (per-token work identical to 128 experts), "
-                      f"{threads} threads, {dt_s:.1f} s"}
+    return {"value": done * batch / dt_s, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{done} steps of batch {batch} x 1 layer (128 experts, top-8) through the torch "
+                      f"restatement of the reference forward (oracle/torch_port.py: NVFP4 dequantize + f32 "
+                      f"matmul), one process, torch threads {threads}, {dt_s:.1f} s"}
 
 
 def run_reference(args, rank):
     if rank != 0:
         return
-    t_budget = max(5.0, min(60.0, args.steps * 0.05))
-    cb = cpu_baseline(t_budget)
+    t_budget = max(5.0, min(30.0, args.steps * 0.5))
+    cb = cpu_baseline(t_budget, args.batch)
     print(json.dumps({
         "metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "tok/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp4(e2m1)+e4m3 scales, fp32 accumulate", "data": "synthetic",
-        "config": {"workload": "config1: M=1 NVFP4 expert-gather decode, one MoE layer, batch 1",
-                   "experts": E, "hidden": H, "intermediate": I, "top_k": TOPK},
+        "ms_per_step": 1000.0 * args.batch / cb["value"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp4(e2m1)+e4m3 scales, fp32 accumulate, bf16 io", "data": "synthetic",
+        "config": decode_config(args.batch, args.layers, args.gpus),
         "cpu_baseline": cb,
         "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -845,11 +856,7 @@ def main():
             "warmup": W, "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp4(e2m1)+e4m3 scales, fp32 accumulate, bf16 io",
             "data": "synthetic (bf16 N(0,0.02) weights quantized on device; N(0,1) hidden; uniform top-8)",
-            "config": {"workload": f"config1: M=1 NVFP4 expert-gather decode, one MoE layer, batch {B}",
-                       "experts": E, "hidden": H, "intermediate": I, "top_k": TOPK, "batch": B,
-                       "resident_layers": L, "l2": f"inputs larger than L2: {L} layers cycled, "
-                       f"{L * 428} MB resident, 26.8 MB streamed per step",
-                       "parallelism": f"replicas x{world}", "timing": "one CUDA graph of K steps, CUDA events"},
+            "config": decode_config(B, L, world),
             "step_hbm_gbs": round(step_bytes / (ms_max / K / 1000.0) / 1e9, 1),
             "gpu_launches": (2 if tc_path else 1) * K,
             "clocks": clk.summary(),
@@ -861,7 +868,7 @@ def main():
             "prefill": prefill,
         }
         if world == 1 and not args.no_cpu_baseline:
-            res["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+            res["cpu_baseline"] = cpu_baseline(args.cpu_seconds, B)
         print(json.dumps(res), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -16,7 +16,8 @@ The test proves that this is the only source of error above the bar: it
 feeds the oracle's down projection and combine with the GPU's own gate_up
 rows, and requires the GPU output within 2e-3 * max|ref| (or one bf16 ulp)
 of that; it requires every GPU gate_up value within one bf16 ulp of the
-oracle's, and bounds how many differ at all.
+oracle's (or, for outputs near zero after cancellation, within 1e-4 of the
+block's largest), and bounds how many differ at all.
 """
 import numpy as np
 import pytest
@@ -131,7 +132,10 @@ def test_fp8_grouped_benched_size():
         gu = bf16_to_np(moe_ops.fp8_linear(rows, gq[e], gs[e].reshape(1, -1).float()))
         gu_ref = OM.fp8_linear(hn[tok], om.gate_up_proj[e], om.gate_up_proj_scale[e])
         diff = np.abs(gu.astype(np.float64) - gu_ref)
-        assert np.all(diff <= bf16_ulp(gu_ref)), "a gate_up output is more than one bf16 ulp from the oracle"
+        # one bf16 ulp, or (outputs near zero after cancellation) the f32
+        # accumulation error of 2816 products, far below 1e-4 * max|ref|
+        lim = np.maximum(bf16_ulp(gu_ref), 1e-4 * np.max(np.abs(gu_ref)))
+        assert np.all(diff <= lim), ("gate_up beyond one bf16 ulp", float(np.max(diff / lim)))
         flips += int(np.count_nonzero(diff))
         total += gu.size
         return gu
