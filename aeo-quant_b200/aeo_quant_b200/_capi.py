@@ -61,6 +61,9 @@ _SIGS["aeoq_moe_fp8_forward"] = [_P, _L, _P, _I, _P, _L, _P, _P, _P, _P, _L, _L,
 _SIGS["aeoq_moe_nvfp4_decode_tc_supported"] = [_L, _L, _L]
 _SIGS["aeoq_moe_nvfp4_decode_tc_workspace_size"] = [_L, _L, _L]
 _SIGS["aeoq_moe_nvfp4_decode_tc"] = [_P, _P, _I, _P, _L, _P, _P, _P, _I, _P, _P, _P, _I, _L, _L, _L, _P, _P, _Z, _P, _P]
+_SIGS["aeoq_moe_nvfp4_decode_stream_supported"] = [_L, _L, _L]
+_SIGS["aeoq_moe_nvfp4_decode_stream_workspace_size"] = [_L, _L, _L]
+_SIGS["aeoq_moe_nvfp4_decode_stream"] = _SIGS["aeoq_moe_nvfp4_decode_tc"]
 _SIGS["aeoq_nvfp4_tile_n"] = [_L, _L, _L]
 _SIGS["aeoq_nvfp4_weight_atoms_size"] = [_L, _L]
 _SIGS["aeoq_nvfp4_act_atoms_size"] = [_L, _L, _I]
@@ -71,6 +74,7 @@ _SIGS["aeoq_nvfp4_gemm_tc"] = [_P, _P, _P, _I, _L, _P, _P, _P, _I, _L, _P, _I, _
 _SIGS["aeoq_moe_nvfp4_decode_fused_noalloc"] = [_P, _P, _I, _P, _L, _P, _P, _P, _I, _P, _P, _P, _I, _L, _L, _L,
                                                 _P, _P]
 _RESTYPE = {"aeoq_moe_nvfp4_decode_tc_workspace_size": C.c_size_t,
+            "aeoq_moe_nvfp4_decode_stream_workspace_size": C.c_size_t,
             "aeoq_nvfp4_weight_atoms_size": C.c_size_t, "aeoq_nvfp4_act_atoms_size": C.c_size_t,
             "aeoq_last_error": C.c_char_p, "aeoq_nvfp4_quantize_workspace_size": C.c_size_t,
             "aeoq_moe_nvfp4_decode_workspace_size": C.c_size_t,

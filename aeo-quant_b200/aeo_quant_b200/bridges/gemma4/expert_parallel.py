@@ -130,9 +130,16 @@ def global_amax(hidden: torch.Tensor, group) -> torch.Tensor:
     return amax
 
 
-def ep_moe_forward(hidden, top_k_index, top_k_weights, *, num_experts: int, group, ops, owner=None):
+def ep_moe_forward(hidden, top_k_index, top_k_weights, *, num_experts: int, group, ops, owner=None, mark=None):
     """One expert-parallel MoE layer over ``group`` (see module docstring).
-    ``owner``: optional placement (E,) of experts on ranks."""
+    ``owner``: optional placement (E,) of experts on ranks. ``mark``: optional
+    callable taking a phase name ("dispatch", "experts", "combine", "end"),
+    called where each phase starts (a profiler hook, e.g. recording CUDA
+    events)."""
+    if mark is None:
+        def mark(_):
+            return None
+    mark("dispatch")
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     e_loc = num_experts // world
@@ -167,12 +174,16 @@ def ep_moe_forward(hidden, top_k_index, top_k_weights, *, num_experts: int, grou
     recv_payload = [_all_to_all_rows(p[send_tok], sc, rc, group) for p in payload]
     recv_meta = _all_to_all_rows(meta, sc, rc, group)
     recv_w = recv_meta[:, 1].to(torch.int16).view(torch.bfloat16)
+    mark("experts")
     out_rows = ops.experts(recv_payload, recv_meta[:, 0], recv_w, ts, my_experts)   # (n_recv, H)
 
+    mark("combine")
     back = _all_to_all_rows(out_rows, rc, sc, group)     # in this rank's send order
     pair_row = torch.full((T * k,), -1, dtype=torch.int32, device=dev)
     pair_row[send_pairs] = torch.arange(send_pairs.numel(), dtype=torch.int32, device=dev)
-    return ops.combine(back, pair_row, top_k_index, T, k)
+    out = ops.combine(back, pair_row, top_k_index, T, k)
+    mark("end")
+    return out
 
 
 class NVFP4EpOps:
@@ -230,6 +241,7 @@ class ExpertParallelNVFP4(torch.nn.Module):
         self.num_experts = num_experts
         self.group = group
         self.owner = None if owner is None else torch.as_tensor(owner, dtype=torch.int64).reshape(-1).cpu()
+        self.mark = None   # optional phase hook passed to ep_moe_forward
 
     def forward(self, hidden_states, top_k_index, top_k_weights):
         m = self.local
@@ -238,4 +250,4 @@ class ExpertParallelNVFP4(torch.nn.Module):
         ops = NVFP4EpOps(m.gate_up_proj, m.gate_up_proj_scale, m.gate_up_proj_scale_2,
                          m.down_proj, m.down_proj_scale, m.down_proj_scale_2)
         return ep_moe_forward(hidden_states, top_k_index, top_k_weights, num_experts=self.num_experts,
-                              group=self.group, ops=ops, owner=self.owner)
+                              group=self.group, ops=ops, owner=self.owner, mark=self.mark)

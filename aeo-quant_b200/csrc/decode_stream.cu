@@ -1,0 +1,498 @@
+// One-token NVFP4 MoE expert forward, streamed: one launch, one grid barrier.
+//
+// Restates Gemma4TextExpertsNVFP4._forward_decode_3d (aeo_quant
+// src/aeo_quant/bridges/gemma4/modeling_nvfp4.py:132-186) for one token:
+// quantize the hidden vector (:150-153), gate_up GEMV of the k routed
+// experts (:155-160), GeGLU in bf16 (:161-162), re-quantize the k GeGLU rows
+// with ONE shared tensor scale (:164-172), down GEMV (:174-179), weighted
+// sum over the k experts (:181-186).
+//
+// At one token the layer is a pure stream of the k experts' packed weights
+// (26.8 MB for Gemma-4-26B-A4B), so the kernel is laid out for HBM:
+//
+// * Work split by bytes. CTA c (one per SM) owns a contiguous range of the
+//   k*I gate/up row pairs and a block of `rows` down rows (a multiple of 4,
+//   so that its 44-byte scale rows start on 16-byte boundaries) for all k
+//   experts. The host plan balances the CTAs' total bytes: CTAs without down
+//   rows take more pairs.
+// * Everything the CTA will ever read from HBM is requested at entry: every
+//   warp loads the expert ids itself and issues its share of the bulk copies
+//   (cp.async.bulk, L2 evict-first) of the CTA's gate rows, up rows, scale
+//   rows, down rows and down scale rows into shared memory (about 181 KB), in
+//   consumption order, completing on one mbarrier per group of kGroup pairs
+//   and one per expert slot for the down block.
+// * Meanwhile the hidden vector is staged in shared memory and quantized
+//   (global amax, bf16 tensor scale, e4m3 block scales, E2M1 codes) into
+//   exact fp16 operands.
+// * gate/up dot products run per pair group as soon as its barrier flips,
+//   so compute overlaps the stream; h = bf16(bf16(gelu(g)) * u) goes to the
+//   workspace.
+// * One grid barrier (an arrival counter with a bounded spin; the launch is
+//   cooperative, so every CTA is resident); the grid's max |h| is one word
+//   updated with atomicMax before the arrival. Then each CTA reads the k
+//   GeGLU rows (its down rows cover every expert) into shared memory in one
+//   coalesced pass, quantizes them with the shared tensor scale and runs its
+//   down dot products from shared memory (landed long before).
+// * Each output row sums its k weighted products bf16(bf16(a*d_j) * w_j) in
+//   f64 and rounds once to f32 then bf16, as the reference's sum does.
+// * The last CTA to leave zeroes the counters, so a zeroed workspace stays
+//   valid for every call on one stream.
+//
+// An expert id outside [0, E) reads no weights and contributes zeros.
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace aeoq {
+namespace dst {
+
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxK = 16;
+constexpr int kMaxCtas = 160;
+constexpr int kGroup = 8;             // gate/up pairs per arrival barrier
+constexpr int kMaxGroups = 12;
+constexpr int kMaxRows = 32;          // down rows per CTA
+constexpr int kMaxChunks = 4;         // 32-value chunks per lane of a hidden row (H <= 4096)
+constexpr size_t kSmemCap = 227 * 1024;
+
+// Host-side plan (passed by value).
+struct Plan {
+  int H, I, k, G;
+  int rows;                    // down rows per CTA (multiple of 4)
+  int max_pairs;               // largest pair range of any CTA
+  size_t bytes;                // dynamic shared memory
+  int pair0[kMaxCtas + 1];     // CTA c owns pairs [pair0[c], pair0[c+1])
+};
+
+struct Args {
+  const __nv_bfloat16* hidden;
+  const void* ids; int ids_dt;
+  const __nv_bfloat16* topw;
+  const uint8_t* gu; const uint8_t* gu_sf; const void* gu_ts; int gu_ts_dt;
+  const uint8_t* dw; const uint8_t* dw_sf; const void* d_ts; int d_ts_dt;
+  int64_t E;
+  __nv_bfloat16* out;
+  __nv_bfloat16* h;      // k*I bf16 GeGLU rows
+  uint32_t* sync;        // [0] arrivals, [1] departures, [2] max |h| key over the grid
+  int* err;              // error word (bounded waits)
+};
+
+__host__ __device__ inline size_t a16(size_t v) { return (v + 15) / 16 * 16; }
+
+// Shared-memory carve-up of one CTA (np pairs, nr down rows).
+struct Carve {
+  size_t gate, up, gsf, usf, dn, dsf, hid, act, asa, hrow, end;
+};
+__host__ __device__ inline Carve carve(int H, int I, int k, int np, int nr) {
+  Carve c{};
+  const size_t rb = H / 2, sb = H / 16, rb2 = I / 2, sb2 = I / 16;
+  size_t o = 0;
+  c.gate = o; o = a16(o + (size_t)np * rb);
+  c.up = o;   o = a16(o + (size_t)np * rb);
+  c.gsf = o;  o = a16(o + (size_t)np * sb);
+  c.usf = o;  o = a16(o + (size_t)np * sb);
+  c.dn = o;   o = a16(o + (size_t)k * nr * rb2);
+  c.dsf = o;  o = a16(o + (size_t)k * nr * sb2);
+  c.hid = o;  o = a16(o + (size_t)H * 2);
+  c.act = o;  o = a16(o + (size_t)(H / 16) * 8 * sizeof(__half2));
+  c.asa = o;  o = a16(o + (size_t)(H / 16) * sizeof(float));
+  c.hrow = o; o = a16(o + (size_t)k * I * 2);
+  c.end = o;
+  return c;
+}
+
+static bool make_plan(int64_t k, int64_t H, int64_t I, int G, Plan& p) {
+  if (k < 1 || k > kMaxK || G < 1 || G > kMaxCtas) return false;
+  if (H <= 0 || I <= 0 || H % 256 != 0 || I % 64 != 0) return false;
+  if (H / 32 > 32 * kMaxChunks || I / 32 > 32) return false;
+  p.H = (int)H; p.I = (int)I; p.k = (int)k; p.G = G;
+  p.rows = (int)(((H + G - 1) / G + 3) / 4 * 4);
+  if (p.rows > kMaxRows) return false;
+  const double pair_b = 2.0 * (H / 2 + H / 16);
+  const double row_b = (double)k * (I / 2 + I / 16);
+  const int64_t pairs = k * I;
+  const double total = pairs * pair_b + H * row_b;
+  const double target = total / G;
+  double down_before = 0.0;
+  for (int c = 0; c <= G; ++c) {
+    int64_t q = (int64_t)((c * target - down_before) / pair_b + 0.5);
+    q = q < 0 ? 0 : (q > pairs ? pairs : q);
+    if (c == G) q = pairs;
+    if (c > 0 && q < p.pair0[c - 1]) q = p.pair0[c - 1];
+    p.pair0[c] = (int)q;
+    if (c < G) {
+      const int64_t r0 = (int64_t)c * p.rows;
+      const int64_t nr = r0 < H ? (H - r0 < p.rows ? H - r0 : p.rows) : 0;
+      down_before += nr * row_b;
+    }
+  }
+  size_t need = 0;
+  p.max_pairs = 0;
+  for (int c = 0; c < G; ++c) {
+    const int np = p.pair0[c + 1] - p.pair0[c];
+    p.max_pairs = np > p.max_pairs ? np : p.max_pairs;
+    const int64_t r0 = (int64_t)c * p.rows;
+    const int nr = (int)(r0 < H ? (H - r0 < p.rows ? H - r0 : p.rows) : 0);
+    const size_t b = carve(p.H, p.I, p.k, np, nr).end;
+    need = b > need ? b : need;
+  }
+  if ((p.max_pairs + kGroup - 1) / kGroup > kMaxGroups) return false;
+  p.bytes = need + 1024;
+  return p.bytes <= kSmemCap;
+}
+
+__device__ __forceinline__ void complete_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(sm100::smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// Quantize 16 bf16 values with tensor scale ts into exact halves plus the
+// 2^14-scaled block scale (chunk_dot's activation operand).
+__device__ __forceinline__ void quant16_smem(const __nv_bfloat16* src, float ts, __half2* dst, float* sa16k) {
+  float v[16];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const uint4 u = reinterpret_cast<const uint4*>(src)[q];
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[8 * q + j] = __bfloat162float(e[j]);
+  }
+  uint32_t w0, w1;
+  const uint32_t sf = nvfp4_quant_block(v, ts, w0, w1);
+  __half2 t[4];
+  fp4x8_to_half2x4_exact(w0, t);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[i] = t[i];
+  fp4x8_to_half2x4_exact(w1, t);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[4 + i] = t[i];
+  *sa16k = e4m3_decode(sf) * 16384.0f;
+}
+
+// L2 policy for data read once: evict first.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// Bulk global -> shared copy with an L2 cache policy.
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+          "r"((uint32_t)__cvta_generic_to_shared(dst)),
+      "l"(src), "r"(bytes), "r"((uint32_t)__cvta_generic_to_shared(bar)), "l"(pol)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const Args a, const Plan pl) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bars[kMaxGroups + kMaxK];
+  __shared__ int64_t ids_w[kWarps][kMaxK];
+  __shared__ uint32_t red[kWarps];
+  __shared__ float prod[kMaxK][kMaxRows];
+  __shared__ float topw_s[kMaxK];
+  __shared__ uint32_t hmax_s;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int H = pl.H, I = pl.I, k = pl.k;
+  const size_t rb = H / 2, sb = H / 16, rb2 = I / 2, sb2 = I / 16;
+  const int p0 = pl.pair0[blockIdx.x], np = pl.pair0[blockIdx.x + 1] - p0;
+  const int ngroups = (np + kGroup - 1) / kGroup;
+  const int r0 = (int)blockIdx.x * pl.rows;
+  const int nr = r0 < H ? min(pl.rows, H - r0) : 0;
+  const Carve cv = carve(H, I, k, np, nr);
+  uint64_t* bdown = &bars[kMaxGroups];   // one per expert slot
+
+  // ---- every warp: its barriers, the expert ids, its share of the copies ----
+  // Warp w owns pair groups g = w, w + 16, ... and the down block of slot
+  // j = w. Every warp loads the k ids itself (one L2 line), so no warp waits
+  // for another before issuing. The copies carry an L2 evict-first hint: the
+  // streamed weights are read once and must not push the kernel's code and
+  // small operands out of L2.
+  if (lane == 0) {
+    for (int g = warp; g < ngroups; g += kWarps) sm100::mbar_init(&bars[g], 1);
+    if (warp < k) sm100::mbar_init(&bdown[warp], 1);
+    sm100::fence_barrier_init();
+  }
+  if (lane < k) {
+    const int64_t e = load_index(a.ids, a.ids_dt, lane);
+    ids_w[warp][lane] = (e < 0 || e >= a.E) ? -1 : e;
+  }
+  __syncwarp();
+  if (lane == 0) {
+    const uint64_t pol = l2_evict_first();
+    for (int g = warp; g < ngroups; g += kWarps) {
+      const int i0 = g * kGroup, i1 = min(np, i0 + kGroup);
+      sm100::mbar_arrive_expect_tx(&bars[g], (uint32_t)((i1 - i0) * (2 * rb + 2 * sb)));
+      int i = i0;
+      while (i < i1) {   // split at slot boundaries
+        const int p = p0 + i, j = p / I, n = p - j * I;
+        const int len = min(i1 - i, I - n);
+        const int64_t e = ids_w[warp][j];
+        if (e >= 0) {
+          const uint8_t* g0 = a.gu + ((size_t)e * 2 * I + n) * rb;
+          const uint8_t* s0 = a.gu_sf + ((size_t)e * 2 * I + n) * sb;
+          bulk_g2s_hint(smem + cv.gate + i * rb, g0, (uint32_t)(len * rb), &bars[g], pol);
+          bulk_g2s_hint(smem + cv.up + i * rb, g0 + (size_t)I * rb, (uint32_t)(len * rb), &bars[g], pol);
+          bulk_g2s_hint(smem + cv.gsf + i * sb, s0, (uint32_t)(len * sb), &bars[g], pol);
+          bulk_g2s_hint(smem + cv.usf + i * sb, s0 + (size_t)I * sb, (uint32_t)(len * sb), &bars[g], pol);
+        } else {
+          complete_tx(&bars[g], (uint32_t)(len * (2 * rb + 2 * sb)));
+        }
+        i += len;
+      }
+    }
+    if (warp < k) {
+      const int j = warp;
+      const int64_t e = ids_w[warp][j];
+      sm100::mbar_arrive_expect_tx(&bdown[j], (uint32_t)(nr * (rb2 + sb2)));
+      if (e >= 0 && nr > 0) {
+        bulk_g2s_hint(smem + cv.dn + (size_t)j * nr * rb2, a.dw + ((size_t)e * H + r0) * rb2, (uint32_t)(nr * rb2),
+                      &bdown[j], pol);
+        bulk_g2s_hint(smem + cv.dsf + (size_t)j * nr * sb2, a.dw_sf + ((size_t)e * H + r0) * sb2,
+                      (uint32_t)(nr * sb2), &bdown[j], pol);
+      } else if (nr > 0) {
+        complete_tx(&bdown[j], (uint32_t)(nr * (rb2 + sb2)));
+      }
+    }
+  }
+  __syncwarp();
+
+  // ---- hidden vector: stage in shared memory, amax, quantize ---------------
+  __nv_bfloat16* hid_s = reinterpret_cast<__nv_bfloat16*>(smem + cv.hid);
+  uint32_t key = 0;
+  for (int i = tid; i < H / 8; i += kThreads) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(a.hidden) + i);
+    reinterpret_cast<uint4*>(hid_s)[i] = u;
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) key = max(key, In<AEOQ_BF16>::abs_key(e[j]));
+  }
+  const float gu_ts = load_scalar_f(a.gu_ts, a.gu_ts_dt);
+  const float d_ts = load_scalar_f(a.d_ts, a.d_ts_dt);
+  if (tid < k) topw_s[tid] = __bfloat162float(a.topw[tid]);
+  key = warp_umax(key);
+  if (lane == 0) red[warp] = key;
+  __syncthreads();   // hid_s, red, topw_s, ids_w, barrier inits
+  key = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) key = max(key, red[w]);
+  const float ts = nvfp4_tensor_scale<AEOQ_BF16>(In<AEOQ_BF16>::key_to_f(key));
+  const float alpha = ts * gu_ts;
+  __half2* act_s = reinterpret_cast<__half2*>(smem + cv.act);
+  float* asa_s = reinterpret_cast<float*>(smem + cv.asa);
+  for (int b = tid; b < H / 16; b += kThreads) quant16_smem(hid_s + 16 * b, ts, act_s + 8 * b, asa_s + b);
+  __syncthreads();
+
+  // ---- gate/up GEMV + GeGLU, pair groups as they land ----------------------
+  const int nchunk = H / 32;
+  __half2 act[kMaxChunks][16];
+  float sa[kMaxChunks][2];
+#pragma unroll
+  for (int q = 0; q < kMaxChunks; ++q) {
+    const int c = lane + 32 * q;
+    if (c < nchunk) {
+      const uint4* ap = reinterpret_cast<const uint4*>(act_s + 16 * c);
+#pragma unroll
+      for (int z = 0; z < 4; ++z) *reinterpret_cast<uint4*>(&act[q][4 * z]) = ap[z];
+      sa[q][0] = asa_s[2 * c];
+      sa[q][1] = asa_s[2 * c + 1];
+    }
+  }
+  const uint8_t* gate_s = smem + cv.gate;
+  const uint8_t* up_s = smem + cv.up;
+  const uint8_t* gsf_s = smem + cv.gsf;
+  const uint8_t* usf_s = smem + cv.usf;
+  uint32_t hkey = 0;
+  bool ok = true;
+  for (int i = warp; i < np; i += kWarps) {
+    // pair i lies in group i / kGroup, whose copies another warp may own
+    ok &= sm100::mbar_wait(&bars[i / kGroup], 0, a.err, 31);
+    const int p = p0 + i, j = p / I;
+    const bool valid = ok && ids_w[0][j] >= 0;
+    float ag = 0.f, au = 0.f;
+    if (valid) {
+#pragma unroll
+      for (int q = 0; q < kMaxChunks; ++q) {
+        const int c = lane + 32 * q;
+        if (c < nchunk) {
+          const uint4 gw = *reinterpret_cast<const uint4*>(gate_s + i * rb + 16 * c);
+          const uint4 uw = *reinterpret_cast<const uint4*>(up_s + i * rb + 16 * c);
+          const uint16_t gs = *reinterpret_cast<const uint16_t*>(gsf_s + i * sb + 2 * c);
+          const uint16_t us = *reinterpret_cast<const uint16_t*>(usf_s + i * sb + 2 * c);
+          ag = chunk_dot(act[q], sa[q], gw, gs, ag);
+          au = chunk_dot(act[q], sa[q], uw, us, au);
+        }
+      }
+    }
+    ag = warp_sum(ag);
+    au = warp_sum(au);
+    if (lane == 0) {
+      const float gv = bf16r(ag * alpha), uv = bf16r(au * alpha);
+      const __nv_bfloat16 hv = __float2bfloat16_rn(bf16r(gelu_tanh(gv)) * uv);
+      a.h[p] = hv;
+      hkey = max(hkey, In<AEOQ_BF16>::abs_key(hv));
+    }
+  }
+  // every group barrier completes before the CTA exits (the copies land)
+  for (int g = warp; g < ngroups; g += kWarps) sm100::mbar_wait(&bars[g], 0, a.err, 31);
+  hkey = warp_umax(hkey);
+  if (lane == 0) red[warp] = hkey;
+  __syncthreads();
+
+  // ---- grid barrier ----------------------------------------------------------
+  // One word holds the grid's max |h| key (atomicMax before the arrival), so
+  // after the barrier each CTA reads one word, not every CTA's maximum: all
+  // CTAs reading the same few L2 lines at once serialise there. The pollers
+  // back off after a short spin for the same reason.
+  if (tid == 0) {
+    uint32_t m = 0;
+    for (int w = 0; w < kWarps; ++w) m = max(m, red[w]);
+    if (m) atomicMax(a.sync + 2, m);
+    __threadfence();   // h and the maximum ordered before the arrival
+    atomicAdd(a.sync + 0, 1u);
+    bool done = false;
+    for (uint32_t it = 0; it < sm100::kSpinLimit; ++it) {
+      uint32_t v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync + 0) : "memory");
+      if (v >= (uint32_t)pl.G) { done = true; break; }
+      if (it >= 32) __nanosleep(40);
+    }
+    if (!done) atomicCAS(a.err, 0, 32);
+    hmax_s = __ldcg(a.sync + 2);
+  }
+  __syncthreads();
+
+  // ---- the k GeGLU rows into shared memory, one coalesced read per CTA -------
+  __nv_bfloat16* hrow_s = reinterpret_cast<__nv_bfloat16*>(smem + cv.hrow);
+  for (int i = tid; i < k * I / 8; i += kThreads)
+    reinterpret_cast<uint4*>(hrow_s)[i] = __ldcg(reinterpret_cast<const uint4*>(a.h) + i);
+  const float hts = nvfp4_tensor_scale<AEOQ_BF16>(In<AEOQ_BF16>::key_to_f(hmax_s));
+  const float alpha_d = hts * d_ts;
+  __syncthreads();
+
+  // ---- down GEMV: warps own one expert slot each -----------------------------
+  const int wpj = kWarps / k;            // warps per slot
+  const int nchunk2 = I / 32;            // <= 32: one chunk per lane
+  if (warp < wpj * k && nr > 0) {
+    const int j = warp / wpj;
+    const bool ok_dn = sm100::mbar_wait(&bdown[j], 0, a.err, 33);
+    const bool valid = ok_dn && ids_w[0][j] >= 0;
+    const float wj = topw_s[j];
+    __half2 hv[16];
+    float hs[2] = {0.f, 0.f};
+    if (lane < nchunk2) {
+      const __nv_bfloat16* src = hrow_s + (size_t)j * I + 32 * lane;
+      quant16_smem(src, hts, hv, &hs[0]);
+      quant16_smem(src + 16, hts, hv + 8, &hs[1]);
+    }
+    const uint8_t* dn_s = smem + cv.dn + (size_t)j * nr * rb2;
+    const uint8_t* dsf_s = smem + cv.dsf + (size_t)j * nr * sb2;
+    for (int r = warp % wpj; r < nr; r += wpj) {
+      float acc = 0.f;
+      if (valid && lane < nchunk2)
+        acc = chunk_dot(hv, hs, *reinterpret_cast<const uint4*>(dn_s + r * rb2 + 16 * lane),
+                        *reinterpret_cast<const uint16_t*>(dsf_s + r * sb2 + 2 * lane), acc);
+      acc = warp_sum(acc);
+      if (lane == 0) prod[j][r] = valid ? bf16r(bf16r(acc * alpha_d) * wj) : 0.0f;
+    }
+  } else if (warp < k) {
+    sm100::mbar_wait(&bdown[warp], 0, a.err, 33);   // nr == 0: nothing in flight, the phase is complete
+  }
+  __syncthreads();
+  if (tid < nr) {
+    double s = 0.0;
+    for (int j = 0; j < k; ++j) s += (double)prod[j][tid];
+    a.out[r0 + tid] = __float2bfloat16_rn((float)s);
+  }
+
+  // ---- departure: the last CTA out resets the counters ----------------------
+  if (tid == 0) {
+    const uint32_t d = atomicAdd(a.sync + 1, 1u);
+    if (d == (uint32_t)pl.G - 1) {
+      a.sync[0] = 0;
+      a.sync[1] = 0;
+      a.sync[2] = 0;
+      __threadfence();
+    }
+  }
+}
+
+}  // namespace dst
+}  // namespace aeoq
+
+using namespace aeoq;
+
+static bool stream_plan(int64_t k, int64_t H, int64_t I, dst::Plan& p) {
+  return dst::make_plan(k, H, I, device_sm_count(), p);
+}
+
+extern "C" int aeoq_moe_nvfp4_decode_stream_supported(int64_t top_k, int64_t hidden, int64_t inter) {
+  dst::Plan p;
+  return stream_plan(top_k, hidden, inter, p) ? 1 : 0;
+}
+
+// Workspace: [counters 256 B][k*I bf16 GeGLU rows, 256-aligned].
+extern "C" size_t aeoq_moe_nvfp4_decode_stream_workspace_size(int64_t top_k, int64_t hidden, int64_t inter) {
+  (void)hidden;
+  return 256 + ((size_t)(top_k * inter) * 2 + 255) / 256 * 256;
+}
+
+extern "C" int aeoq_moe_nvfp4_decode_stream(const void* hidden, const void* top_k_index, int idx_dtype,
+                                            const void* top_k_weights, int64_t top_k, const uint8_t* gate_up,
+                                            const uint8_t* gate_up_sf, const void* gate_up_ts, int gate_up_ts_dtype,
+                                            const uint8_t* down, const uint8_t* down_sf, const void* down_ts,
+                                            int down_ts_dtype, int64_t num_experts, int64_t hidden_dim,
+                                            int64_t inter_dim, void* out, void* workspace, size_t workspace_bytes,
+                                            int* err_word, void* stream) {
+  dst::Plan pl;
+  AEOQ_REQUIRE(stream_plan(top_k, hidden_dim, inter_dim, pl), AEOQ_ERR_INVALID,
+               "moe_decode_stream: unsupported shape (top_k=%lld hidden=%lld inter=%lld)", (long long)top_k,
+               (long long)hidden_dim, (long long)inter_dim);
+  AEOQ_REQUIRE(idx_dtype == AEOQ_I32 || idx_dtype == AEOQ_I64, AEOQ_ERR_INVALID,
+               "moe_decode_stream: top_k_index must be int32 or int64");
+  AEOQ_REQUIRE(hidden && top_k_index && top_k_weights && gate_up && gate_up_sf && gate_up_ts && down && down_sf &&
+                   down_ts && out && err_word,
+               AEOQ_ERR_INVALID, "moe_decode_stream: null pointer");
+  AEOQ_REQUIRE(((uintptr_t)hidden % 16 == 0) && ((uintptr_t)gate_up % 16 == 0) && ((uintptr_t)down % 16 == 0) &&
+                   ((uintptr_t)gate_up_sf % 16 == 0) && ((uintptr_t)down_sf % 16 == 0),
+               AEOQ_ERR_INVALID, "moe_decode_stream: hidden, weights and scales must be 16-byte aligned");
+  const size_t need = aeoq_moe_nvfp4_decode_stream_workspace_size(top_k, hidden_dim, inter_dim);
+  AEOQ_REQUIRE(workspace && workspace_bytes >= need && (uintptr_t)workspace % 256 == 0, AEOQ_ERR_WORKSPACE,
+               "moe_decode_stream: workspace of %zu bytes (256-aligned, first 256 B zero) needed, %zu given", need,
+               workspace_bytes);
+  char* w = reinterpret_cast<char*>(workspace);
+  dst::Args a{};
+  a.hidden = reinterpret_cast<const __nv_bfloat16*>(hidden);
+  a.ids = top_k_index; a.ids_dt = idx_dtype;
+  a.topw = reinterpret_cast<const __nv_bfloat16*>(top_k_weights);
+  a.gu = gate_up; a.gu_sf = gate_up_sf; a.gu_ts = gate_up_ts; a.gu_ts_dt = gate_up_ts_dtype;
+  a.dw = down; a.dw_sf = down_sf; a.d_ts = down_ts; a.d_ts_dt = down_ts_dtype;
+  a.E = num_experts;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out);
+  a.sync = reinterpret_cast<uint32_t*>(w);
+  a.h = reinterpret_cast<__nv_bfloat16*>(w + 256);
+  a.err = err_word;
+  {
+    const int rc = func_smem_attr((const void*)dst::decode_stream_kernel, pl.bytes, -1, "moe_decode_stream");
+    if (rc) return rc;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)pl.G);
+  cfg.blockDim = dim3(dst::kThreads);
+  cfg.dynamicSmemBytes = pl.bytes;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, dst::decode_stream_kernel, a, pl);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(AEOQ_ERR_CUDA, "decode_stream_kernel: %s", cudaGetErrorString(e));
+  }
+  return check_launch("decode_stream_kernel");
+}

@@ -11,13 +11,24 @@ softmax(N(0, 1)). 32 independent layers are resident and steps cycle through
 them, so each step streams cold weights from HBM (26.8 MB per step, 830 MB
 between revisits; L2 is 126 MB): inputs larger than L2, no flush needed.
 
+The same line carries the other measured rows, each through the public API:
+``prefill`` (the single NVFP4 linear at M = 128 with its HBM fraction, at
+M = 8192 and 32768, and the grouped FP8 / NVFP4 expert prefill at 4096
+tokens), ``decode_batch_sweep`` (batch 4, 16, 64 with an HBM roofline from
+the realized unique experts), ``quantizer`` (NVFP4 activation quantization,
+HBM GB/s) and ``ep`` (the expert-parallel stack of 4 layers over 65,536
+Zipf-routed tokens on the same N GPUs, strong scaling, with the one-GPU time
+of the same stack for the efficiency).
+
 Multi-GPU: one-token decode does not shard (expert parallelism only pays at
 prefill sizes), so N GPUs run N independent replicas; value = all ranks'
-tokens / max-over-ranks device time ("scaling": "weak").
+tokens / max-over-ranks device time ("scaling": "weak"). The ``ep`` leg is
+the sharded workload.
 
 ``--impl reference`` times the reference algorithm on the host CPU: the
-numpy port in ``oracle/`` (the reference's own path needs a GPU and Triton)
-on a bounded token sample with all host threads, rank 0 only.
+torch restatement in ``oracle/torch_port.py`` (the reference's own path needs
+a GPU and Triton) on a bounded token sample with every host thread, rank 0
+only.
 """
 from __future__ import annotations
 
@@ -41,10 +52,10 @@ DOWN_BYTES = 2816 * 352 + 2816 * 44
 METRIC = "MoE decode tok/s (M=1 gather) + NVFP4 prefill TFLOPS, % of roofline"
 FALLBACK_HBM_GBS = 6650.0
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one tensor-core decode
-# (both launches) at this workload, from the ncu capture summarised in
-# the committed ncu summary of the decode pair (None until captured).
-NCU_TRAFFIC_TC = 27048448
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode at this
+# workload, from the committed ncu summary of each one-token kernel (None
+# where the current kernel has not been captured).
+NCU_TRAFFIC = {"stream": None, "tc": 27048448}
 
 
 def parse():
@@ -58,6 +69,7 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     p.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM measurements")
+    p.add_argument("--no-ep", action="store_true", help="skip the expert-parallel (config 4) leg")
     p.add_argument("--workload", default="decode", choices=["decode", "ep", "gemm", "stack", "router", "grouped"],
                    help="decode: config 1 (default); ep: config 4, expert-parallel prefill stack; "
                         "gemm: config-0 NVFP4 linear at --gemm-m rows (profiling)")
@@ -289,6 +301,12 @@ def measure_prefill(torch, dev, lib, A):
                             20 if M < 32768 else 10)
         tf = 2.0 * M * 1408 * 2816 / us / 1e6
         out[f"config0_M{M}"] = {"us": round(us, 2), "tflops": round(tf, 1), "frac_fp4_nominal": round(tf / 9000, 4)}
+        if M == 128:
+            # HBM-bound shape: packed operands + scales in, bf16 out
+            byt = M * 2816 * 0.5625 + 1408 * 2816 * 0.5625 + M * 1408 * 2
+            gbs = byt / (us * 1e-6) / 1e9
+            out[f"config0_M{M}"].update({"algorithmic_bytes": int(byt), "gbs": round(gbs, 1),
+                                         "frac_hbm": round(gbs / peaks()[0], 4)})
     T, k = 4096, TOPK
     gq, gs = Q.quantize_3d_to_fp8((torch.randn(E, 2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16))
     dq, ds = Q.quantize_3d_to_fp8((torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16))
@@ -383,112 +401,189 @@ def main_grouped(args, local):
                       **out}), flush=True)
 
 
-def main_ep(args, rank, world, local):
-    """Config 4: a stack of NVFP4 MoE layers (config-2 shapes), experts
-    sharded E/world per GPU, tokens sharded by sequence, NCCL all-to-all
-    dispatch (NVFP4-packed rows) and combine (bf16 rows). One step = the
-    whole stack over all ranks' tokens; value = tokens / max-over-ranks
-    device time (strong scaling: the token count is fixed)."""
-    import torch
-    import torch.distributed as dist
+def ep_layers(torch, dev, rank, world, n_layers, owner):
+    """The config-4 stack's NVFP4 expert layers for this rank: expert e of
+    layer l drawn from its own seeded generator (the same weights whatever
+    the world size or placement), this rank's experts (owner[e] == rank,
+    ascending id; all of them when owner is None) quantized on the device."""
+    import types
     from aeo_quant_b200.bridges.gemma4.expert_parallel import ExpertParallelNVFP4
     from aeo_quant_b200.bridges.gemma4.modeling_nvfp4 import Gemma4TextExpertsNVFP4
     from aeo_quant_b200.gpu import quant as Q
-    import types
-
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
-    else:
-        dist.init_process_group("nccl", init_method="tcp://127.0.0.1:29599", rank=0, world_size=1, device_id=dev)
-    K, W = args.steps, max(3, args.warmup)
-    e_loc = E // world
-    T = args.tokens // world
-    g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    cfg = types.SimpleNamespace(num_experts=e_loc, hidden_size=H, moe_intermediate_size=I,
+    mine = list(range(E)) if owner is None else [e for e in range(E) if int(owner[e]) == rank]
+    cfg = types.SimpleNamespace(num_experts=len(mine), hidden_size=H, moe_intermediate_size=I,
                                 hidden_activation="gelu_pytorch_tanh")
     layers = []
-    for l in range(args.ep_layers):
-        gl = torch.Generator(device=dev).manual_seed(10 * l + 1)   # same weights on every rank
+    for l in range(n_layers):
+        wgu = torch.empty(len(mine), 2 * I, H, dtype=torch.bfloat16, device=dev)
+        wd = torch.empty(len(mine), H, I, dtype=torch.bfloat16, device=dev)
+        for i, e in enumerate(mine):
+            ge = torch.Generator(device=dev).manual_seed(100000 * (l + 1) + e)
+            wgu[i] = (torch.randn(2 * I, H, generator=ge, device=dev) * 0.02).to(torch.bfloat16)
+            wd[i] = (torch.randn(H, I, generator=ge, device=dev) * 0.02).to(torch.bfloat16)
         m = Gemma4TextExpertsNVFP4(cfg).to(dev)
-        for r in range(world):   # draw every rank's slice so the stack is independent of world
-            wgu = (torch.randn(e_loc, 2 * I, H, generator=gl, device=dev) * 0.02).to(torch.bfloat16)
-            wd = (torch.randn(e_loc, H, I, generator=gl, device=dev) * 0.02).to(torch.bfloat16)
-            if r == rank:
-                gp, gs, gt = Q.quantize_3d_to_nvfp4(wgu)
-                dp, ds, dt = Q.quantize_3d_to_nvfp4(wd)
-            del wgu, wd
+        gp, gs, gt = Q.quantize_3d_to_nvfp4(wgu)
+        dp, ds, dt = Q.quantize_3d_to_nvfp4(wd)
+        del wgu, wd
         m.gate_up_proj.copy_(gp); m.gate_up_proj_scale.copy_(gs); m.gate_up_proj_scale_2.copy_(gt.float())
         m.down_proj.copy_(dp); m.down_proj_scale.copy_(ds); m.down_proj_scale_2.copy_(dt.float())
-        layers.append(ExpertParallelNVFP4(m, E))
-    hid = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
-    # Zipf(s=1.2) over a seeded permutation of the experts, 8 distinct per token
+        layers.append(ExpertParallelNVFP4(m, E, owner=owner) if owner is not None else m)
+    return layers
+
+
+def zipf_ids(torch, dev, T, seed):
+    """Zipf(s=1.2) over a seeded permutation of the experts, 8 distinct per
+    token; softmax(N(0,1)) weights."""
+    g = torch.Generator(device=dev).manual_seed(seed)
     perm = torch.randperm(E, generator=torch.Generator().manual_seed(5)).to(dev)
     p = 1.0 / torch.arange(1, E + 1, device=dev, dtype=torch.float32) ** 1.2
     ids = perm[torch.multinomial(p.expand(T, E), TOPK, replacement=False, generator=g)]
     wts = torch.softmax(torch.randn(T, TOPK, generator=g, device=dev), -1).to(torch.bfloat16)
+    return ids, wts
+
+
+def run_ep(args, rank, world, local, steps, warmup):
+    """Config 4: a stack of ``--ep-layers`` NVFP4 MoE layers (128 experts,
+    H 2816, I 704) over ``--tokens`` tokens split by sequence over the
+    ranks, Zipf(1.2) top-8 routing. With N > 1 experts are placed on ranks by
+    ``balanced_placement`` of the global routing histogram (E/N per rank);
+    dispatch (NVFP4-packed rows) and combine (bf16 rows) are NCCL
+    all-to-alls. One step = the whole stack over every rank's tokens; value
+    = tokens / max-over-ranks device time (strong scaling: the token count
+    is fixed). At N = 1 it is the one-GPU forward. The process group must be
+    initialised when N > 1. Returns the leg's dict on rank 0."""
+    import torch
+    import torch.distributed as dist
+    from aeo_quant_b200.bridges.gemma4.expert_parallel import balanced_placement
+    dev = torch.device("cuda", local)
+    T = args.tokens // world
+    ids, wts = zipf_ids(torch, dev, T, 1000 + rank)
+    hid = torch.randn(T, H, generator=torch.Generator(device=dev).manual_seed(2000 + rank), device=dev).to(
+        torch.bfloat16)
+    owner = None
+    if world > 1:
+        load = torch.bincount(ids.reshape(-1), minlength=E).to(torch.float64)
+        dist.all_reduce(load)
+        owner = balanced_placement(load.cpu(), world)
+    layers = ep_layers(torch, dev, rank, world, args.ep_layers, owner)
 
     def step(x):
         for lay in layers:
             x = lay(x, ids, wts)
         return x
 
-    for _ in range(W):
-        step(hid)
-    torch.cuda.synchronize()
-    dist.barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        ev0.record()
-        for _ in range(K):
-            y = step(hid)
-        ev1.record()
+    def timed(fn, K):
         torch.cuda.synchronize()
-    dist.barrier()
-    t = torch.tensor([ev0.elapsed_time(ev1)], device=dev)
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(K):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(warmup):
+        step(hid)
+    with ClockSampler(local) as clk:
+        ms = timed(lambda: step(hid), steps)
+    phases = None
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    value = args.tokens * K / (ms / 1000.0)
-    flops = args.tokens * TOPK * 2 * (1408 * 2816 + 2816 * 704) * args.ep_layers * K
+        # phase split of one instrumented step (CUDA events at each phase start)
+        evs = []
+
+        def mark(name):
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            evs.append((name, ev))
+        for lay in layers:
+            lay.mark = mark
+        step(hid)
+        torch.cuda.synchronize()
+        for lay in layers:
+            lay.mark = None
+        acc = {"dispatch": 0.0, "experts": 0.0, "combine": 0.0}
+        for (n0, a), (_, b) in zip(evs, evs[1:]):
+            if n0 in acc:
+                acc[n0] += a.elapsed_time(b)
+        ph = torch.tensor([acc["dispatch"], acc["experts"], acc["combine"]], device=dev)
+        dist.all_reduce(ph, op=dist.ReduceOp.MAX)
+        phases = dict(zip(("dispatch", "experts", "combine"), [round(v, 3) for v in ph.tolist()]))
     # e2e: this rank's tokens from pinned host memory, the output back
     hid_h = hid.cpu().pin_memory()
     out_h = torch.empty_like(hid_h).pin_memory()
-    dist.barrier()
-    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    b0.record()
     x_in = torch.empty_like(hid)
-    for _ in range(K):
+
+    def e2e_step():
         x_in.copy_(hid_h, non_blocking=True)
         out_h.copy_(step(x_in), non_blocking=True)
-    b1.record()
-    torch.cuda.synchronize()
-    te = torch.tensor([b0.elapsed_time(b1)], device=dev)
+    ms_e2e = timed(e2e_step, steps)
+    # the same stack with every expert on one GPU, for the efficiency
+    ms_1 = None
     if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e = args.tokens * K / (float(te.item()) / 1000.0)
+        del layers
+        torch.cuda.empty_cache()
+        if rank == 0:
+            parts = [zipf_ids(torch, dev, T, 1000 + r) for r in range(world)]
+            all_ids = torch.cat([p[0] for p in parts])
+            all_w = torch.cat([p[1] for p in parts])
+            all_h = torch.cat([torch.randn(T, H, generator=torch.Generator(device=dev).manual_seed(2000 + r),
+                                           device=dev).to(torch.bfloat16) for r in range(world)])
+            one = ep_layers(torch, dev, 0, 1, args.ep_layers, None)
+
+            def step1():
+                x = all_h
+                for lay in one:
+                    x = lay(x, all_ids, all_w)
+            for _ in range(warmup):
+                step1()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                step1()
+            e1.record()
+            torch.cuda.synchronize()
+            ms_1 = e0.elapsed_time(e1)
+            del one
+        dist.barrier()
+    if rank != 0:
+        return None
+    flops = args.tokens * TOPK * 11894784 * args.ep_layers * steps
+    ach = flops / (ms / 1000.0) / 1e12 / world
+    out = {"workload": f"config4: NVFP4 MoE stack, {args.ep_layers} layers, {args.tokens} tokens "
+                       f"(Zipf(1.2) top-8) over {world} GPU(s)",
+           "tok_s": round(args.tokens * steps / (ms / 1000.0), 1), "ms_per_step": round(ms / steps, 3),
+           "steps": steps, "warmup": warmup, "scaling": "strong",
+           "placement": "balanced_placement of the global routing histogram" if world > 1 else "one GPU, all experts",
+           "phase_ms_per_step": phases,
+           "tflops_per_gpu": round(ach, 1), "frac_fp4_nominal": round(ach / 9000.0, 4),
+           "e2e_tok_s": round(args.tokens * steps / (ms_e2e / 1000.0), 1),
+           "clocks": clk.summary()}
+    if ms_1 is not None:
+        out["one_gpu_ms_per_step"] = round(ms_1 / steps, 3)
+        out["efficiency_vs_one_gpu"] = round(ms_1 / (world * ms), 4)
+    return out
+
+
+def main_ep(args, rank, world, local):
+    """``--workload ep``: the config-4 leg alone, as its own JSON line."""
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    r = run_ep(args, rank, world, local, args.steps, max(3, args.warmup))
     if rank == 0:
-        ach = flops / (ms / 1000.0) / 1e12 / world
-        print(json.dumps({
-            "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": K,
-            "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "fp4(e2m1)+e4m3 scales, fp32 accumulate, bf16 io",
-            "data": "synthetic (bf16 N(0,0.02) weights quantized on device; N(0,1) hidden; Zipf(1.2) top-8)",
-            "config": {"workload": f"config4: expert-parallel NVFP4 MoE stack, {args.ep_layers} layers, "
-                                   f"{args.tokens} tokens over {world} GPU(s)",
-                       "experts": E, "experts_per_gpu": e_loc, "hidden": H, "intermediate": I, "top_k": TOPK,
-                       "parallelism": f"ep{world}", "timing": "CUDA events around K steps, max over ranks",
-                       "l2": "inputs larger than L2 (activations and expert weights per step)"},
-            "gpu_launches": None,
-            "clocks": clk.summary(),
-            "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": args.tokens * H * 2,
-                    "d2h_bytes_per_step": args.tokens * H * 2},
-            "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": 9000.0, "unit": "TFLOP/s",
-                         "frac": round(ach / 9000.0, 4), "peak_source": "nominal dense FP4 (no measured FP4 peak)",
-                         "traffic": None, "per": "GPU"},
-        }), flush=True)
-    dist.destroy_process_group()
+        print(json.dumps({"metric": "config4 expert-parallel MoE stack tok/s", "value": r["tok_s"], "unit": "tok/s",
+                          "n_gpus": world, "higher_is_better": True, "ep": r}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
 
 
 def stack_config(layers):
@@ -665,6 +760,61 @@ def main_stack(args, local):
     }), flush=True)
 
 
+def measure_batch_sweep(torch, dev, mods, L, steps, seed):
+    """Config 1 at batch 4, 16 and 64: B tokens through one MoE layer via
+    the module API (the reference's prefill semantics for B > 1), layers
+    cycled as in the headline, timed as one CUDA graph of ``steps`` calls.
+    HBM roofline per B with the realized unique experts U per step:
+    bytes = U * 3,345,408 + B * 2816 * 4 + B * 8 * 10."""
+    hbm = peaks()[0]
+    out = {}
+    for B in (4, 16, 64):
+        S = steps + 4
+        idx, wts, hid = routing(torch, S, B, seed + B)
+        idx_d, wts_d, hid_d = idx.to(dev), wts.to(dev), hid.to(dev)
+        uniq = sum(len(set(idx[s2].reshape(-1).tolist())) for s2 in range(4, S)) / steps
+        for s2 in range(4):
+            mods[s2 % L](hid_d[s2], idx_d[s2], wts_d[s2])
+        torch.cuda.synchronize()
+        cs = torch.cuda.Stream(dev)
+        cs.wait_stream(torch.cuda.current_stream(dev))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(cs):
+            with torch.cuda.graph(g, stream=cs):
+                for s2 in range(4, S):
+                    mods[s2 % L](hid_d[s2], idx_d[s2], wts_d[s2])
+        torch.cuda.current_stream(dev).wait_stream(cs)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / steps
+        byt = uniq * EXPERT_BYTES + B * H * 4 + B * TOPK * 10
+        gbs = byt / (us * 1e-6) / 1e9
+        out[f"B{B}"] = {"us_per_step": round(us, 2), "tok_s": round(B / (us * 1e-6), 1),
+                        "unique_experts": round(uniq, 2), "algorithmic_bytes": int(byt), "gbs": round(gbs, 1),
+                        "frac_hbm": round(gbs / hbm, 4)}
+        del g
+    return out
+
+
+def measure_quantizer(torch, dev):
+    """The NVFP4 activation quantizer (quantize_2d_to_nvfp4) on 32768 x 2816
+    bf16 (184.5 MB, larger than L2), through the public API, one CUDA graph
+    of 10 calls. Algorithmic bytes per element: 2 read + 0.5625 written (the
+    amax pass's second read is not counted)."""
+    from aeo_quant_b200.gpu import quant as Q
+    x = torch.randn(32768, H, generator=torch.Generator(device=dev).manual_seed(3), device=dev).to(torch.bfloat16)
+    us = _graph_time_us(torch, dev, lambda: Q.quantize_2d_to_nvfp4(x), 10)
+    byt = x.numel() * 2.5625
+    gbs = byt / (us * 1e-6) / 1e9
+    return {"shape": [32768, H], "us": round(us, 2), "algorithmic_bytes": int(byt), "gbs": round(gbs, 1),
+            "frac_hbm": round(gbs / peaks()[0], 4)}
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
@@ -755,11 +905,13 @@ def main():
 
     tws_n = lib.aeoq_moe_nvfp4_decode_tc_workspace_size(TOPK, H, I)
     tws = torch.zeros(max(tws_n, 1), dtype=torch.uint8, device=dev)
+    sws_n = lib.aeoq_moe_nvfp4_decode_stream_workspace_size(TOPK, H, I)
+    sws = torch.zeros(max(sws_n, 1), dtype=torch.uint8, device=dev)
     err = A.err_word(dev)
 
     def launch(fn, s, ws, ws_n):
         gp, gs, gt, dp, ds, dt = layers[s % L]
-        extra = (err.data_ptr(),) if fn is lib.aeoq_moe_nvfp4_decode_tc else ()
+        extra = (err.data_ptr(),) if fn in (lib.aeoq_moe_nvfp4_decode_tc, lib.aeoq_moe_nvfp4_decode_stream) else ()
         return fn(hid_d[s].data_ptr(), idx_d[s].data_ptr(), A.I64, wts_d[s].data_ptr(), TOPK,
                   gp.data_ptr(), gs.data_ptr(), gt.data_ptr(), A.F32, dp.data_ptr(), ds.data_ptr(),
                   dt.data_ptr(), A.F32, E, H, I, out.data_ptr(), ws.data_ptr(), ws_n, *extra,
@@ -787,9 +939,12 @@ def main():
         return a0.elapsed_time(a1) / K
 
     stage_ms = {}
-    tc_path = B == 1 and moe_ops.DECODE_PATH in ("auto", "tc") and bool(
-        lib.aeoq_moe_nvfp4_decode_tc_supported(TOPK, H, I))
+    stream_path = B == 1 and moe_ops.DECODE_PATH in ("auto", "stream") and bool(
+        lib.aeoq_moe_nvfp4_decode_stream_supported(TOPK, H, I))
+    tc_path = B == 1 and bool(lib.aeoq_moe_nvfp4_decode_tc_supported(TOPK, H, I))
     if B == 1:
+        if stream_path:
+            stage_ms["stream"] = time_graph(lib.aeoq_moe_nvfp4_decode_stream, sws, sws_n)
         if tc_path:
             stage_ms["tc"] = time_graph(lib.aeoq_moe_nvfp4_decode_tc, tws, tws_n)
         stage_ms["fused"] = time_graph(lib.aeoq_moe_nvfp4_decode_fused, fws, fws_n)
@@ -797,6 +952,9 @@ def main():
 
     # ---- prefill: config-0 GEMMs and the config-2 FP8 expert prefill ----
     prefill = measure_prefill(torch, dev, lib, A) if (B == 1 and not args.no_prefill) else None
+    sweep = measure_batch_sweep(torch, dev, mods, L, min(K, 20), 31 + rank) if (
+        B == 1 and not args.no_prefill) else None
+    quantizer = measure_quantizer(torch, dev) if (B == 1 and not args.no_prefill) else None
 
     # ---- end to end through the public module API with host buffers ----
     hid_h = hid.pin_memory()
@@ -831,23 +989,32 @@ def main():
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_val = world * B * n_e2e / (float(e2e_ms.item()) / 1000.0)
 
+    # ---- config 4: the expert-parallel stack over the same N GPUs ----------
+    ep = None
+    if not args.no_ep and B == 1:
+        del mods, layers
+        torch.cuda.empty_cache()
+        ep = run_ep(args, rank, world, local, steps=min(K, 5), warmup=3)
+
     if rank == 0:
         hbm, peak_src = peaks()
         roof = None
-        key = "tc" if "tc" in stage_ms else "fused" if "fused" in stage_ms else None
+        key = next((k2 for k2 in ("stream", "tc", "fused") if k2 in stage_ms), None)
         if key:
             # algorithmic bytes: the k experts' packed weights and scales, the
             # hidden vector in and the output out (intermediates stay on chip
             # or in L2 and are not counted)
             alg = TOPK * EXPERT_BYTES + 2 * H * 2
             ach = alg / (stage_ms[key] / 1000.0) / 1e9
-            roof = {"bound": "hbm",
-                    "kernel": ("decode_gateup_tc_kernel + decode_down_tc_kernel (one programmatically "
-                               "dependent pair)") if key == "tc" else "moe_decode_fused_kernel",
+            kernel_names = {"stream": "decode_stream_kernel (one cooperative launch)",
+                            "tc": "decode_gateup_tc_kernel + decode_down_tc_kernel (one programmatically "
+                                  "dependent pair)",
+                            "fused": "moe_decode_fused_kernel"}
+            roof = {"bound": "hbm", "kernel": kernel_names[key],
                     "achieved": round(ach, 1), "peak": hbm,
                     "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
                     else "of fallback", "unit": "GB/s", "frac": round(ach / hbm, 4),
-                    "traffic": NCU_TRAFFIC_TC if key == "tc" else None, "algorithmic_bytes": alg,
+                    "traffic": NCU_TRAFFIC.get(key), "algorithmic_bytes": alg,
                     "launch_us": round(stage_ms[key] * 1000, 3),
                     "other_paths_us": {k2: round(v * 1000, 3) for k2, v in stage_ms.items() if k2 != key}}
         step_bytes = TOPK * EXPERT_BYTES + 2 * H * 2
@@ -858,7 +1025,7 @@ def main():
             "data": "synthetic (bf16 N(0,0.02) weights quantized on device; N(0,1) hidden; uniform top-8)",
             "config": decode_config(B, L, world),
             "step_hbm_gbs": round(step_bytes / (ms_max / K / 1000.0) / 1e9, 1),
-            "gpu_launches": (2 if tc_path else 1) * K,
+            "gpu_launches": (1 if stream_path else 2 if tc_path else 1) * K,
             "clocks": clk.summary(),
             "e2e": {"value": round(e2e_val, 1), "unit": "tok/s", "steps": n_e2e,
                     "h2d_bytes_per_step": B * H * 2 + B * TOPK * 8 + B * TOPK * 2,
@@ -866,6 +1033,9 @@ def main():
                     "path": "Gemma4TextExpertsNVFP4.forward eager, pinned host in/out, sync per step"},
             "roofline": roof,
             "prefill": prefill,
+            "decode_batch_sweep": sweep,
+            "quantizer": quantizer,
+            "ep": ep,
         }
         if world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline(args.cpu_seconds, B)

@@ -366,6 +366,34 @@ AEOQ_API int aeoq_moe_nvfp4_decode_tc(const void* hidden, const void* top_k_inde
                                       void* stream);
 
 /* ------------------------------------------------------------------------
+ * One-token NVFP4 MoE expert forward streamed through ONE cooperative
+ * launch (the default one-token path). Same math, rounding points and
+ * arguments as aeoq_moe_nvfp4_decode (replaces the same reference function,
+ * modeling_nvfp4.py:132-186) plus an error word. Work is split across the
+ * SMs by bytes; each CTA requests every weight, scale and down row it needs
+ * from HBM at entry (about 181 KB of shared memory per CTA at Gemma-4
+ * shapes) and computes as the copies land; one grid barrier separates the
+ * gate/up and down halves. The down scales are bulk-copied too, so the
+ * weight scales must be 16-byte aligned.
+ * Workspace contract: aeoq_moe_nvfp4_decode_stream_workspace_size() bytes,
+ * 256-aligned, whose first 256 bytes are zero before the first call; each
+ * call leaves them zero again, so one workspace serves successive calls on
+ * one stream (calls that overlap on the device must not share it). A bounded
+ * wait that times out records a nonzero code in *err_word.
+ * aeoq_moe_nvfp4_decode_stream_supported(): hidden % 256 == 0, inter % 64
+ * == 0, inter <= 1024, top_k <= 16, shared-memory budget.
+ * ------------------------------------------------------------------------ */
+AEOQ_API int aeoq_moe_nvfp4_decode_stream_supported(int64_t top_k, int64_t hidden, int64_t inter);
+AEOQ_API size_t aeoq_moe_nvfp4_decode_stream_workspace_size(int64_t top_k, int64_t hidden, int64_t inter);
+AEOQ_API int aeoq_moe_nvfp4_decode_stream(const void* hidden, const void* top_k_index, int idx_dtype,
+                                          const void* top_k_weights, int64_t top_k, const uint8_t* gate_up,
+                                          const uint8_t* gate_up_sf, const void* gate_up_ts, int gate_up_ts_dtype,
+                                          const uint8_t* down, const uint8_t* down_sf, const void* down_ts,
+                                          int down_ts_dtype, int64_t num_experts, int64_t hidden_dim,
+                                          int64_t inter_dim, void* out, void* workspace, size_t workspace_bytes,
+                                          int* err_word, void* stream);
+
+/* ------------------------------------------------------------------------
  * Allocation-free one-token decode. No counterpart in the reference: it
  * exists for callers that cannot allocate device memory where they run the
  * expert forward (a serving runtime that pre-reserves all device memory, a
