@@ -32,11 +32,21 @@ def router_supported(router) -> bool:
     return (H % 8 == 0 and 2 * E + 128 <= H <= 6144 and E % 8 == 0 and E <= 256 and 1 <= k <= min(E, 32))
 
 
+# Above this many tokens HF's eager forward is faster: its 2816 -> 128
+# projection is a cuBLAS GEMM, while the fused kernel runs it on CUDA cores
+# (measured with ``bench.py --workload router``).
+FUSED_MAX_TOKENS = 128
+
+
 class Gemma4TextRouterB200(Gemma4TextRouter):
-    """Gemma4TextRouter with a fused CUDA forward (bf16 only)."""
+    """Gemma4TextRouter with a fused CUDA forward (bf16 only) for up to
+    ``FUSED_MAX_TOKENS`` tokens; larger batches (prefill) take HF's eager
+    forward, which is faster there."""
 
     def forward(self, hidden_states: torch.Tensor):
         x = hidden_states
+        if x.dim() == 2 and x.shape[0] > FUSED_MAX_TOKENS:
+            return Gemma4TextRouter.forward(self, x)
         if x.dim() != 2:
             raise ValueError(f"router expects (tokens, hidden), got shape {tuple(x.shape)}")
         w = self.proj.weight

@@ -634,13 +634,18 @@ def main_router(args, local):
     with torch.no_grad():
         r.proj.weight.normal_(0.0, 0.5)
     swap_routers(torch.nn.Sequential(r))
+    from aeo_quant_b200.bridges.gemma4 import router as R
     out = {}
     with torch.no_grad():
-        for T in (1, args.prompt):
+        for T in (1, 16, 64, 128, 256, 512, args.prompt):
             x = torch.randn(T, H, device=dev).to(torch.bfloat16)
-            out[f"fused_T{T}_us"] = round(_graph_time_us(torch, dev, lambda: r(x), 200 if T == 1 else 50), 2)
+            n = 200 if T <= 64 else 50
+            old, R.FUSED_MAX_TOKENS = R.FUSED_MAX_TOKENS, 1 << 30     # the fused kernel at every size
+            out[f"fused_kernel_T{T}_us"] = round(_graph_time_us(torch, dev, lambda: r(x), n), 2)
+            R.FUSED_MAX_TOKENS = old
+            out[f"module_T{T}_us"] = round(_graph_time_us(torch, dev, lambda: r(x), n), 2)
             out[f"hf_eager_T{T}_us"] = round(
-                _graph_time_us(torch, dev, lambda: Gemma4TextRouter.forward(r, x), 200 if T == 1 else 50), 2)
+                _graph_time_us(torch, dev, lambda: Gemma4TextRouter.forward(r, x), n), 2)
     print(json.dumps({"metric": "Gemma-4 router latency", "unit": "us", "higher_is_better": False,
                       "config": {"workload": "router alone, H 2816, 128 experts, top-8, bf16"}, **out}), flush=True)
 

@@ -23,7 +23,9 @@ def fused(r):
 @pytest.mark.parametrize("H,E,k,T", [(2816, 128, 8, 1), (2816, 128, 8, 7), (2816, 128, 8, 8), (2816, 128, 8, 9),
                                      (2816, 128, 8, 64), (2816, 128, 8, 300), (512, 16, 4, 5), (1024, 256, 32, 17),
                                      (6144, 64, 8, 3), (2816, 128, 8, 33)])
-def test_router_vs_oracle(H, E, k, T):
+def test_router_vs_oracle(H, E, k, T, monkeypatch):
+    from aeo_quant_b200.bridges.gemma4 import router as R
+    monkeypatch.setattr(R, "FUSED_MAX_TOKENS", 1 << 30)   # the kernel at every token count
     r = hf_router(H, E, k, 11, 0.5).cuda()
     f = fused(r)
     x = (torch.randn(T, H, generator=torch.Generator().manual_seed(T)) * 2.0).to(torch.bfloat16).cuda()
@@ -69,3 +71,15 @@ def test_router_rejects_unsupported_shapes():
         f(x)
     with pytest.raises(ValueError, match="bfloat16"):
         f(x.float())
+
+
+def test_router_large_batches_take_hf_forward():
+    """Above FUSED_MAX_TOKENS the swapped router runs HF's eager forward
+    (faster there): identical outputs to the unswapped module."""
+    from aeo_quant_b200.bridges.gemma4 import router as R
+    r = hf_router(2816, 128, 8, 15, 0.5).cuda()
+    f = fused(r)
+    x = torch.randn(R.FUSED_MAX_TOKENS + 1, 2816, device="cuda").to(torch.bfloat16)
+    with torch.no_grad():
+        for u, v in zip(f(x), r(x)):
+            assert torch.equal(u, v)
