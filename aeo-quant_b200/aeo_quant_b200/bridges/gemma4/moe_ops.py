@@ -111,7 +111,10 @@ def pick_tile_n(n_pairs: int, num_experts: int) -> int:
     for bn in (8, 16, 32, 64):
         if avg <= bn:
             return bn
-    return 128   # the persistent kernel (accumulator double-buffered in TMEM)
+    # the persistent kernel (accumulator double-buffered in TMEM); an MMA
+    # costs about the same up to 256 tokens wide, so wide tiles pay once the
+    # experts hold more than a 128-row tile on average
+    return 128 if avg < 160 else 224
 
 
 class _Route:

@@ -33,7 +33,7 @@ int pick_tile_n(int64_t pairs, int64_t experts) {
   const int64_t avg = std::max<int64_t>(1, pairs / std::max<int64_t>(1, std::min(experts, pairs)));
   for (int bn : {8, 16, 32, 64})
     if (avg <= bn) return bn;
-  return 128;
+  return avg < 160 ? 128 : 224;
 }
 
 struct Carver {

@@ -1038,8 +1038,9 @@ extern "C" int aeoq_nvfp4_gemm_grouped(const uint8_t* b, const uint8_t* b_sf, in
   AEOQ_REQUIRE(N % 128 == 0 && K % 64 == 0 && K > 0 && (K / 2) % 16 == 0, AEOQ_ERR_INVALID,
                "nvfp4_gemm_grouped: N %% 128 == 0 and K %% 64 == 0 required");
   AEOQ_REQUIRE(epi >= 0 && epi <= 2, AEOQ_ERR_INVALID, "nvfp4_gemm_grouped: bad epilogue %d", epi);
-  AEOQ_REQUIRE(tile_n == 8 || tile_n == 16 || tile_n == 32 || tile_n == 64 || tile_n == 128 || tile_n == 256,
-               AEOQ_ERR_INVALID, "nvfp4_gemm_grouped: tile_n must be 8..256, a power of two");
+  AEOQ_REQUIRE(tile_n == 8 || tile_n == 16 || tile_n == 32 || tile_n == 64 || tile_n == 128 || tile_n == 224 ||
+                   tile_n == 256,
+               AEOQ_ERR_INVALID, "nvfp4_gemm_grouped: tile_n must be 224 or a power of two in [8, 256]");
   AEOQ_REQUIRE(num_experts >= 1 && num_experts <= 1024, AEOQ_ERR_INVALID, "nvfp4_gemm_grouped: bad expert count");
   if (max_rows <= 0) return AEOQ_OK;
   AEOQ_REQUIRE(b && b_sf && grp_off && tile_off && w && w_sf && w_ts && c && err_word, AEOQ_ERR_INVALID,
@@ -1069,7 +1070,8 @@ extern "C" int aeoq_nvfp4_gemm_grouped(const uint8_t* b, const uint8_t* b_sf, in
   const int64_t max_tiles = (max_rows + tile_n - 1) / tile_n + num_experts;
   const unsigned gx = (unsigned)(epi == kEpiGeglu ? (N / 2) / 64 : N / 128);
   dim3 grid(gx, (unsigned)max_tiles, 1);
-  if (tile_n == 128) return tc_gemm_persistent<false>(tile_n, w, num_experts * N, b, p, grid, (cudaStream_t)stream);
+  if (tile_n == 128 || tile_n == 224)
+    return tc_gemm_persistent<false>(tile_n, w, num_experts * N, b, p, grid, (cudaStream_t)stream);
   return tc_gemm_dispatch(tile_n, w, num_experts * N, b, p, grid, (cudaStream_t)stream);
 }
 
@@ -1117,8 +1119,9 @@ extern "C" int aeoq_fp8_gemm_grouped(const uint8_t* b, const float* sa_rows, int
   AEOQ_REQUIRE(N % 128 == 0 && K % 32 == 0 && K > 0, AEOQ_ERR_INVALID,
                "fp8_gemm_grouped: N %% 128 == 0 and K %% 32 == 0 required");
   AEOQ_REQUIRE(epi >= 0 && epi <= 2, AEOQ_ERR_INVALID, "fp8_gemm_grouped: bad epilogue %d", epi);
-  AEOQ_REQUIRE(tile_n == 8 || tile_n == 16 || tile_n == 32 || tile_n == 64 || tile_n == 128 || tile_n == 256,
-               AEOQ_ERR_INVALID, "fp8_gemm_grouped: tile_n must be 8..256, a power of two");
+  AEOQ_REQUIRE(tile_n == 8 || tile_n == 16 || tile_n == 32 || tile_n == 64 || tile_n == 128 || tile_n == 224 ||
+                   tile_n == 256,
+               AEOQ_ERR_INVALID, "fp8_gemm_grouped: tile_n must be 224 or a power of two in [8, 256]");
   AEOQ_REQUIRE(num_experts >= 1 && num_experts <= 1024, AEOQ_ERR_INVALID, "fp8_gemm_grouped: bad expert count");
   if (max_rows <= 0) return AEOQ_OK;
   AEOQ_REQUIRE(b && sa_rows && grp_off && tile_off && w && sb_rows && c && err_word, AEOQ_ERR_INVALID,
@@ -1145,6 +1148,7 @@ extern "C" int aeoq_fp8_gemm_grouped(const uint8_t* b, const float* sa_rows, int
   const int64_t max_tiles = (max_rows + tile_n - 1) / tile_n + num_experts;
   const unsigned gx = (unsigned)(epi == kEpiGeglu ? (N / 2) / 64 : N / 128);
   dim3 grid(gx, (unsigned)max_tiles, 1);
-  if (tile_n == 128) return tc_gemm_persistent<true>(tile_n, w, num_experts * N, b, p, grid, (cudaStream_t)stream);
+  if (tile_n == 128 || tile_n == 224)
+    return tc_gemm_persistent<true>(tile_n, w, num_experts * N, b, p, grid, (cudaStream_t)stream);
   return tc_gemm_dispatch_kind<true>(tile_n, w, num_experts * N, b, p, grid, (cudaStream_t)stream);
 }
