@@ -10,33 +10,34 @@
 // At one token the layer is a pure stream of the k experts' packed weights
 // (26.8 MB for Gemma-4-26B-A4B), so the kernel is laid out for HBM:
 //
-// * Work split by bytes. CTA c (one per SM) owns a contiguous range of the
-//   k*I gate/up row pairs and a block of `rows` down rows (a multiple of 4,
-//   so that its 44-byte scale rows start on 16-byte boundaries) for all k
-//   experts. The host plan balances the CTAs' total bytes: CTAs without down
-//   rows take more pairs.
-// * Everything the CTA will ever read from HBM is requested at entry: every
-//   warp loads the expert ids itself and issues its share of the bulk copies
-//   (cp.async.bulk, L2 evict-first) of the CTA's gate rows, up rows, scale
-//   rows, down rows and down scale rows into shared memory (about 181 KB), in
-//   consumption order, completing on one mbarrier per group of kGroup pairs
-//   and one per expert slot for the down block.
-// * Meanwhile the hidden vector is staged in shared memory and quantized
-//   (global amax, bf16 tensor scale, e4m3 block scales, E2M1 codes) into
-//   exact fp16 operands.
-// * gate/up dot products run per pair group as soon as its barrier flips,
-//   so compute overlaps the stream; h = bf16(bf16(gelu(g)) * u) goes to the
-//   workspace.
+// * Work split by bytes into few, large copies. HBM serves a CTA's bulk
+//   copies at full rate when they are large; many small copies from
+//   scattered addresses (a few KB each) run at a third of it. So CTA c
+//   (one per SM) owns ONE down block: `rows` consecutive down rows (a
+//   multiple of 4, so its 44-byte scale rows start on 16-byte boundaries)
+//   of ONE expert slot (two copies, ~63 KB), and a contiguous range of the
+//   k*I gate/up row pairs (gate rows, up rows and their scales: four copies
+//   per slot segment, split in groups of kGroup pairs for early compute).
+//   The host plan balances the CTAs' bytes.
+// * Everything the CTA will read from HBM is requested at entry (L2
+//   evict-first): every warp loads the expert ids itself and issues its
+//   share of the copies. Meanwhile the hidden vector is staged in shared
+//   memory and quantized (global amax, bf16 tensor scale, e4m3 block scales,
+//   E2M1 codes) into exact fp16 operands.
+// * gate/up dot products run per pair group as soon as its barrier flips;
+//   h = bf16(bf16(gelu(g)) * u) goes to the workspace.
 // * One grid barrier (an arrival counter with a bounded spin; the launch is
 //   cooperative, so every CTA is resident); the grid's max |h| is one word
-//   updated with atomicMax before the arrival. Then each CTA reads the k
-//   GeGLU rows (its down rows cover every expert) into shared memory in one
-//   coalesced pass, quantizes them with the shared tensor scale and runs its
-//   down dot products from shared memory (landed long before).
-// * Each output row sums its k weighted products bf16(bf16(a*d_j) * w_j) in
-//   f64 and rounds once to f32 then bf16, as the reference's sum does.
-// * The last CTA to leave zeroes the counters, so a zeroed workspace stays
-//   valid for every call on one stream.
+//   updated with atomicMax before the arrival.
+// * Each CTA then reads its slot's GeGLU row (I values), quantizes it with
+//   the shared tensor scale and runs its down dot products from shared
+//   memory. The weighted products bf16(bf16(a*d_j) * w_j) of the k slots
+//   meet in an f64 accumulator per output row (atomic adds: a sum of k bf16
+//   values in f64 is exact, so the order does not matter); the CTA that
+//   brings a row block's arrival count to k rounds it once to f32 then bf16,
+//   as the reference's sum does, and clears the accumulator and the count.
+// * The last CTA to leave zeroes the grid counters, so a zeroed workspace
+//   stays valid for every call on one stream.
 //
 // An expert id outside [0, E) reads no weights and contributes zeros.
 #include "common.cuh"
@@ -49,16 +50,17 @@ constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxK = 16;
 constexpr int kMaxCtas = 160;
-constexpr int kGroup = 8;             // gate/up pairs per arrival barrier
-constexpr int kMaxGroups = 12;
-constexpr int kMaxRows = 32;          // down rows per CTA
+constexpr int kGroup = 20;            // gate/up pairs per arrival barrier
+constexpr int kMaxGroups = 8;
+constexpr int kMaxRows = 512;         // down rows per CTA
 constexpr int kMaxChunks = 4;         // 32-value chunks per lane of a hidden row (H <= 4096)
 constexpr size_t kSmemCap = 227 * 1024;
 
 // Host-side plan (passed by value).
 struct Plan {
   int H, I, k, G;
-  int rows;                    // down rows per CTA (multiple of 4)
+  int rows;                    // down rows per block (multiple of 4)
+  int nb;                      // down blocks per expert slot; CTA c < k*nb owns slot c/nb, block c%nb
   int max_pairs;               // largest pair range of any CTA
   size_t bytes;                // dynamic shared memory
   int pair0[kMaxCtas + 1];     // CTA c owns pairs [pair0[c], pair0[c+1])
@@ -74,6 +76,8 @@ struct Args {
   __nv_bfloat16* out;
   __nv_bfloat16* h;      // k*I bf16 GeGLU rows
   uint32_t* sync;        // [0] arrivals, [1] departures, [2] max |h| key over the grid
+  uint32_t* cnt;         // [nb] slots folded into each down row block
+  double* acc;           // [H] f64 sums of the weighted down products
   int* err;              // error word (bounded waits)
 };
 
@@ -91,14 +95,22 @@ __host__ __device__ inline Carve carve(int H, int I, int k, int np, int nr) {
   c.up = o;   o = a16(o + (size_t)np * rb);
   c.gsf = o;  o = a16(o + (size_t)np * sb);
   c.usf = o;  o = a16(o + (size_t)np * sb);
-  c.dn = o;   o = a16(o + (size_t)k * nr * rb2);
-  c.dsf = o;  o = a16(o + (size_t)k * nr * sb2);
+  c.dn = o;   o = a16(o + (size_t)nr * rb2);
+  c.dsf = o;  o = a16(o + (size_t)nr * sb2);
   c.hid = o;  o = a16(o + (size_t)H * 2);
   c.act = o;  o = a16(o + (size_t)(H / 16) * 8 * sizeof(__half2));
   c.asa = o;  o = a16(o + (size_t)(H / 16) * sizeof(float));
-  c.hrow = o; o = a16(o + (size_t)k * I * 2);
+  c.hrow = o; o = a16(o + (size_t)I * 2);
   c.end = o;
   return c;
+}
+
+// Down rows of CTA c (0 when it owns no down block).
+__host__ __device__ inline int down_rows(const Plan& p, int c, int* slot, int* r0) {
+  if (c >= p.k * p.nb) { *slot = 0; *r0 = 0; return 0; }
+  *slot = c / p.nb;
+  *r0 = (c % p.nb) * p.rows;
+  return min(p.rows, p.H - *r0);
 }
 
 static bool make_plan(int64_t k, int64_t H, int64_t I, int G, Plan& p) {
@@ -106,12 +118,16 @@ static bool make_plan(int64_t k, int64_t H, int64_t I, int G, Plan& p) {
   if (H <= 0 || I <= 0 || H % 256 != 0 || I % 64 != 0) return false;
   if (H / 32 > 32 * kMaxChunks || I / 32 > 32) return false;
   p.H = (int)H; p.I = (int)I; p.k = (int)k; p.G = G;
-  p.rows = (int)(((H + G - 1) / G + 3) / 4 * 4);
-  if (p.rows > kMaxRows) return false;
+  // smallest multiple of 4 rows whose k * ceil(H / rows) blocks fit the grid
+  int rows = (int)((H * k + G - 1) / G + 3) / 4 * 4;
+  while (rows <= kMaxRows && k * ((H + rows - 1) / rows) > G) rows += 4;
+  if (rows > kMaxRows) return false;
+  p.rows = rows;
+  p.nb = (int)((H + rows - 1) / rows);
   const double pair_b = 2.0 * (H / 2 + H / 16);
-  const double row_b = (double)k * (I / 2 + I / 16);
+  const double row_b = (double)(I / 2 + I / 16);
   const int64_t pairs = k * I;
-  const double total = pairs * pair_b + H * row_b;
+  const double total = pairs * pair_b + (double)k * H * row_b;
   const double target = total / G;
   double down_before = 0.0;
   for (int c = 0; c <= G; ++c) {
@@ -121,9 +137,8 @@ static bool make_plan(int64_t k, int64_t H, int64_t I, int G, Plan& p) {
     if (c > 0 && q < p.pair0[c - 1]) q = p.pair0[c - 1];
     p.pair0[c] = (int)q;
     if (c < G) {
-      const int64_t r0 = (int64_t)c * p.rows;
-      const int64_t nr = r0 < H ? (H - r0 < p.rows ? H - r0 : p.rows) : 0;
-      down_before += nr * row_b;
+      int j, r0;
+      down_before += down_rows(p, c, &j, &r0) * row_b;
     }
   }
   size_t need = 0;
@@ -131,8 +146,8 @@ static bool make_plan(int64_t k, int64_t H, int64_t I, int G, Plan& p) {
   for (int c = 0; c < G; ++c) {
     const int np = p.pair0[c + 1] - p.pair0[c];
     p.max_pairs = np > p.max_pairs ? np : p.max_pairs;
-    const int64_t r0 = (int64_t)c * p.rows;
-    const int nr = (int)(r0 < H ? (H - r0 < p.rows ? H - r0 : p.rows) : 0);
+    int j, r0;
+    const int nr = down_rows(p, c, &j, &r0);
     const size_t b = carve(p.H, p.I, p.k, np, nr).end;
     need = b > need ? b : need;
   }
@@ -188,32 +203,32 @@ __device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32
 __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const Args a, const Plan pl) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t bars[kMaxGroups + kMaxK];
+  __shared__ uint64_t bars[kMaxGroups + 1];
   __shared__ int64_t ids_w[kWarps][kMaxK];
   __shared__ uint32_t red[kWarps];
-  __shared__ float prod[kMaxK][kMaxRows];
   __shared__ float topw_s[kMaxK];
   __shared__ uint32_t hmax_s;
+  __shared__ int last_s;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int H = pl.H, I = pl.I, k = pl.k;
   const size_t rb = H / 2, sb = H / 16, rb2 = I / 2, sb2 = I / 16;
   const int p0 = pl.pair0[blockIdx.x], np = pl.pair0[blockIdx.x + 1] - p0;
   const int ngroups = (np + kGroup - 1) / kGroup;
-  const int r0 = (int)blockIdx.x * pl.rows;
-  const int nr = r0 < H ? min(pl.rows, H - r0) : 0;
+  int dslot, r0;
+  const int nr = down_rows(pl, (int)blockIdx.x, &dslot, &r0);
   const Carve cv = carve(H, I, k, np, nr);
-  uint64_t* bdown = &bars[kMaxGroups];   // one per expert slot
+  uint64_t* bdown = &bars[kMaxGroups];
 
   // ---- every warp: its barriers, the expert ids, its share of the copies ----
-  // Warp w owns pair groups g = w, w + 16, ... and the down block of slot
-  // j = w. Every warp loads the k ids itself (one L2 line), so no warp waits
+  // Warp w owns pair groups g = w, w + 16, ...; the last warp owns the down
+  // block. Every warp loads the k ids itself (one L2 line), so no warp waits
   // for another before issuing. The copies carry an L2 evict-first hint: the
   // streamed weights are read once and must not push the kernel's code and
   // small operands out of L2.
   if (lane == 0) {
     for (int g = warp; g < ngroups; g += kWarps) sm100::mbar_init(&bars[g], 1);
-    if (warp < k) sm100::mbar_init(&bdown[warp], 1);
+    if (warp == kWarps - 1) sm100::mbar_init(bdown, 1);
     sm100::fence_barrier_init();
   }
   if (lane < k) {
@@ -244,17 +259,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const Args a
         i += len;
       }
     }
-    if (warp < k) {
-      const int j = warp;
-      const int64_t e = ids_w[warp][j];
-      sm100::mbar_arrive_expect_tx(&bdown[j], (uint32_t)(nr * (rb2 + sb2)));
+    if (warp == kWarps - 1) {
+      const int64_t e = ids_w[warp][dslot];
+      sm100::mbar_arrive_expect_tx(bdown, (uint32_t)(nr * (rb2 + sb2)));
       if (e >= 0 && nr > 0) {
-        bulk_g2s_hint(smem + cv.dn + (size_t)j * nr * rb2, a.dw + ((size_t)e * H + r0) * rb2, (uint32_t)(nr * rb2),
-                      &bdown[j], pol);
-        bulk_g2s_hint(smem + cv.dsf + (size_t)j * nr * sb2, a.dw_sf + ((size_t)e * H + r0) * sb2,
-                      (uint32_t)(nr * sb2), &bdown[j], pol);
+        bulk_g2s_hint(smem + cv.dn, a.dw + ((size_t)e * H + r0) * rb2, (uint32_t)(nr * rb2), bdown, pol);
+        bulk_g2s_hint(smem + cv.dsf, a.dw_sf + ((size_t)e * H + r0) * sb2, (uint32_t)(nr * sb2), bdown, pol);
       } else if (nr > 0) {
-        complete_tx(&bdown[j], (uint32_t)(nr * (rb2 + sb2)));
+        complete_tx(bdown, (uint32_t)(nr * (rb2 + sb2)));
       }
     }
   }
@@ -365,47 +377,54 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const Args a
   }
   __syncthreads();
 
-  // ---- the k GeGLU rows into shared memory, one coalesced read per CTA -------
-  __nv_bfloat16* hrow_s = reinterpret_cast<__nv_bfloat16*>(smem + cv.hrow);
-  for (int i = tid; i < k * I / 8; i += kThreads)
-    reinterpret_cast<uint4*>(hrow_s)[i] = __ldcg(reinterpret_cast<const uint4*>(a.h) + i);
-  const float hts = nvfp4_tensor_scale<AEOQ_BF16>(In<AEOQ_BF16>::key_to_f(hmax_s));
-  const float alpha_d = hts * d_ts;
-  __syncthreads();
-
-  // ---- down GEMV: warps own one expert slot each -----------------------------
-  const int wpj = kWarps / k;            // warps per slot
-  const int nchunk2 = I / 32;            // <= 32: one chunk per lane
-  if (warp < wpj * k && nr > 0) {
-    const int j = warp / wpj;
-    const bool ok_dn = sm100::mbar_wait(&bdown[j], 0, a.err, 33);
-    const bool valid = ok_dn && ids_w[0][j] >= 0;
-    const float wj = topw_s[j];
+  // ---- this CTA's down block: its slot's GeGLU row, dot products ------------
+  if (nr > 0) {
+    __nv_bfloat16* hrow_s = reinterpret_cast<__nv_bfloat16*>(smem + cv.hrow);
+    for (int i = tid; i < I / 8; i += kThreads)
+      reinterpret_cast<uint4*>(hrow_s)[i] = __ldcg(reinterpret_cast<const uint4*>(a.h + (size_t)dslot * I) + i);
+    const float hts = nvfp4_tensor_scale<AEOQ_BF16>(In<AEOQ_BF16>::key_to_f(hmax_s));
+    const float alpha_d = hts * d_ts;
+    __syncthreads();
+    const bool ok_dn = sm100::mbar_wait(bdown, 0, a.err, 33);
+    const bool valid = ok_dn && ids_w[0][dslot] >= 0;
+    const float wj = topw_s[dslot];
+    const int nchunk2 = I / 32;            // <= 32: one chunk per lane
     __half2 hv[16];
     float hs[2] = {0.f, 0.f};
     if (lane < nchunk2) {
-      const __nv_bfloat16* src = hrow_s + (size_t)j * I + 32 * lane;
-      quant16_smem(src, hts, hv, &hs[0]);
-      quant16_smem(src + 16, hts, hv + 8, &hs[1]);
+      quant16_smem(hrow_s + 32 * lane, hts, hv, &hs[0]);
+      quant16_smem(hrow_s + 32 * lane + 16, hts, hv + 8, &hs[1]);
     }
-    const uint8_t* dn_s = smem + cv.dn + (size_t)j * nr * rb2;
-    const uint8_t* dsf_s = smem + cv.dsf + (size_t)j * nr * sb2;
-    for (int r = warp % wpj; r < nr; r += wpj) {
-      float acc = 0.f;
-      if (valid && lane < nchunk2)
-        acc = chunk_dot(hv, hs, *reinterpret_cast<const uint4*>(dn_s + r * rb2 + 16 * lane),
-                        *reinterpret_cast<const uint16_t*>(dsf_s + r * sb2 + 2 * lane), acc);
-      acc = warp_sum(acc);
-      if (lane == 0) prod[j][r] = valid ? bf16r(bf16r(acc * alpha_d) * wj) : 0.0f;
+    const uint8_t* dn_s = smem + cv.dn;
+    const uint8_t* dsf_s = smem + cv.dsf;
+    if (valid) {
+      for (int r = warp; r < nr; r += kWarps) {
+        float acc = 0.f;
+        if (lane < nchunk2)
+          acc = chunk_dot(hv, hs, *reinterpret_cast<const uint4*>(dn_s + r * rb2 + 16 * lane),
+                          *reinterpret_cast<const uint16_t*>(dsf_s + r * sb2 + 2 * lane), acc);
+        acc = warp_sum(acc);
+        if (lane == 0) atomicAdd(a.acc + r0 + r, (double)bf16r(bf16r(acc * alpha_d) * wj));
+      }
     }
-  } else if (warp < k) {
-    sm100::mbar_wait(&bdown[warp], 0, a.err, 33);   // nr == 0: nothing in flight, the phase is complete
-  }
-  __syncthreads();
-  if (tid < nr) {
-    double s = 0.0;
-    for (int j = 0; j < k; ++j) s += (double)prod[j][tid];
-    a.out[r0 + tid] = __float2bfloat16_rn((float)s);
+    // arrival on the row block; the k-th arrival rounds and clears it
+    __threadfence();   // this thread's adds ordered before the CTA's arrival
+    __syncthreads();
+    if (tid == 0) {
+      const uint32_t old = atomicAdd(a.cnt + r0 / pl.rows, 1u);
+      last_s = (old == (uint32_t)k - 1);
+      __threadfence();   // every arrival's adds visible to the reads below
+    }
+    __syncthreads();
+    if (last_s) {
+      for (int r = tid; r < nr; r += kThreads) {
+        a.out[r0 + r] = __float2bfloat16_rn((float)__ldcg(a.acc + r0 + r));
+        a.acc[r0 + r] = 0.0;
+      }
+      if (tid == 0) a.cnt[r0 / pl.rows] = 0;
+    }
+  } else {
+    sm100::mbar_wait(bdown, 0, a.err, 33);   // nothing in flight; the phase is complete
   }
 
   // ---- departure: the last CTA out resets the counters ----------------------
@@ -434,10 +453,15 @@ extern "C" int aeoq_moe_nvfp4_decode_stream_supported(int64_t top_k, int64_t hid
   return stream_plan(top_k, hidden, inter, p) ? 1 : 0;
 }
 
-// Workspace: [counters 256 B][k*I bf16 GeGLU rows, 256-aligned].
+static size_t al256(size_t v) { return (v + 255) / 256 * 256; }
+
+// Workspace: [grid counters 256 B][row-block counters nb u32][f64 row sums H]
+// [k*I bf16 GeGLU rows], each part 256-aligned. Everything but the GeGLU
+// rows must be zero before the first call; every call leaves it zero.
 extern "C" size_t aeoq_moe_nvfp4_decode_stream_workspace_size(int64_t top_k, int64_t hidden, int64_t inter) {
-  (void)hidden;
-  return 256 + ((size_t)(top_k * inter) * 2 + 255) / 256 * 256;
+  dst::Plan p;
+  if (!stream_plan(top_k, hidden, inter, p)) return 0;
+  return 256 + al256((size_t)p.nb * 4) + al256((size_t)hidden * 8) + al256((size_t)(top_k * inter) * 2);
 }
 
 extern "C" int aeoq_moe_nvfp4_decode_stream(const void* hidden, const void* top_k_index, int idx_dtype,
@@ -461,7 +485,7 @@ extern "C" int aeoq_moe_nvfp4_decode_stream(const void* hidden, const void* top_
                AEOQ_ERR_INVALID, "moe_decode_stream: hidden, weights and scales must be 16-byte aligned");
   const size_t need = aeoq_moe_nvfp4_decode_stream_workspace_size(top_k, hidden_dim, inter_dim);
   AEOQ_REQUIRE(workspace && workspace_bytes >= need && (uintptr_t)workspace % 256 == 0, AEOQ_ERR_WORKSPACE,
-               "moe_decode_stream: workspace of %zu bytes (256-aligned, first 256 B zero) needed, %zu given", need,
+               "moe_decode_stream: workspace of %zu bytes (256-aligned, zeroed before first use) needed, %zu given", need,
                workspace_bytes);
   char* w = reinterpret_cast<char*>(workspace);
   dst::Args a{};
@@ -473,7 +497,9 @@ extern "C" int aeoq_moe_nvfp4_decode_stream(const void* hidden, const void* top_
   a.E = num_experts;
   a.out = reinterpret_cast<__nv_bfloat16*>(out);
   a.sync = reinterpret_cast<uint32_t*>(w);
-  a.h = reinterpret_cast<__nv_bfloat16*>(w + 256);
+  a.cnt = reinterpret_cast<uint32_t*>(w + 256);
+  a.acc = reinterpret_cast<double*>(w + 256 + al256((size_t)pl.nb * 4));
+  a.h = reinterpret_cast<__nv_bfloat16*>(w + 256 + al256((size_t)pl.nb * 4) + al256((size_t)hidden_dim * 8));
   a.err = err_word;
   {
     const int rc = func_smem_attr((const void*)dst::decode_stream_kernel, pl.bytes, -1, "moe_decode_stream");
