@@ -138,7 +138,8 @@ struct TileInfo {
 };
 
 template <int BN>
-__device__ __forceinline__ TileInfo resolve_tile_at(const TcParams& p, int y_tile, int z_slot) {
+__device__ __forceinline__ TileInfo resolve_tile_at(const TcParams& p, int y_tile, int z_slot,
+                                                    const int* tile_off = nullptr, const int* grp_off = nullptr) {
   TileInfo t{};
   if (p.mode == 0) {
     const int64_t s = z_slot;
@@ -152,23 +153,25 @@ __device__ __forceinline__ TileInfo resolve_tile_at(const TcParams& p, int y_til
     t.active = t.n_valid > 0;
   } else {
     const int y = y_tile;
+    const int* toff = tile_off ? tile_off : p.tile_off;
+    const int* goff = grp_off ? grp_off : p.grp_off;
     const int E = (int)p.num_experts;
-    if (y >= p.tile_off[E]) {
+    if (y >= toff[E]) {
       t.active = false;
       return t;
     }
     int lo = 0, hi = E;   // largest e with tile_off[e] <= y
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
-      if (p.tile_off[mid] <= y) lo = mid; else hi = mid;
+      if (toff[mid] <= y) lo = mid; else hi = mid;
     }
-    while (lo < E - 1 && p.tile_off[lo + 1] <= y) ++lo;
+    while (lo < E - 1 && toff[lo + 1] <= y) ++lo;
     t.expert = lo;
     t.tile = y;
-    const int64_t tb = (int64_t)(y - p.tile_off[lo]) * BN;
-    t.b_row0 = p.grp_off[lo] + tb;
+    const int64_t tb = (int64_t)(y - toff[lo]) * BN;
+    t.b_row0 = goff[lo] + tb;
     t.c_row0 = t.b_row0;
-    t.n_valid = (int)min((int64_t)BN, (int64_t)(p.grp_off[lo + 1] - p.grp_off[lo]) - tb);
+    t.n_valid = (int)min((int64_t)BN, (int64_t)(goff[lo + 1] - goff[lo]) - tb);
     t.slot = 0;
     t.active = t.n_valid > 0;
   }
@@ -510,6 +513,7 @@ int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int64_t row_bytes, 
 //   warp 1          TMEM owner + MMA issuer
 //   warps 4 .. 19   epilogue (four per TMEM lane quadrant)
 constexpr int kPEpiWarps = 16;
+constexpr int kPMaxExperts = 256;   // grouped offsets held in shared memory up to this many experts
 constexpr int kPThreads = 128 + 32 * kPEpiWarps;
 constexpr int kPProducers = 3;
 
@@ -526,6 +530,10 @@ struct PLayout {
     uint64_t full[kTcMaxStages], empty[kTcMaxStages], acc_full[2], acc_empty[2];
     uint32_t tmem_base;
     float colscale[256];
+    // grouped mode: the expert tile and row offsets, so every role resolves
+    // a tile from shared memory instead of a chain of dependent L2 loads
+    int tile_off[kPMaxExperts + 1];
+    int grp_off[kPMaxExperts + 1];
   };
   static constexpr size_t kFixed = 1024 + kXchg + sizeof(Smem) + 64;
   static constexpr int kStages =
@@ -561,13 +569,24 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
   auto stSFB = [&](int s) { return stage0 + s * L::kStage + L::kA + L::kB + L::kSfa; };
 
   // the tile schedule: tile t -> (weight tile t % tiles_x, token tile, slot)
+  const bool offs_smem = p.mode == 1 && p.num_experts <= kPMaxExperts;
+  if (offs_smem) {
+    for (int i = tid; i <= (int)p.num_experts; i += kPThreads) {
+      sh->tile_off[i] = p.tile_off[i];
+      sh->grp_off[i] = p.grp_off[i];
+    }
+    __syncthreads();
+  }
+  const int* toff = offs_smem ? sh->tile_off : nullptr;
+  const int* goff = offs_smem ? sh->grp_off : nullptr;
   const int tx = p.tiles_x;
-  const int ty = p.mode == 1 ? p.tile_off[p.num_experts] : p.tiles_y;
+  const int ty = p.mode == 1 ? (offs_smem ? sh->tile_off[p.num_experts] : p.tile_off[p.num_experts]) : p.tiles_y;
   const int64_t total = (int64_t)tx * ty * (p.mode == 1 ? 1 : p.tiles_z);
   auto tile_of = [&](int64_t t, int64_t& m_tile) {
     m_tile = t % tx;
     const int64_t r = t / tx;
-    return p.mode == 1 ? resolve_tile_at<BN>(p, (int)r, 0) : resolve_tile_at<BN>(p, (int)(r % ty), (int)(r / ty));
+    return p.mode == 1 ? resolve_tile_at<BN>(p, (int)r, 0, toff, goff)
+                       : resolve_tile_at<BN>(p, (int)(r % ty), (int)(r / ty));
   };
 
   if (tid == 0) {
