@@ -31,10 +31,11 @@ def _fused_workspace(lib, device, k, H, I):
 _TC_WS: dict = {}
 _STREAM_WS: dict = {}
 
-# One-token kernel choice: "stream" (one cooperative launch that streams every
-# routed weight into shared memory at entry), "tc" (tensor cores, two
-# launches), "fused" (the first cooperative CUDA-core kernel), "chained"
-# (three CUDA-core launches); "auto" takes the first that supports the shape.
+# One-token kernel choice: "tc" (tensor cores, two launches), "stream" (one
+# cooperative launch that streams every routed weight into shared memory at
+# entry), "fused" (the first cooperative CUDA-core kernel), "chained" (three
+# CUDA-core launches); "auto" takes the first that supports the shape, in
+# that order (the order of their measured one-token times on a B200).
 DECODE_PATH = "auto"
 
 
@@ -54,6 +55,22 @@ def nvfp4_decode(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf
     w = top_k_weights.reshape(-1)[:k].to(torch.bfloat16).contiguous()
     out = torch.empty(1, H, dtype=torch.bfloat16, device=hidden.device)
     path = path or ("fused" if fused else "chained" if fused is False else DECODE_PATH)
+    if path in ("auto", "tc") and lib.aeoq_moe_nvfp4_decode_tc_supported(k, H, I):
+        key = (hidden.device.index, k, H, I)
+        ws = _TC_WS.get(key)
+        if ws is None:
+            ws = torch.zeros(lib.aeoq_moe_nvfp4_decode_tc_workspace_size(k, H, I), dtype=torch.uint8,
+                             device=hidden.device)
+            _TC_WS[key] = ws
+        A.check(lib.aeoq_moe_nvfp4_decode_tc(
+            hidden.data_ptr(), idx.data_ptr(), A.dtype_code(idx.dtype), w.data_ptr(), k,
+            gu.data_ptr(), gu_sf.data_ptr(), gu_ts.data_ptr(), A.dtype_code(gu_ts.dtype),
+            dw.data_ptr(), dw_sf.data_ptr(), dw_ts.data_ptr(), A.dtype_code(dw_ts.dtype),
+            E, H, I, out.data_ptr(), ws.data_ptr(), ws.numel(), A.err_word(hidden.device).data_ptr(),
+            A.stream_ptr(hidden.device)))
+        return out
+    if path == "tc":
+        raise ValueError(f"tensor-core decode does not support top_k={k}, hidden={H}, inter={I}")
     if path in ("auto", "stream") and lib.aeoq_moe_nvfp4_decode_stream_supported(k, H, I) and \
             gu_sf.data_ptr() % 16 == 0 and dw_sf.data_ptr() % 16 == 0:
         key = (hidden.device.index, k, H, I)
@@ -71,22 +88,6 @@ def nvfp4_decode(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf
         return out
     if path == "stream":
         raise ValueError(f"streamed decode does not support top_k={k}, hidden={H}, inter={I}")
-    if path in ("auto", "tc") and lib.aeoq_moe_nvfp4_decode_tc_supported(k, H, I):
-        key = (hidden.device.index, k, H, I)
-        ws = _TC_WS.get(key)
-        if ws is None:
-            ws = torch.zeros(lib.aeoq_moe_nvfp4_decode_tc_workspace_size(k, H, I), dtype=torch.uint8,
-                             device=hidden.device)
-            _TC_WS[key] = ws
-        A.check(lib.aeoq_moe_nvfp4_decode_tc(
-            hidden.data_ptr(), idx.data_ptr(), A.dtype_code(idx.dtype), w.data_ptr(), k,
-            gu.data_ptr(), gu_sf.data_ptr(), gu_ts.data_ptr(), A.dtype_code(gu_ts.dtype),
-            dw.data_ptr(), dw_sf.data_ptr(), dw_ts.data_ptr(), A.dtype_code(dw_ts.dtype),
-            E, H, I, out.data_ptr(), ws.data_ptr(), ws.numel(), A.err_word(hidden.device).data_ptr(),
-            A.stream_ptr(hidden.device)))
-        return out
-    if path == "tc":
-        raise ValueError(f"tensor-core decode does not support top_k={k}, hidden={H}, inter={I}")
     fused = path in ("auto", "fused")
     if fused:
         fused = bool(lib.aeoq_moe_nvfp4_decode_fused_supported(k, H, I))

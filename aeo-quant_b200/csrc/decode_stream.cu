@@ -160,9 +160,26 @@ __device__ __forceinline__ void complete_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(sm100::smem_u32(bar)), "r"(bytes) : "memory");
 }
 
-// Quantize 16 bf16 values with tensor scale ts into exact halves plus the
-// 2^14-scaled block scale (chunk_dot's activation operand).
-__device__ __forceinline__ void quant16_smem(const __nv_bfloat16* src, float ts, __half2* dst, float* sa16k) {
+// Eight E2M1 values (one 32-bit word, two per byte) to four f16x2 with the
+// hardware conversion (cvt.rn.f16x2.e2m1x2, exact). Activations and weights
+// go through the same conversion, so both operands pair their elements the
+// same way and the dot product is unchanged.
+__device__ __forceinline__ void e2m1x8_to_h2x4(uint32_t w, __half2 (&h)[4]) {
+  uint32_t r0, r1, r2, r3;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\tcvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\tcvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+      : "r"(w));
+  h[0] = *reinterpret_cast<__half2*>(&r0);
+  h[1] = *reinterpret_cast<__half2*>(&r1);
+  h[2] = *reinterpret_cast<__half2*>(&r2);
+  h[3] = *reinterpret_cast<__half2*>(&r3);
+}
+
+// Quantize 16 bf16 values (shared memory) with tensor scale ts
+// (quant.py:169-183) and store them as 8 exact f16x2 plus the block scale.
+__device__ __forceinline__ void quant16_h2(const __nv_bfloat16* src, float ts, __half2* dst, float* scale) {
   float v[16];
 #pragma unroll
   for (int q = 0; q < 2; ++q) {
@@ -174,13 +191,45 @@ __device__ __forceinline__ void quant16_smem(const __nv_bfloat16* src, float ts,
   uint32_t w0, w1;
   const uint32_t sf = nvfp4_quant_block(v, ts, w0, w1);
   __half2 t[4];
-  fp4x8_to_half2x4_exact(w0, t);
+  e2m1x8_to_h2x4(w0, t);
 #pragma unroll
   for (int i = 0; i < 4; ++i) dst[i] = t[i];
-  fp4x8_to_half2x4_exact(w1, t);
+  e2m1x8_to_h2x4(w1, t);
 #pragma unroll
   for (int i = 0; i < 4; ++i) dst[4 + i] = t[i];
-  *sa16k = e4m3_decode(sf) * 16384.0f;
+  *scale = e4m3_decode(sf);
+}
+
+// 32-value chunk dot product: a[16] the activation's f16x2 (two 16-blocks),
+// sa[2] their block scales, w 16 packed weight bytes, wsf the weight's two
+// e4m3 block scales. Within a block every product of two E2M1 values is a
+// multiple of 1/4 at most 36, so each f16 half sums 8 of them exactly
+// (|sum| <= 288); the block sum is exact in f32 and is scaled and added to
+// the f32 accumulator once per block, as the tensor core's block16 MMA does.
+__device__ __forceinline__ float dot32(const __half2 (&a)[16], const float (&sa)[2], uint4 w, uint16_t wsf,
+                                       float acc) {
+  const float2 sw = __half22float2(e4m3x2_to_half2(wsf));
+  const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int b = 0; b < 2; ++b) {
+    __half2 h = __float2half2_rn(0.0f);
+    __half2 d[4];
+    e2m1x8_to_h2x4(words[2 * b], d);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h = __hfma2(a[8 * b + i], d[i], h);
+    e2m1x8_to_h2x4(words[2 * b + 1], d);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h = __hfma2(a[8 * b + 4 + i], d[i], h);
+    const float2 f = __half22float2(h);
+    acc = fmaf(f.x + f.y, sa[b] * (b ? sw.y : sw.x), acc);
+  }
+  return acc;
+}
+
+// Fire-and-forget f64 add at L2 (no value returned, so the issuing warp does
+// not wait for the round trip).
+__device__ __forceinline__ void red_add_f64(double* p, double v) {
+  asm volatile("red.relaxed.gpu.global.add.f64 [%0], %1;" ::"l"(p), "d"(v) : "memory");
 }
 
 // L2 policy for data read once: evict first.
@@ -219,6 +268,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const Args a
   const int nr = down_rows(pl, (int)blockIdx.x, &dslot, &r0);
   const Carve cv = carve(H, I, k, np, nr);
   uint64_t* bdown = &bars[kMaxGroups];
+
+  // The hidden vector and the small operands are requested before the weight
+  // copies: issued after them, they would queue behind ~27 MB of traffic.
+  uint4 hid_u[(4096 / 8 + kThreads - 1) / kThreads];
+#pragma unroll
+  for (int q = 0; q < (4096 / 8 + kThreads - 1) / kThreads; ++q) {
+    const int i = tid + q * kThreads;
+    if (i < H / 8) hid_u[q] = __ldg(reinterpret_cast<const uint4*>(a.hidden) + i);
+  }
+  const float gu_ts = load_scalar_f(a.gu_ts, a.gu_ts_dt);
+  const float d_ts = load_scalar_f(a.d_ts, a.d_ts_dt);
+  const float topw_r = tid < k ? __bfloat162float(a.topw[tid]) : 0.0f;
 
   // ---- every warp: its barriers, the expert ids, its share of the copies ----
   // Warp w owns pair groups g = w, w + 16, ...; the last warp owns the down
@@ -275,16 +336,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const Args a
   // ---- hidden vector: stage in shared memory, amax, quantize ---------------
   __nv_bfloat16* hid_s = reinterpret_cast<__nv_bfloat16*>(smem + cv.hid);
   uint32_t key = 0;
-  for (int i = tid; i < H / 8; i += kThreads) {
-    const uint4 u = __ldg(reinterpret_cast<const uint4*>(a.hidden) + i);
-    reinterpret_cast<uint4*>(hid_s)[i] = u;
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) key = max(key, In<AEOQ_BF16>::abs_key(e[j]));
+  for (int q = 0; q < (4096 / 8 + kThreads - 1) / kThreads; ++q) {
+    const int i = tid + q * kThreads;
+    if (i < H / 8) {
+      const uint4 u = hid_u[q];
+      reinterpret_cast<uint4*>(hid_s)[i] = u;
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) key = max(key, In<AEOQ_BF16>::abs_key(e[j]));
+    }
   }
-  const float gu_ts = load_scalar_f(a.gu_ts, a.gu_ts_dt);
-  const float d_ts = load_scalar_f(a.d_ts, a.d_ts_dt);
-  if (tid < k) topw_s[tid] = __bfloat162float(a.topw[tid]);
+  if (tid < k) topw_s[tid] = topw_r;
   key = warp_umax(key);
   if (lane == 0) red[warp] = key;
   __syncthreads();   // hid_s, red, topw_s, ids_w, barrier inits
@@ -295,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const Args a
   const float alpha = ts * gu_ts;
   __half2* act_s = reinterpret_cast<__half2*>(smem + cv.act);
   float* asa_s = reinterpret_cast<float*>(smem + cv.asa);
-  for (int b = tid; b < H / 16; b += kThreads) quant16_smem(hid_s + 16 * b, ts, act_s + 8 * b, asa_s + b);
+  for (int b = tid; b < H / 16; b += kThreads) quant16_h2(hid_s + 16 * b, ts, act_s + 8 * b, asa_s + b);
   __syncthreads();
 
   // ---- gate/up GEMV + GeGLU, pair groups as they land ----------------------
@@ -319,33 +382,52 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const Args a
   const uint8_t* usf_s = smem + cv.usf;
   uint32_t hkey = 0;
   bool ok = true;
-  for (int i = warp; i < np; i += kWarps) {
+  // Two pairs per warp iteration (i and i + kWarps): four independent dot
+  // product chains and one interleaved reduction, for latency hiding.
+  for (int i = warp; i < np; i += 2 * kWarps) {
+    const int i2 = i + kWarps;
+    const bool two = i2 < np;
     // pair i lies in group i / kGroup, whose copies another warp may own
     ok &= sm100::mbar_wait(&bars[i / kGroup], 0, a.err, 31);
-    const int p = p0 + i, j = p / I;
-    const bool valid = ok && ids_w[0][j] >= 0;
-    float ag = 0.f, au = 0.f;
-    if (valid) {
+    if (two) ok &= sm100::mbar_wait(&bars[i2 / kGroup], 0, a.err, 31);
+    const int p = p0 + i, pb = p0 + i2;
+    const bool v1 = ok && ids_w[0][p / I] >= 0;
+    const bool v2 = two && ok && ids_w[0][pb / I] >= 0;
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int q = 0; q < kMaxChunks; ++q) {
-        const int c = lane + 32 * q;
-        if (c < nchunk) {
+    for (int q = 0; q < kMaxChunks; ++q) {
+      const int c = lane + 32 * q;
+      if (c < nchunk) {
+        if (v1) {
           const uint4 gw = *reinterpret_cast<const uint4*>(gate_s + i * rb + 16 * c);
           const uint4 uw = *reinterpret_cast<const uint4*>(up_s + i * rb + 16 * c);
-          const uint16_t gs = *reinterpret_cast<const uint16_t*>(gsf_s + i * sb + 2 * c);
-          const uint16_t us = *reinterpret_cast<const uint16_t*>(usf_s + i * sb + 2 * c);
-          ag = chunk_dot(act[q], sa[q], gw, gs, ag);
-          au = chunk_dot(act[q], sa[q], uw, us, au);
+          s[0] = dot32(act[q], sa[q], gw, *reinterpret_cast<const uint16_t*>(gsf_s + i * sb + 2 * c), s[0]);
+          s[1] = dot32(act[q], sa[q], uw, *reinterpret_cast<const uint16_t*>(usf_s + i * sb + 2 * c), s[1]);
+        }
+        if (v2) {
+          const uint4 gw = *reinterpret_cast<const uint4*>(gate_s + i2 * rb + 16 * c);
+          const uint4 uw = *reinterpret_cast<const uint4*>(up_s + i2 * rb + 16 * c);
+          s[2] = dot32(act[q], sa[q], gw, *reinterpret_cast<const uint16_t*>(gsf_s + i2 * sb + 2 * c), s[2]);
+          s[3] = dot32(act[q], sa[q], uw, *reinterpret_cast<const uint16_t*>(usf_s + i2 * sb + 2 * c), s[3]);
         }
       }
     }
-    ag = warp_sum(ag);
-    au = warp_sum(au);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int z = 0; z < 4; ++z) s[z] += __shfl_xor_sync(0xffffffffu, s[z], o);
+    }
     if (lane == 0) {
-      const float gv = bf16r(ag * alpha), uv = bf16r(au * alpha);
+      const float gv = bf16r(s[0] * alpha), uv = bf16r(s[1] * alpha);
       const __nv_bfloat16 hv = __float2bfloat16_rn(bf16r(gelu_tanh(gv)) * uv);
       a.h[p] = hv;
       hkey = max(hkey, In<AEOQ_BF16>::abs_key(hv));
+      if (two) {
+        const float gv2 = bf16r(s[2] * alpha), uv2 = bf16r(s[3] * alpha);
+        const __nv_bfloat16 hv2 = __float2bfloat16_rn(bf16r(gelu_tanh(gv2)) * uv2);
+        a.h[pb] = hv2;
+        hkey = max(hkey, In<AEOQ_BF16>::abs_key(hv2));
+      }
     }
   }
   // every group barrier completes before the CTA exits (the copies land)
@@ -385,6 +467,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const Args a
     const float hts = nvfp4_tensor_scale<AEOQ_BF16>(In<AEOQ_BF16>::key_to_f(hmax_s));
     const float alpha_d = hts * d_ts;
     __syncthreads();
+    // the slot's GeGLU row quantized once per CTA (one 16-block per thread)
+    __half2* hact_s = act_s;          // the hidden vector's operand is no longer read
+    float* hsa_s = asa_s;
+    for (int b = tid; b < I / 16; b += kThreads) quant16_h2(hrow_s + 16 * b, hts, hact_s + 8 * b, hsa_s + b);
+    __syncthreads();
     const bool ok_dn = sm100::mbar_wait(bdown, 0, a.err, 33);
     const bool valid = ok_dn && ids_w[0][dslot] >= 0;
     const float wj = topw_s[dslot];
@@ -392,19 +479,35 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const Args a
     __half2 hv[16];
     float hs[2] = {0.f, 0.f};
     if (lane < nchunk2) {
-      quant16_smem(hrow_s + 32 * lane, hts, hv, &hs[0]);
-      quant16_smem(hrow_s + 32 * lane + 16, hts, hv + 8, &hs[1]);
+      const uint4* hp = reinterpret_cast<const uint4*>(hact_s + 16 * lane);
+#pragma unroll
+      for (int z = 0; z < 4; ++z) *reinterpret_cast<uint4*>(&hv[4 * z]) = hp[z];
+      hs[0] = hsa_s[2 * lane];
+      hs[1] = hsa_s[2 * lane + 1];
     }
     const uint8_t* dn_s = smem + cv.dn;
     const uint8_t* dsf_s = smem + cv.dsf;
     if (valid) {
-      for (int r = warp; r < nr; r += kWarps) {
-        float acc = 0.f;
-        if (lane < nchunk2)
-          acc = chunk_dot(hv, hs, *reinterpret_cast<const uint4*>(dn_s + r * rb2 + 16 * lane),
-                          *reinterpret_cast<const uint16_t*>(dsf_s + r * sb2 + 2 * lane), acc);
-        acc = warp_sum(acc);
-        if (lane == 0) atomicAdd(a.acc + r0 + r, (double)bf16r(bf16r(acc * alpha_d) * wj));
+      // two rows per warp iteration (r and r + kWarps) for latency hiding
+      for (int r = warp; r < nr; r += 2 * kWarps) {
+        const int r2 = r + kWarps;
+        float s0 = 0.f, s1 = 0.f;
+        if (lane < nchunk2) {
+          s0 = dot32(hv, hs, *reinterpret_cast<const uint4*>(dn_s + r * rb2 + 16 * lane),
+                     *reinterpret_cast<const uint16_t*>(dsf_s + r * sb2 + 2 * lane), s0);
+          if (r2 < nr)
+            s1 = dot32(hv, hs, *reinterpret_cast<const uint4*>(dn_s + r2 * rb2 + 16 * lane),
+                       *reinterpret_cast<const uint16_t*>(dsf_s + r2 * sb2 + 2 * lane), s1);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+          s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        }
+        if (lane == 0) {
+          red_add_f64(a.acc + r0 + r, (double)bf16r(bf16r(s0 * alpha_d) * wj));
+          if (r2 < nr) red_add_f64(a.acc + r0 + r2, (double)bf16r(bf16r(s1 * alpha_d) * wj));
+        }
       }
     }
     // arrival on the row block; the k-th arrival rounds and clears it

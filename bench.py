@@ -944,9 +944,9 @@ def main():
         return a0.elapsed_time(a1) / K
 
     stage_ms = {}
-    stream_path = B == 1 and moe_ops.DECODE_PATH in ("auto", "stream") and bool(
-        lib.aeoq_moe_nvfp4_decode_stream_supported(TOPK, H, I))
-    tc_path = B == 1 and bool(lib.aeoq_moe_nvfp4_decode_tc_supported(TOPK, H, I))
+    tc_path = B == 1 and moe_ops.DECODE_PATH in ("auto", "tc") and bool(
+        lib.aeoq_moe_nvfp4_decode_tc_supported(TOPK, H, I))
+    stream_path = B == 1 and bool(lib.aeoq_moe_nvfp4_decode_stream_supported(TOPK, H, I))
     if B == 1:
         if stream_path:
             stage_ms["stream"] = time_graph(lib.aeoq_moe_nvfp4_decode_stream, sws, sws_n)
@@ -1004,7 +1004,7 @@ def main():
     if rank == 0:
         hbm, peak_src = peaks()
         roof = None
-        key = next((k2 for k2 in ("stream", "tc", "fused") if k2 in stage_ms), None)
+        key = next((k2 for k2 in ("tc", "stream", "fused") if k2 in stage_ms), None)
         if key:
             # algorithmic bytes: the k experts' packed weights and scales, the
             # hidden vector in and the output out (intermediates stay on chip
@@ -1030,7 +1030,7 @@ def main():
             "data": "synthetic (bf16 N(0,0.02) weights quantized on device; N(0,1) hidden; uniform top-8)",
             "config": decode_config(B, L, world),
             "step_hbm_gbs": round(step_bytes / (ms_max / K / 1000.0) / 1e9, 1),
-            "gpu_launches": (1 if stream_path else 2 if tc_path else 1) * K,
+            "gpu_launches": (2 if tc_path else 1) * K,
             "clocks": clk.summary(),
             "e2e": {"value": round(e2e_val, 1), "unit": "tok/s", "steps": n_e2e,
                     "h2d_bytes_per_step": B * H * 2 + B * TOPK * 8 + B * TOPK * 2,
