@@ -244,8 +244,11 @@ __device__ __forceinline__ void nvfp4_block_thresholds(float ts, float bs, float
 // every nonzero |x| is in [2^-30, 2^30], ts in [2^-40, 2^40] and bs in
 // [2^-9, 448] (all quotients then stay finite normal floats); any other
 // block runs the two divisions per element.
-__device__ __forceinline__ uint32_t nvfp4_quant_block(const float (&v)[16], float ts,
-                                                      uint32_t& w0, uint32_t& w1) {
+// The block's binning once its thresholds w[7] are known (fast path) or
+// with the two divisions per element (any other block).
+template <class GetThresholds>
+__device__ __forceinline__ uint32_t nvfp4_quant_block_core(const float (&v)[16], float ts, uint32_t& w0,
+                                                           uint32_t& w1, GetThresholds get_w) {
   float amax = 0.0f, amin = 0x1p30f;
   bool anynan = false;
 #pragma unroll
@@ -263,7 +266,7 @@ __device__ __forceinline__ uint32_t nvfp4_quant_block(const float (&v)[16], floa
                     bs >= 0x1p-9f && bs <= 448.0f;
   if (__builtin_expect(fast, 1)) {
     float w[7];
-    nvfp4_block_thresholds(ts, bs, w);
+    get_w(sf, bs, w);
     uint32_t words[2] = {0u, 0u};
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
@@ -280,6 +283,40 @@ __device__ __forceinline__ uint32_t nvfp4_quant_block(const float (&v)[16], floa
                              bs, w0, w1);
   }
   return sf;
+}
+
+__device__ __forceinline__ uint32_t nvfp4_quant_block(const float (&v)[16], float ts,
+                                                      uint32_t& w0, uint32_t& w1) {
+  return nvfp4_quant_block_core(v, ts, w0, w1, [&](uint32_t, float bs, float (&w)[7]) {
+    nvfp4_block_thresholds(ts, bs, w);
+  });
+}
+
+// Thresholds of every positive e4m3 block scale for one tensor scale ts:
+// tab[8 * code + j], j < 7 (codes whose scale leaves the fast-path range
+// are never read). Filled cooperatively by the threads of a block
+// (nthreads of them, this one being `t`); the caller synchronises before use.
+__device__ __forceinline__ void nvfp4_threshold_table(float ts, float* tab, int t, int nthreads) {
+  for (int c = t; c < 127; c += nthreads) {
+    const float bs = e4m3_decode((uint32_t)c);
+    float w[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (bs >= 0x1p-9f && bs <= 448.0f && ts >= 0x1p-40f && ts <= 0x1p40f) nvfp4_block_thresholds(ts, bs, w);
+#pragma unroll
+    for (int j = 0; j < 7; ++j) tab[8 * c + j] = w[j];
+    tab[8 * c + 7] = 0.0f;
+  }
+}
+
+// nvfp4_quant_block with the block thresholds read from a table made by
+// nvfp4_threshold_table for the same ts (shared memory, 4 KB): the same bits,
+// without the per-block double-precision threshold arithmetic.
+__device__ __forceinline__ uint32_t nvfp4_quant_block_tab(const float (&v)[16], float ts, const float* tab,
+                                                          uint32_t& w0, uint32_t& w1) {
+  return nvfp4_quant_block_core(v, ts, w0, w1, [&](uint32_t code, float, float (&w)[7]) {
+    const float4 a = *reinterpret_cast<const float4*>(tab + 8 * code);
+    const float4 b = *reinterpret_cast<const float4*>(tab + 8 * code + 4);
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z;
+  });
 }
 
 // ---------------------------------------------------------------------------

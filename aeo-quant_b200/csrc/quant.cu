@@ -72,12 +72,12 @@ __device__ __forceinline__ uint32_t block_umax(uint32_t v, uint32_t* sm) {
 
 template <int DT, bool VEC>
 __device__ __forceinline__ void quant_group(const typename In<DT>::T* x, int64_t g, int64_t gpr,
-                                            int64_t ld, float ts, uint8_t* packed, uint8_t* sf) {
+                                            int64_t ld, float ts, const float* tab, uint8_t* packed, uint8_t* sf) {
   const int64_t r = g / gpr, c = g - r * gpr;
   float v[16];
   load_group<DT, VEC>(x + r * ld + c * 16, v);
   uint32_t w0, w1;
-  uint32_t code = nvfp4_quant_block(v, ts, w0, w1);
+  uint32_t code = nvfp4_quant_block_tab(v, ts, tab, w0, w1);
   *reinterpret_cast<uint2*>(packed + g * 8) = make_uint2(w0, w1);
   sf[g] = (uint8_t)code;
 }
@@ -87,6 +87,7 @@ __global__ void __launch_bounds__(1024) nvfp4_quant_small_kernel(
     const typename In<DT>::T* __restrict__ x, int64_t rows, int64_t gpr, int64_t ld,
     uint8_t* __restrict__ packed, uint8_t* __restrict__ sf, void* ts_out) {
   __shared__ uint32_t sm[32];
+  __shared__ __align__(16) float tab[128 * 8];
   const int64_t ng = rows * gpr;
   uint32_t key = 0;
   for (int64_t g = threadIdx.x; g < ng; g += blockDim.x) {
@@ -96,7 +97,10 @@ __global__ void __launch_bounds__(1024) nvfp4_quant_small_kernel(
   key = block_umax(key, sm);
   const float ts = nvfp4_tensor_scale<DT>(ng ? In<DT>::key_to_f(key) : 0.0f);
   if (threadIdx.x == 0) In<DT>::store(ts_out, ts);
-  for (int64_t g = threadIdx.x; g < ng; g += blockDim.x) quant_group<DT, VEC>(x, g, gpr, ld, ts, packed, sf);
+  nvfp4_threshold_table(ts, tab, threadIdx.x, blockDim.x);
+  __syncthreads();
+  for (int64_t g = threadIdx.x; g < ng; g += blockDim.x)
+    quant_group<DT, VEC>(x, g, gpr, ld, ts, tab, packed, sf);
 }
 
 template <int DT, bool VEC>
@@ -121,6 +125,7 @@ __global__ void __launch_bounds__(kQuantThreads) nvfp4_quant_kernel(
     const uint32_t* __restrict__ parts, int nparts, const void* ts_in,
     uint8_t* __restrict__ packed, uint8_t* __restrict__ sf, void* ts_out) {
   __shared__ uint32_t sm[32];
+  __shared__ __align__(16) float tab[128 * 8];
   float ts;
   if (ts_in) {
     ts = In<DT>::load(reinterpret_cast<const typename In<DT>::T*>(ts_in));
@@ -131,10 +136,12 @@ __global__ void __launch_bounds__(kQuantThreads) nvfp4_quant_kernel(
     ts = nvfp4_tensor_scale<DT>(In<DT>::key_to_f(key));
     if (blockIdx.x == 0 && threadIdx.x == 0 && ts_out) In<DT>::store(ts_out, ts);
   }
+  nvfp4_threshold_table(ts, tab, threadIdx.x, blockDim.x);
+  __syncthreads();
   const int64_t ng = rows * gpr;
   for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < ng;
        g += (int64_t)gridDim.x * blockDim.x)
-    quant_group<DT, VEC>(x, g, gpr, ld, ts, packed, sf);
+    quant_group<DT, VEC>(x, g, gpr, ld, ts, tab, packed, sf);
 }
 
 static int dtype_size(int dt) { return dt == AEOQ_F32 ? 4 : 2; }
