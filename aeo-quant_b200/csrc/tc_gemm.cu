@@ -509,14 +509,13 @@ int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int64_t row_bytes, 
 // L2). The producers run ahead across tile boundaries, and the accumulator
 // is double-buffered in TMEM: the epilogue of tile i (eight warps, two per
 // lane quadrant) overlaps the main loop of tile i + 1.
-//   warps 0, 2, 3, 12 .. 19   producers (each stage's copies spread over them)
-//   warp 1                    TMEM owner + MMA issuer
-//   warps 4 .. 11             epilogue (two per TMEM lane quadrant)
-constexpr int kPEpiWarps = 8;
+//   warps 0, 2, 3   producers (ring slot s is filled by producer s % 3)
+//   warp 1          TMEM owner + MMA issuer
+//   warps 4 .. 19   epilogue (four per TMEM lane quadrant)
+constexpr int kPEpiWarps = 16;
 constexpr int kPMaxExperts = 256;   // grouped offsets held in shared memory up to this many experts
-constexpr int kPExtraProducers = 8;
-constexpr int kPThreads = 128 + 32 * kPEpiWarps + 32 * kPExtraProducers;
-constexpr int kPProducers = 3 + kPExtraProducers;
+constexpr int kPThreads = 128 + 32 * kPEpiWarps;
+constexpr int kPProducers = 3;
 
 template <int BN, bool kF8>
 struct PLayout {
@@ -609,23 +608,9 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
   sm100::tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
 
-  if (warp == 0 || warp == 2 || warp == 3 || warp >= 4 + kPEpiWarps) {
+  if (warp == 0 || warp == 2 || warp == 3) {
     // ------------------------------------------------------------ producers
-    // A stage's copies are spread over the producer warps: request
-    // r = kOps * slot + op (op 0 the A tile, which also posts the stage's
-    // expected bytes, 1 the B tile, 2 and 3 the scale atoms) is issued by
-    // producer r % kPProducers, for every use of that ring slot. One warp's
-    // copies complete one after another, so a stage whose copies come from
-    // several warps refills sooner, and the ring covers more of the load
-    // latency. The assignment depends on the slot, not the stage: a producer
-    // waits on every use of its slots in order, so each parity wait on a
-    // slot's empty barrier refers to the previous use of that slot (a
-    // producer that skipped a use could run two phases ahead, where the
-    // parity no longer tells the phases apart). (A copy may complete before
-    // its stage's expected bytes are posted; the transaction count then dips
-    // below zero until they are.)
-    constexpr int kOps = kF8 ? 2 : 4;
-    const int pidx = warp == 0 ? 0 : warp <= 3 ? warp - 1 : 3 + (warp - 4 - kPEpiWarps);
+    const int pidx = warp == 0 ? 0 : warp - 1;
     const bool leader = sm100::elect_one();
     int64_t g = 0;   // stage counter over all of this CTA's tiles
     bool alive = true;
@@ -637,36 +622,32 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
       const int64_t m_tiles = p.n_out / 128;
       const uint8_t* sfa_base = kF8 ? nullptr : p.sfa + ((ti.expert * m_tiles + m_tile) * kb_total) * 512;
       const uint8_t* sfb_base = kF8 ? nullptr : p.sfb + (ti.tile * kb_total) * (size_t)L::kSfbAtoms * 512;
-      for (int kt = 0; kt < num_kt && alive; ++kt, ++g) {
+      for (int kt = 0; kt < num_kt; ++kt, ++g) {
         const int s = (int)(g % L::kStages);
+        if (s % kPProducers != pidx) continue;
         const uint32_t ph = (uint32_t)((g / L::kStages) & 1);
+        if (!sm100::mbar_wait(&sh->empty[s], ph ^ 1, p.err, 61)) { alive = false; break; }
         const int nkb = min(4, kb_total - kt * 4);
         const uint32_t sfa_bytes = kF8 ? 0u : (uint32_t)nkb * 512;
         const uint32_t sfb_bytes = kF8 ? 0u : (uint32_t)nkb * L::kSfbAtoms * 512;
         const int32_t x = kt * kKTBytes;
-        for (int op = 0; op < kOps; ++op) {
-          if ((s * kOps + op) % kPProducers != pidx) continue;
-          if (!sm100::mbar_wait(&sh->empty[s], ph ^ 1, p.err, 61)) { alive = false; break; }
-          if (leader) {
-            if (op == 0) {
-              sm100::mbar_arrive_expect_tx(&sh->full[s], (uint32_t)(L::kA + L::kB) + sfa_bytes + sfb_bytes);
-              if (geglu) {
-                const int64_t n0 = m_tile * 64;
-                sm100::tma_load_2d(stA(s), &tmA, x, (int32_t)(a_row_base + n0), &sh->full[s]);
-                sm100::tma_load_2d(stA(s) + 64 * kKTBytes, &tmA, x, (int32_t)(a_row_base + p.n_out / 2 + n0),
-                                   &sh->full[s]);
-              } else {
-                sm100::tma_load_2d(stA(s), &tmA, x, (int32_t)(a_row_base + m_tile * 128), &sh->full[s]);
-              }
-            } else if (op == 1) {
-              sm100::tma_load_2d(stB(s), &tmB, x, (int32_t)ti.b_row0, &sh->full[s]);
-            } else if constexpr (!kF8) {
-              if (op == 2) bulk_g2s(stSFA(s), sfa_base + (size_t)kt * 4 * 512, sfa_bytes, &sh->full[s]);
-              else bulk_g2s(stSFB(s), sfb_base + (size_t)kt * 4 * L::kSfbAtoms * 512, sfb_bytes, &sh->full[s]);
-            }
+        if (leader) {
+          sm100::mbar_arrive_expect_tx(&sh->full[s], (uint32_t)(L::kA + L::kB) + sfa_bytes + sfb_bytes);
+          if constexpr (!kF8) {
+            bulk_g2s(stSFA(s), sfa_base + (size_t)kt * 4 * 512, sfa_bytes, &sh->full[s]);
+            bulk_g2s(stSFB(s), sfb_base + (size_t)kt * 4 * L::kSfbAtoms * 512, sfb_bytes, &sh->full[s]);
           }
-          __syncwarp();
+          if (geglu) {
+            const int64_t n0 = m_tile * 64;
+            sm100::tma_load_2d(stA(s), &tmA, x, (int32_t)(a_row_base + n0), &sh->full[s]);
+            sm100::tma_load_2d(stA(s) + 64 * kKTBytes, &tmA, x, (int32_t)(a_row_base + p.n_out / 2 + n0),
+                               &sh->full[s]);
+          } else {
+            sm100::tma_load_2d(stA(s), &tmA, x, (int32_t)(a_row_base + m_tile * 128), &sh->full[s]);
+          }
+          sm100::tma_load_2d(stB(s), &tmB, x, (int32_t)ti.b_row0, &sh->full[s]);
         }
+        __syncwarp();
       }
     }
   } else if (warp == 1) {
@@ -728,7 +709,7 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
     // multiple of 8 tokens)
     constexpr int kSegs = kPEpiWarps / 4;
     constexpr int kSeg = ((BN + 8 * kSegs - 1) / (8 * kSegs)) * 8;
-    const int hseg = (warp - 4) >> 2;   // epilogue warps 4 .. 4 + kPEpiWarps - 1
+    const int hseg = (warp - 4) >> 2;
     const int tbeg = hseg * kSeg, tend = min(BN, tbeg + kSeg);
     constexpr int kChunk = kSeg < 32 ? kSeg : 32;
     const int ncol = geglu ? 64 : 128;
