@@ -130,15 +130,21 @@ def check(rc: int) -> None:
         raise AeoqError(f"aeoq status {rc}: {msg}")
 
 
+_SM100_DEVICES: set = set()
+
+
 def require_cuda(*tensors: torch.Tensor) -> None:
     for t in tensors:
         if not t.is_cuda:
             raise AeoqError("aeo_quant_b200 runs on CUDA tensors only (no CPU path); "
                             f"got a tensor on {t.device}")
     dev = tensors[0].device
+    if dev.index in _SM100_DEVICES:
+        return
     major, _ = torch.cuda.get_device_capability(dev)
     if major != 10:
         raise AeoqError(f"aeo_quant_b200 is built for sm_100a (B200); device {dev} is sm_{major}x")
+    _SM100_DEVICES.add(dev.index)
 
 
 def stream_ptr(device: torch.device) -> int:

@@ -78,14 +78,26 @@ class Gemma4TextExpertsNVFP4(Gemma4TextExperts):
             return self._forward_decode_3d(hidden_states, top_k_index, top_k_weights)
         return self._forward_prefill(hidden_states, top_k_index, top_k_weights)
 
+    def _decode_launcher(self):
+        """The cached one-token launcher, rebuilt when a weight buffer moves
+        or is modified in place."""
+        bufs = (self.gate_up_proj, self.gate_up_proj_scale, self.gate_up_proj_scale_2,
+                self.down_proj, self.down_proj_scale, self.down_proj_scale_2)
+        key = tuple((b.data_ptr(), b._version) for b in bufs)
+        cached = self.__dict__.get("_decode_cache")
+        if cached is None or cached[0] != key:
+            cached = (key, moe_ops.DecodeLauncher(*bufs))
+            self.__dict__["_decode_cache"] = cached
+        return cached[1]
+
     def _forward_decode_3d(self, hidden_states, top_k_index, top_k_weights):
         """One token: fused gather GEMV pair (modeling_nvfp4.py:132-186)."""
+        if not hidden_states.is_cuda:
+            raise moe_ops.A.AeoqError("aeo_quant_b200 runs on CUDA tensors only (no CPU path); "
+                                      f"got a tensor on {hidden_states.device}")
         with _moe_range("nvfp4_moe_decode_fused"):
-            out = moe_ops.nvfp4_decode(
-                hidden_states, top_k_index, top_k_weights,
-                self.gate_up_proj, self.gate_up_proj_scale, self.gate_up_proj_scale_2,
-                self.down_proj, self.down_proj_scale, self.down_proj_scale_2)
-        return out.to(hidden_states.dtype)
+            out = self._decode_launcher()(hidden_states, top_k_index, top_k_weights)
+        return out if out.dtype == hidden_states.dtype else out.to(hidden_states.dtype)
 
     def _forward_prefill(self, hidden_states, top_k_index, top_k_weights):
         """Many tokens (modeling_nvfp4.py:188-255)."""

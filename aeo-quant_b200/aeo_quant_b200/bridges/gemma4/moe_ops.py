@@ -106,6 +106,60 @@ def nvfp4_decode(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf
     return out
 
 
+class DecodeLauncher:
+    """The one-token forward of one expert layer with everything that does
+    not change between tokens resolved once: the kernel (the path
+    ``nvfp4_decode`` would pick), the weight pointers and dtype codes, the
+    workspace and the error word. A call then checks the token's tensors,
+    allocates the output and makes one C call: the same launches and bits as
+    ``nvfp4_decode``, with less host time per token. Build a new one when
+    the weights change (``Gemma4TextExpertsNVFP4`` keys it on the buffers'
+    addresses and versions)."""
+
+    def __init__(self, gu, gu_sf, gu_ts, dw, dw_sf, dw_ts):
+        A.require_cuda(gu, dw)
+        lib = A.load()
+        E, two_i, h_half = gu.shape
+        self.E, self.H, self.I = E, h_half * 2, two_i // 2
+        self.dev = gu.device
+        self.lib = lib
+        self.k = None
+        self.weights = (gu.data_ptr(), gu_sf.data_ptr(), gu_ts.data_ptr(), A.dtype_code(gu_ts.dtype),
+                        dw.data_ptr(), dw_sf.data_ptr(), dw_ts.data_ptr(), A.dtype_code(dw_ts.dtype))
+        self._keep = (gu, gu_sf, gu_ts, dw, dw_sf, dw_ts)
+
+    def _setup(self, k):
+        lib, H, I, dev = self.lib, self.H, self.I, self.dev
+        self.fn = None
+        if DECODE_PATH in ("auto", "tc") and lib.aeoq_moe_nvfp4_decode_tc_supported(k, H, I):
+            self.ws = torch.zeros(lib.aeoq_moe_nvfp4_decode_tc_workspace_size(k, H, I), dtype=torch.uint8,
+                                  device=dev)
+            self.fn, self.err = lib.aeoq_moe_nvfp4_decode_tc, (A.err_word(dev).data_ptr(),)
+        elif DECODE_PATH in ("auto", "stream") and lib.aeoq_moe_nvfp4_decode_stream_supported(k, H, I) and \
+                self._keep[1].data_ptr() % 16 == 0 and self._keep[4].data_ptr() % 16 == 0:
+            self.ws = torch.zeros(lib.aeoq_moe_nvfp4_decode_stream_workspace_size(k, H, I), dtype=torch.uint8,
+                                  device=dev)
+            self.fn, self.err = lib.aeoq_moe_nvfp4_decode_stream, (A.err_word(dev).data_ptr(),)
+        self.k = k
+
+    def __call__(self, hidden, top_k_index, top_k_weights):
+        k = top_k_index.shape[-1]
+        if k != self.k:
+            self._setup(k)
+        if (self.fn is None or hidden.dtype != torch.bfloat16 or hidden.device != self.dev
+                or not hidden.is_contiguous() or hidden.shape[-1] != self.H
+                or top_k_weights.dtype != torch.bfloat16 or not top_k_index.is_contiguous()
+                or not top_k_weights.is_contiguous()):
+            gu, gu_sf, gu_ts, dw, dw_sf, dw_ts = self._keep
+            return nvfp4_decode(hidden, top_k_index, top_k_weights, gu, gu_sf, gu_ts, dw, dw_sf, dw_ts)
+        out = torch.empty(1, self.H, dtype=torch.bfloat16, device=self.dev)
+        A.check(self.fn(hidden.data_ptr(), top_k_index.data_ptr(), A.dtype_code(top_k_index.dtype),
+                        top_k_weights.data_ptr(), k, *self.weights, self.E, self.H, self.I, out.data_ptr(),
+                        self.ws.data_ptr(), self.ws.numel(), *self.err,
+                        torch.cuda.current_stream(self.dev).cuda_stream))
+        return out
+
+
 def pick_tile_n(n_pairs: int, num_experts: int) -> int:
     """Token-tile width of the grouped GEMMs from the mean rows per expert."""
     avg = max(1, n_pairs // max(1, min(num_experts, n_pairs)))
