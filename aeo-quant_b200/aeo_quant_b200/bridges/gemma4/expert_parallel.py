@@ -4,28 +4,35 @@ combine.
 
 Semantics are those of the one-GPU prefill forward
 (aeo_quant ``src/aeo_quant/bridges/gemma4/modeling_nvfp4.py:188-255``) over
-the union of all ranks' tokens, bit for bit:
+the union of all ranks' tokens:
 
 * the activation tensor scale comes from the global amax (one
   all-reduce(max) of a scalar; ``quantize_2d_to_nvfp4`` over the whole
   batch, :203-206), and each rank quantizes its own tokens with it;
-* every routed (token, slot) pair is sent, NVFP4-packed (H/2 bytes of E2M1
-  plus H/16 e4m3 scales, 3.6x fewer bytes than bf16), to the rank owning
-  its expert; an expert's rows therefore all meet on one rank, so its
-  per-expert down re-quantization (:239-244) sees exactly the rows it
-  would on one GPU;
-* the weighted expert outputs travel back to the token's rank, which folds
-  them per token in ascending expert order with bf16 rounding after each
-  add (``index_add_``, :250-253).
+* each token is sent once to every rank that owns at least one of its
+  experts, NVFP4-packed (H/2 bytes of E2M1 plus H/16 e4m3 scales, 3.6x
+  fewer bytes than bf16), with the local ids and routing weights of its
+  experts there; an expert's rows therefore all meet on one rank, so its
+  per-expert down re-quantization (:239-244) sees exactly the rows it would
+  on one GPU, and every expert output is bit for bit the one-GPU value;
+* the owning rank folds the weighted outputs of a token's experts it holds
+  (ascending expert id, bf16 rounding after each add, as ``index_add_``
+  does, :250-253) and sends back ONE row per (token, rank); the home rank
+  folds those partial rows in rank order with the same rounding.
+
+Only the association of the final fold differs from one GPU: the result
+is within the bf16 rounding of up to k adds of the one-GPU forward (a few
+ulps), and the bytes on the wire are one row per (token, owning rank) each
+way instead of one per (token, expert).
 
 By default rank r owns experts [r * E/world, (r+1) * E/world). A placement
 (``owner[e]`` = the rank holding expert e, E/world experts per rank, e.g.
 from ``balanced_placement`` for skewed routing) may replace that; a rank
-then holds its experts in ascending id order. Results do not depend on the
-placement. Pairs whose expert id is outside [0, E) are dropped (:209-211). ``ep_moe_forward`` is the
+then holds its experts in ascending id order. Pairs whose expert id is
+outside [0, E) are dropped (:209-211). ``ep_moe_forward`` is the
 orchestration shared by every backend; the expert arithmetic, the payload
-codec and the combine are supplied by an ``ops`` object (``NVFP4EpOps``
-for the CUDA library).
+codec and the folds are supplied by an ``ops`` object (``NVFP4EpOps`` for
+the CUDA library).
 """
 from __future__ import annotations
 
@@ -130,6 +137,41 @@ def global_amax(hidden: torch.Tensor, group) -> torch.Tensor:
     return amax
 
 
+def plan_token_dispatch(top_k_index: torch.Tensor, num_experts: int, world: int, owner: torch.Tensor | None = None):
+    """Send list of one expert-parallel layer: every (token, rank) where the
+    rank owns at least one of the token's experts, ordered by rank, then
+    token.
+
+    Returns ``(send_tok, send_dest, counts, local_ids)``: the token and the
+    destination of each send, sends per destination rank, and per send the k
+    local expert ids on the destination (``E/world``, an id the grouped
+    forward drops, where the slot's expert lives elsewhere or is invalid)."""
+    if num_experts % world:
+        raise ValueError(f"num_experts ({num_experts}) must be divisible by the world size ({world})")
+    e_loc = num_experts // world
+    ids = top_k_index.to(torch.int64)
+    T, k = ids.shape
+    dev = ids.device
+    valid = (ids >= 0) & (ids < num_experts)
+    safe = ids.clamp(0, num_experts - 1)
+    if owner is None:
+        dest = torch.div(safe, e_loc, rounding_mode="floor")
+        local = safe - dest * e_loc
+    else:
+        owner = torch.as_tensor(owner, dtype=torch.int64).reshape(-1)
+        dest = owner.to(dev)[safe]
+        local = local_index(owner, world).to(dev)[safe]
+    dest = torch.where(valid, dest, torch.full_like(dest, world))
+    present = torch.zeros(world + 1, T, dtype=torch.bool, device=dev)
+    present[dest, torch.arange(T, device=dev).unsqueeze(1).expand(T, k)] = True
+    sel = torch.nonzero(present[:world].reshape(-1)).reshape(-1)    # rank-major, then token
+    send_tok = sel % T
+    send_dest = torch.div(sel, T, rounding_mode="floor")
+    counts = torch.bincount(send_dest, minlength=world)
+    lid = torch.where(dest[send_tok] == send_dest.unsqueeze(1), local[send_tok], torch.full_like(local[send_tok], e_loc))
+    return send_tok, send_dest, counts, lid.to(torch.int32)
+
+
 def ep_moe_forward(hidden, top_k_index, top_k_weights, *, num_experts: int, group, ops, owner=None, mark=None):
     """One expert-parallel MoE layer over ``group`` (see module docstring).
     ``owner``: optional placement (E,) of experts on ranks. ``mark``: optional
@@ -147,41 +189,34 @@ def ep_moe_forward(hidden, top_k_index, top_k_weights, *, num_experts: int, grou
     dev = hidden.device
     if owner is None:
         my_experts = torch.arange(rank * e_loc, (rank + 1) * e_loc)
-        local_of = None
     else:
         owner = torch.as_tensor(owner, dtype=torch.int64).reshape(-1).cpu()
-        local_of = local_index(owner, world).to(dev)
         my_experts = torch.nonzero(owner == rank).reshape(-1)
-    send_pairs, send_counts, _ = plan_dispatch(top_k_index, num_experts, world, owner)
+    send_tok, send_dest, send_counts, lid = plan_token_dispatch(top_k_index, num_experts, world, owner)
 
-    # counts: one small all-to-all, then the split sizes on the host
+    # counts: one small all-to-all and ONE host read of both split lists
     recv_counts_t = torch.empty_like(send_counts)
     dist.all_to_all_single(recv_counts_t, send_counts, group=group)
-    sc = send_counts.tolist()
-    rc = recv_counts_t.tolist()
+    both = torch.cat([send_counts, recv_counts_t]).tolist()
+    sc, rc = both[:world], both[world:]
 
     ts = ops.tensor_scale(global_amax(hidden, group), hidden.dtype)
     payload = ops.encode(hidden, ts)                     # per-token row tensors
-    send_tok = torch.div(send_pairs, k, rounding_mode="floor")
-    ids = top_k_index.reshape(-1).to(torch.int64)
-    wbits = top_k_weights.reshape(-1).to(torch.bfloat16).view(torch.int16).to(torch.int32)
-    if local_of is None:
-        local_id = (ids[send_pairs] - torch.div(ids[send_pairs], e_loc, rounding_mode="floor") * e_loc).to(torch.int32)
-    else:
-        local_id = local_of[ids[send_pairs]].to(torch.int32)
-    meta = torch.stack([local_id, wbits[send_pairs]], dim=1)
+    wbits = top_k_weights.to(torch.bfloat16).contiguous().view(torch.int16).to(torch.int32)
+    meta = torch.cat([lid, wbits[send_tok]], dim=1)      # (n_send, 2k) int32
 
     recv_payload = [_all_to_all_rows(p[send_tok], sc, rc, group) for p in payload]
     recv_meta = _all_to_all_rows(meta, sc, rc, group)
-    recv_w = recv_meta[:, 1].to(torch.int16).view(torch.bfloat16)
+    recv_lid = recv_meta[:, :k].contiguous()
+    recv_w = recv_meta[:, k:].to(torch.int16).view(torch.bfloat16).contiguous()
     mark("experts")
-    out_rows = ops.experts(recv_payload, recv_meta[:, 0], recv_w, ts, my_experts)   # (n_recv, H)
+    partial = ops.experts(recv_payload, recv_lid, recv_w, ts, my_experts)   # (n_recv, H), one row per token
 
     mark("combine")
-    back = _all_to_all_rows(out_rows, rc, sc, group)     # in this rank's send order
-    pair_row = torch.full((T * k,), -1, dtype=torch.int32, device=dev)
-    pair_row[send_pairs] = torch.arange(send_pairs.numel(), dtype=torch.int32, device=dev)
-    out = ops.combine(back, pair_row, top_k_index, T, k)
+    back = _all_to_all_rows(partial, rc, sc, group)      # in this rank's send order
+    slot_row = torch.full((T, world), -1, dtype=torch.int32, device=dev)
+    slot_row[send_tok, send_dest] = torch.arange(send_tok.numel(), dtype=torch.int32, device=dev)
+    out = ops.fold(back, slot_row, T, world)
     mark("end")
     return out
 
@@ -204,26 +239,38 @@ class NVFP4EpOps:
         return [packed, sf.view(torch.uint8)]
 
     def experts(self, payload, local_ids, weights, ts, my_experts):
+        """Grouped forward of the received tokens over this rank's experts,
+        then each token's weighted outputs folded (ascending expert id, bf16
+        after each add)."""
         packed, sf = payload
-        n = packed.shape[0]
+        n, k = local_ids.shape
         H = self.dw.shape[1]
+        dev = packed.device
+        out = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
         if n == 0:
-            return torch.empty(0, H, dtype=torch.bfloat16, device=packed.device)
+            return out
         E = self.gu.shape[0]
-        r = moe_ops._Route(self.lib, local_ids.reshape(n, 1), weights.reshape(n, 1), E, moe_ops.pick_tile_n(n, E))
+        r = moe_ops._Route(self.lib, local_ids, weights, E, moe_ops.pick_tile_n(max(1, n * k // 2), E))
         c_sorted = moe_ops._nvfp4_expert_rows(self.lib, r, packed, sf, ts, self.gu, self.gu_sf, self.gu_ts,
                                               self.dw, self.dw_sf, self.dw_ts, False)
-        return c_sorted[r.pair_row.to(torch.int64)]
+        A.check(self.lib.aeoq_moe_combine(c_sorted.data_ptr(), r.pair_row.data_ptr(), r.ids.data_ptr(),
+                                          A.dtype_code(r.ids.dtype), n, k, H, 0, out.data_ptr(), A.stream_ptr(dev)))
+        return out
 
-    def combine(self, rows, pair_row, top_k_index, T, k):
+    def fold(self, rows, slot_row, T, world):
+        """out[t] = the partial rows of token t's ranks folded in rank order
+        (bf16 after each add)."""
         H = self.dw.shape[1]
-        dev = pair_row.device
+        dev = slot_row.device
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
-        ids = top_k_index.contiguous()
+        if T == 0:
+            return out
         if rows.shape[0] == 0:
             rows = torch.zeros(1, H, dtype=torch.bfloat16, device=dev)
-        A.check(self.lib.aeoq_moe_combine(rows.contiguous().data_ptr(), pair_row.data_ptr(), ids.data_ptr(),
-                                          A.dtype_code(ids.dtype), T, k, H, 0, out.data_ptr(), A.stream_ptr(dev)))
+        ranks = torch.arange(world, dtype=torch.int32, device=dev).expand(T, world).contiguous()
+        A.check(self.lib.aeoq_moe_combine(rows.contiguous().data_ptr(), slot_row.contiguous().data_ptr(),
+                                          ranks.data_ptr(), A.I32, T, world, H, 0, out.data_ptr(),
+                                          A.stream_ptr(dev)))
         return out
 
 

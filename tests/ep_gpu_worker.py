@@ -1,7 +1,8 @@
 """One rank of the 2-GPU expert-parallel test (NCCL): builds the same
 16-expert NVFP4 layer on every rank, keeps its 8 experts, runs the
 expert-parallel forward on its half of the tokens; rank 0 also runs the
-one-GPU grouped forward over all tokens. Launched by test_ep_gpu.py."""
+one-GPU grouped forward over all tokens and saves the layer and inputs.
+Launched by test_ep_gpu.py."""
 import os
 import sys
 
@@ -50,6 +51,9 @@ def main():
     res = {"y": y.cpu(), "lo": lo, "hi": hi}
     if rank == 0:
         res["ref"] = moe_ops.nvfp4_experts_grouped(hid, ids, w, gp, gs, gt.float(), dp, ds, dt.float()).cpu()
+        res["inputs"] = {"hid": hid.cpu(), "ids": ids.cpu(), "w": w.cpu(),
+                         "weights": [t.cpu() for t in (gp, gs.view(torch.uint8), gt.float(), dp, ds.view(torch.uint8),
+                                                       dt.float())]}
     torch.save(res, out_path)
     dist.barrier()
     dist.destroy_process_group()

@@ -42,11 +42,50 @@ def case_inputs(case):
     return m, hidden, ids, w
 
 
+def pair_outputs(m, hidden, ids, wts, ts=None):
+    """Weighted down output of every valid (token, slot) pair, the one-GPU
+    prefill's per-expert steps (modeling_nvfp4.py:203-249): {(t, j): row}."""
+    hp, hs, hts = OQ.quantize_nvfp4(hidden, "bf16", ts=ts)
+    out = {}
+    for e in np.unique(ids):
+        if e < 0 or e >= m.num_experts:
+            continue
+        pos, tok = np.nonzero(ids.T == e)
+        gu = nvfp4_gemm(hp[tok], hs[tok], hts, m.gate_up_proj[e], m.gate_up_proj_scale[e], m.gate_up_proj_scale_2)
+        d = nvfp4_linear(OM.geglu(gu), m.down_proj[e], m.down_proj_scale[e], m.down_proj_scale_2)
+        d = N.bf16(d * wts[tok, pos][:, None])
+        for i, (t, j) in enumerate(zip(tok, pos)):
+            out[(int(t), int(j))] = d[i]
+    return out
+
+
+def ep_order_reference(m, hidden, ids, wts, owner, world):
+    """The expert-parallel result restated on one process: per token, each
+    owning rank folds its experts' rows (ascending id, bf16 after each add),
+    then the partials are folded in rank order."""
+    pairs = pair_outputs(m, hidden, ids, wts)
+    T, H = hidden.shape[0], m.down_proj.shape[1]
+    out = np.zeros((T, H), np.float32)
+    for t in range(T):
+        acc = np.zeros(H, np.float32)
+        for r in range(world):
+            slots = sorted((int(ids[t, j]), j) for j in range(ids.shape[1])
+                           if 0 <= ids[t, j] < m.num_experts and int(owner[ids[t, j]]) == r)
+            if not slots:
+                continue
+            part = np.zeros(H, np.float32)
+            for _, j in slots:
+                part = N.bf16(part + pairs[(t, j)])
+            acc = N.bf16(acc + part)
+        out[t] = acc
+    return out
+
+
 class OracleEpOps:
     """Oracle arithmetic for ep_moe_forward (the rank's experts only)."""
 
-    def __init__(self, m, first, count):
-        self.m, self.first, self.count = m, first, count
+    def __init__(self, m):
+        self.m = m
 
     def tensor_scale(self, amax, dtype):
         return float(OQ.nvfp4_tensor_scale(np.float32(amax.item()), "bf16"))
@@ -59,27 +98,37 @@ class OracleEpOps:
         p, s = (t.numpy() for t in payload)
         lid = local_ids.numpy()
         w = weights.to(torch.float32).numpy()
+        n, k = lid.shape
         H = self.m.down_proj.shape[1]
-        out = np.zeros((p.shape[0], H), np.float32)
+        rows = {}
         for le in np.unique(lid):
-            rows = np.nonzero(lid == le)[0]
+            if le >= len(my_experts):
+                continue
+            rr, jj = np.nonzero(lid == le)
             e = int(my_experts[le])
-            gu = nvfp4_gemm(p[rows], s[rows], ts, self.m.gate_up_proj[e], self.m.gate_up_proj_scale[e],
+            gu = nvfp4_gemm(p[rr], s[rr], ts, self.m.gate_up_proj[e], self.m.gate_up_proj_scale[e],
                             self.m.gate_up_proj_scale_2)
             d = nvfp4_linear(OM.geglu(gu), self.m.down_proj[e], self.m.down_proj_scale[e], self.m.down_proj_scale_2)
-            out[rows] = N.bf16(d * w[rows][:, None])
+            d = N.bf16(d * w[rr, jj][:, None])
+            for i, (a, b) in enumerate(zip(rr, jj)):
+                rows[(int(a), int(b))] = (le, d[i])
+        out = np.zeros((n, H), np.float32)
+        for a in range(n):
+            part = np.zeros(H, np.float32)
+            for le, d in sorted((v for (a2, _), v in rows.items() if a2 == a), key=lambda x: x[0]):
+                part = N.bf16(part + d)
+            out[a] = part
         return torch.from_numpy(out)
 
-    def combine(self, rows, pair_row, top_k_index, T, k):
+    def fold(self, rows, slot_row, T, world):
         rows = rows.numpy()
-        pr = pair_row.numpy()
-        ids = top_k_index.numpy()
-        out = np.zeros((T, rows.shape[1] if rows.ndim == 2 else self.m.down_proj.shape[1]), np.float32)
+        sr = slot_row.numpy()
+        H = self.m.down_proj.shape[1]
+        out = np.zeros((T, H), np.float32)
         for t in range(T):
-            for j in np.argsort(ids[t], kind="stable"):
-                r = pr[t * k + j]
-                if r >= 0:
-                    out[t] = N.bf16(out[t] + rows[r])
+            for r in range(world):
+                if sr[t, r] >= 0:
+                    out[t] = N.bf16(out[t] + rows[sr[t, r]])
         return torch.from_numpy(out)
 
 
@@ -93,8 +142,7 @@ def main():
     E = m.num_experts
     T = hidden.shape[0]
     lo, hi = rank * T // world, (rank + 1) * T // world
-    e_loc = E // world
-    ops = OracleEpOps(m, rank * e_loc, e_loc)
+    ops = OracleEpOps(m)
     owner = None
     if case == 2:
         load = np.bincount(ids[(ids >= 0) & (ids < E)], minlength=E)
