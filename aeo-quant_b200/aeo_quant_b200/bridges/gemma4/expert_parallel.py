@@ -194,18 +194,20 @@ def ep_moe_forward(hidden, top_k_index, top_k_weights, *, num_experts: int, grou
         my_experts = torch.nonzero(owner == rank).reshape(-1)
     send_tok, send_dest, send_counts, lid = plan_token_dispatch(top_k_index, num_experts, world, owner)
 
-    # counts: one small all-to-all and ONE host read of both split lists
+    # counts: one small all-to-all; everything that does not need the split
+    # sizes on the host (the global scale, the quantized rows in send order,
+    # the metadata) is queued before the one host read of both split lists,
+    # so the device stays busy while the host waits
     recv_counts_t = torch.empty_like(send_counts)
     dist.all_to_all_single(recv_counts_t, send_counts, group=group)
+    ts = ops.tensor_scale(global_amax(hidden, group), hidden.dtype)
+    send_payload = [p[send_tok] for p in ops.encode(hidden, ts)]   # per-token rows, in send order
+    wbits = top_k_weights.to(torch.bfloat16).contiguous().view(torch.int16).to(torch.int32)
+    meta = torch.cat([lid, wbits[send_tok]], dim=1)      # (n_send, 2k) int32
     both = torch.cat([send_counts, recv_counts_t]).tolist()
     sc, rc = both[:world], both[world:]
 
-    ts = ops.tensor_scale(global_amax(hidden, group), hidden.dtype)
-    payload = ops.encode(hidden, ts)                     # per-token row tensors
-    wbits = top_k_weights.to(torch.bfloat16).contiguous().view(torch.int16).to(torch.int32)
-    meta = torch.cat([lid, wbits[send_tok]], dim=1)      # (n_send, 2k) int32
-
-    recv_payload = [_all_to_all_rows(p[send_tok], sc, rc, group) for p in payload]
+    recv_payload = [_all_to_all_rows(p, sc, rc, group) for p in send_payload]
     recv_meta = _all_to_all_rows(meta, sc, rc, group)
     recv_lid = recv_meta[:, :k].contiguous()
     recv_w = recv_meta[:, k:].to(torch.int16).view(torch.bfloat16).contiguous()
