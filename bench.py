@@ -70,7 +70,7 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     p.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM measurements")
     p.add_argument("--no-ep", action="store_true", help="skip the expert-parallel (config 4) leg")
-    p.add_argument("--workload", default="decode", choices=["decode", "ep", "gemm", "stack", "router", "grouped"],
+    p.add_argument("--workload", default="decode", choices=["decode", "ep", "gemm", "stack", "router", "grouped", "quant"],
                    help="decode: config 1 (default); ep: config 4, expert-parallel prefill stack; "
                         "gemm: config-0 NVFP4 linear at --gemm-m rows (profiling)")
     p.add_argument("--gemm-m", type=int, default=32768)
@@ -834,6 +834,12 @@ def main():
         return
     if args.workload == "grouped":
         main_grouped(args, local)
+        return
+    if args.workload == "quant":
+        import torch
+        torch.cuda.set_device(local)
+        print(json.dumps({"metric": "NVFP4 activation quantizer", "quantizer":
+                          measure_quantizer(torch, torch.device("cuda", local))}), flush=True)
         return
     if args.workload == "stack":
         main_stack(args, local)
