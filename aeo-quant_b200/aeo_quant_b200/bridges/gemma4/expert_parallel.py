@@ -172,16 +172,94 @@ def plan_token_dispatch(top_k_index: torch.Tensor, num_experts: int, world: int,
     return send_tok, send_dest, counts, lid.to(torch.int32)
 
 
-def ep_moe_forward(hidden, top_k_index, top_k_weights, *, num_experts: int, group, ops, owner=None, mark=None):
+def plan_dense_dispatch(top_k_index: torch.Tensor, num_experts: int, world: int, owner: torch.Tensor | None = None):
+    """Fixed-layout send plan for ranks that all hold the same number of
+    tokens T: row r * T + t of the send buffer carries token t to rank r
+    whether or not r owns one of its experts, so no split size depends on
+    the routing and nothing is read back to the host.
+
+    Returns ``(local_ids, present)``: (world, T, k) local expert ids on each
+    rank (``E/world``, dropped by the grouped forward, where the slot's
+    expert lives elsewhere or is invalid) and (world, T) whether rank r owns
+    any of token t's experts."""
+    if num_experts % world:
+        raise ValueError(f"num_experts ({num_experts}) must be divisible by the world size ({world})")
+    e_loc = num_experts // world
+    ids = top_k_index.to(torch.int64)
+    dev = ids.device
+    valid = (ids >= 0) & (ids < num_experts)
+    safe = ids.clamp(0, num_experts - 1)
+    if owner is None:
+        dest = torch.div(safe, e_loc, rounding_mode="floor")
+        local = safe - dest * e_loc
+    else:
+        owner = torch.as_tensor(owner, dtype=torch.int64).reshape(-1)
+        dest = owner.to(dev)[safe]
+        local = local_index(owner, world).to(dev)[safe]
+    dest = torch.where(valid, dest, torch.full_like(dest, world))
+    on = dest.unsqueeze(0) == torch.arange(world, device=dev).view(world, 1, 1)       # (world, T, k)
+    lid = torch.where(on, local.unsqueeze(0), torch.full_like(local, e_loc).unsqueeze(0))
+    return lid.to(torch.int32), on.any(-1)
+
+
+def _ep_dense(hidden, top_k_index, top_k_weights, num_experts, group, ops, owner, my_experts, mark):
+    """``ep_moe_forward`` for equal token counts on every rank: fixed-size
+    all-to-alls, no host synchronisation (see ``plan_dense_dispatch``)."""
+    world = dist.get_world_size(group)
+    T, k = top_k_index.shape
+    dev = hidden.device
+    lid, present = plan_dense_dispatch(top_k_index, num_experts, world, owner)
+    ts = ops.tensor_scale(global_amax(hidden, group), hidden.dtype)
+    send_payload = [p.unsqueeze(0).expand(world, *p.shape).reshape(world * T, *p.shape[1:])
+                    for p in ops.encode(hidden, ts)]
+    wbits = top_k_weights.to(torch.bfloat16).contiguous().view(torch.int16).to(torch.int32)
+    meta = torch.cat([lid.reshape(world * T, k), wbits.unsqueeze(0).expand(world, T, k).reshape(world * T, k)], 1)
+    recv_payload = []
+    for p in send_payload:
+        r = torch.empty_like(p)
+        dist.all_to_all_single(r, p, group=group)
+        recv_payload.append(r)
+    recv_meta = torch.empty_like(meta)
+    dist.all_to_all_single(recv_meta, meta, group=group)
+    recv_lid = recv_meta[:, :k].contiguous()
+    recv_w = recv_meta[:, k:].to(torch.int16).view(torch.bfloat16).contiguous()
+    mark("experts")
+    partial = ops.experts(recv_payload, recv_lid, recv_w, ts, my_experts, pairs_hint=T * k)   # (world * T, H)
+
+    mark("combine")
+    back = torch.empty_like(partial)
+    dist.all_to_all_single(back, partial, group=group)   # block r: my tokens as rank r folded them
+    rows = (torch.arange(world, device=dev).view(world, 1) * T + torch.arange(T, device=dev).view(1, T))
+    slot_row = torch.where(present, rows, torch.full_like(rows, -1)).T.to(torch.int32).contiguous()
+    out = ops.fold(back, slot_row, T, world)
+    mark("end")
+    return out
+
+
+def ep_moe_forward(hidden, top_k_index, top_k_weights, *, num_experts: int, group, ops, owner=None, mark=None,
+                   equal_tokens: bool = False):
     """One expert-parallel MoE layer over ``group`` (see module docstring).
     ``owner``: optional placement (E,) of experts on ranks. ``mark``: optional
     callable taking a phase name ("dispatch", "experts", "combine", "end"),
     called where each phase starts (a profiler hook, e.g. recording CUDA
-    events)."""
+    events). ``equal_tokens``: every rank passes the same number of tokens
+    (sequence-sharded prefill); the layer then uses fixed-size all-to-alls
+    and never synchronises with the host. Otherwise each layer reads the
+    split sizes back once."""
     if mark is None:
         def mark(_):
             return None
     mark("dispatch")
+    if equal_tokens:
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        if owner is None:
+            e_loc = num_experts // world
+            my_experts = torch.arange(rank * e_loc, (rank + 1) * e_loc)
+        else:
+            owner = torch.as_tensor(owner, dtype=torch.int64).reshape(-1).cpu()
+            my_experts = torch.nonzero(owner == rank).reshape(-1)
+        return _ep_dense(hidden, top_k_index, top_k_weights, num_experts, group, ops, owner, my_experts, mark)
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     e_loc = num_experts // world
@@ -212,7 +290,7 @@ def ep_moe_forward(hidden, top_k_index, top_k_weights, *, num_experts: int, grou
     recv_lid = recv_meta[:, :k].contiguous()
     recv_w = recv_meta[:, k:].to(torch.int16).view(torch.bfloat16).contiguous()
     mark("experts")
-    partial = ops.experts(recv_payload, recv_lid, recv_w, ts, my_experts)   # (n_recv, H), one row per token
+    partial = ops.experts(recv_payload, recv_lid, recv_w, ts, my_experts, pairs_hint=T * k)   # (n_recv, H)
 
     mark("combine")
     back = _all_to_all_rows(partial, rc, sc, group)      # in this rank's send order
@@ -240,10 +318,12 @@ class NVFP4EpOps:
         packed, sf, _ = _nvfp4_quantize_rows(hidden.contiguous(), ts)
         return [packed, sf.view(torch.uint8)]
 
-    def experts(self, payload, local_ids, weights, ts, my_experts):
+    def experts(self, payload, local_ids, weights, ts, my_experts, pairs_hint=None):
         """Grouped forward of the received tokens over this rank's experts,
         then each token's weighted outputs folded (ascending expert id, bf16
-        after each add)."""
+        after each add). ``pairs_hint``: the expected number of valid
+        (token, expert) pairs, which picks the token-tile width (any width
+        gives the same bits)."""
         packed, sf = payload
         n, k = local_ids.shape
         H = self.dw.shape[1]
@@ -252,7 +332,8 @@ class NVFP4EpOps:
         if n == 0:
             return out
         E = self.gu.shape[0]
-        r = moe_ops._Route(self.lib, local_ids, weights, E, moe_ops.pick_tile_n(max(1, n * k // 2), E))
+        hint = pairs_hint if pairs_hint is not None else n * k // 2
+        r = moe_ops._Route(self.lib, local_ids, weights, E, moe_ops.pick_tile_n(max(1, hint), E))
         c_sorted = moe_ops._nvfp4_expert_rows(self.lib, r, packed, sf, ts, self.gu, self.gu_sf, self.gu_ts,
                                               self.dw, self.dw_sf, self.dw_ts, False)
         A.check(self.lib.aeoq_moe_combine(c_sorted.data_ptr(), r.pair_row.data_ptr(), r.ids.data_ptr(),
@@ -282,15 +363,18 @@ class ExpertParallelNVFP4(torch.nn.Module):
     Holds experts [rank * E/world, (rank+1) * E/world), or with ``owner``
     the experts e with owner[e] == rank in ascending id order, with the
     reference's buffer names (first dimension E/world); ``forward`` takes
-    this rank's tokens and returns their outputs."""
+    this rank's tokens and returns their outputs. With ``equal_tokens`` every
+    rank must pass the same number of tokens, and the layer runs without a
+    host synchronisation (fixed-size all-to-alls)."""
 
-    def __init__(self, local_experts, num_experts: int, group=None, owner=None):
+    def __init__(self, local_experts, num_experts: int, group=None, owner=None, equal_tokens: bool = False):
         super().__init__()
         self.local = local_experts
         self.num_experts = num_experts
         self.group = group
         self.owner = None if owner is None else torch.as_tensor(owner, dtype=torch.int64).reshape(-1).cpu()
         self.mark = None   # optional phase hook passed to ep_moe_forward
+        self.equal_tokens = equal_tokens
 
     def forward(self, hidden_states, top_k_index, top_k_weights):
         m = self.local
@@ -299,4 +383,5 @@ class ExpertParallelNVFP4(torch.nn.Module):
         ops = NVFP4EpOps(m.gate_up_proj, m.gate_up_proj_scale, m.gate_up_proj_scale_2,
                          m.down_proj, m.down_proj_scale, m.down_proj_scale_2)
         return ep_moe_forward(hidden_states, top_k_index, top_k_weights, num_experts=self.num_experts,
-                              group=self.group, ops=ops, owner=self.owner, mark=self.mark)
+                              group=self.group, ops=ops, owner=self.owner, mark=self.mark,
+                              equal_tokens=self.equal_tokens)

@@ -427,7 +427,7 @@ def ep_layers(torch, dev, rank, world, n_layers, owner):
         del wgu, wd
         m.gate_up_proj.copy_(gp); m.gate_up_proj_scale.copy_(gs); m.gate_up_proj_scale_2.copy_(gt.float())
         m.down_proj.copy_(dp); m.down_proj_scale.copy_(ds); m.down_proj_scale_2.copy_(dt.float())
-        layers.append(ExpertParallelNVFP4(m, E, owner=owner) if owner is not None else m)
+        layers.append(ExpertParallelNVFP4(m, E, owner=owner, equal_tokens=True) if owner is not None else m)
     return layers
 
 

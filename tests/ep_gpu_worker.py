@@ -48,7 +48,9 @@ def main():
     ep = ExpertParallelNVFP4(m, E)
     lo, hi = rank * T // world, (rank + 1) * T // world
     y = ep(hid[lo:hi], ids[lo:hi], w[lo:hi])
-    res = {"y": y.cpu(), "lo": lo, "hi": hi}
+    ep.equal_tokens = True                                 # fixed-size all-to-alls, no host sync
+    y_dense = ep(hid[lo:hi], ids[lo:hi], w[lo:hi])
+    res = {"y": y.cpu(), "y_dense": y_dense.cpu(), "lo": lo, "hi": hi}
     if rank == 0:
         res["ref"] = moe_ops.nvfp4_experts_grouped(hid, ids, w, gp, gs, gt.float(), dp, ds, dt.float()).cpu()
         res["inputs"] = {"hid": hid.cpu(), "ids": ids.cpu(), "w": w.cpu(),

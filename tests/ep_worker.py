@@ -94,7 +94,7 @@ class OracleEpOps:
         p, s, _ = OQ.quantize_nvfp4(hidden.to(torch.float32).numpy(), "bf16", ts=ts)
         return [torch.from_numpy(p), torch.from_numpy(s)]
 
-    def experts(self, payload, local_ids, weights, ts, my_experts):
+    def experts(self, payload, local_ids, weights, ts, my_experts, pairs_hint=None):
         p, s = (t.numpy() for t in payload)
         lid = local_ids.numpy()
         w = weights.to(torch.float32).numpy()
@@ -134,6 +134,7 @@ class OracleEpOps:
 
 def main():
     rank, world, port, out_path, case = int(sys.argv[1]), int(sys.argv[2]), sys.argv[3], sys.argv[4], int(sys.argv[5])
+    dense = len(sys.argv) > 6 and sys.argv[6] == "dense"
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = port
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -149,7 +150,7 @@ def main():
         owner = balanced_placement(torch.from_numpy(load), world)
     y = ep_moe_forward(torch.from_numpy(hidden[lo:hi]).to(torch.bfloat16), torch.from_numpy(ids[lo:hi]),
                        torch.from_numpy(w[lo:hi]).to(torch.bfloat16), num_experts=E, group=None, ops=ops,
-                       owner=owner)
+                       owner=owner, equal_tokens=dense)
     np.savez(out_path, y=y.numpy(), lo=lo, hi=hi)
     dist.destroy_process_group()
 

@@ -24,14 +24,15 @@ def _free_port():
         return str(s.getsockname()[1])
 
 
-@pytest.mark.parametrize("case", [0, 1, 2, 3])
-def test_ep_two_ranks_match_one_process(tmp_path, case):
+@pytest.mark.parametrize("case,mode", [(0, "compact"), (1, "compact"), (2, "compact"), (3, "compact"),
+                                       (0, "dense"), (2, "dense")])
+def test_ep_two_ranks_match_one_process(tmp_path, case, mode):
     sys.path.insert(0, HERE)
     from ep_worker import case_inputs
     world, port = 2, _free_port()
     outs = [str(tmp_path / f"r{r}.npz") for r in range(world)]
     procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "ep_worker.py"), str(r), str(world), port,
-                               outs[r], str(case)], stdout=subprocess.PIPE, stderr=subprocess.STDOUT)
+                               outs[r], str(case), mode], stdout=subprocess.PIPE, stderr=subprocess.STDOUT)
              for r in range(world)]
     logs = []
     for p in procs:
