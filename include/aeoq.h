@@ -367,7 +367,8 @@ AEOQ_API int aeoq_moe_nvfp4_decode_tc(const void* hidden, const void* top_k_inde
 
 /* ------------------------------------------------------------------------
  * One-token NVFP4 MoE expert forward streamed through ONE cooperative
- * launch (the default one-token path). Same math, rounding points and
+ * launch (the module's one-token path where the tensor-core pair does not
+ * cover the shape). Same math, rounding points and
  * arguments as aeoq_moe_nvfp4_decode (replaces the same reference function,
  * modeling_nvfp4.py:132-186) plus an error word. Work is split across the
  * SMs by bytes; each CTA requests every weight, scale and down row it needs
