@@ -119,7 +119,8 @@ struct TcLayout {
   static constexpr int kStages = (int)(kBudget / kStage) < kTcMaxStages ? (int)(kBudget / kStage) : kTcMaxStages;
   // The epilogue reuses the stage ring, idle once the accumulator is
   // complete, for the GeGLU exchange of the up half (64 x BN f32).
-  static constexpr size_t kXchg = 64 * (size_t)BN * 4;
+  // row pitch BN + 1 words: the 32 lanes of a warp (32 rows) hit 32 banks
+  static constexpr size_t kXchg = 64 * (size_t)(BN + 1) * 4;
   static_assert(kXchg <= kStages * kStage, "the GeGLU exchange must fit in the stage ring");
   static constexpr size_t kBytes = 1024 + kStages * kStage + sizeof(TcSmem) + 64;
   static constexpr uint32_t kTmemCols =
@@ -457,7 +458,7 @@ __global__ void __launch_bounds__(kTcThreads, (BN <= 128) ? 2 : 1) nvfp4_tc_gemm
           float v[kChunk < 16 ? 16 : kChunk];
           tmem_chunk<kChunk>(tq + (uint32_t)c0, v);
 #pragma unroll
-          for (int j = 0; j < kChunk; ++j) xchg[(row - 64) * BN + c0 + j] = bf16r(scaled(v[j], c0 + j));
+          for (int j = 0; j < kChunk; ++j) xchg[(row - 64) * (BN + 1) + c0 + j] = bf16r(scaled(v[j], c0 + j));
         }
       }
       asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
@@ -475,7 +476,7 @@ __global__ void __launch_bounds__(kTcThreads, (BN <= 128) ? 2 : 1) nvfp4_tc_gemm
               float hvf = 0.0f;
               if (t < ti.n_valid) {
                 const float gv = bf16r(scaled(v[g8 + j], t));
-                const float u = xchg[row * BN + t];
+                const float u = xchg[row * (BN + 1) + t];
                 const __nv_bfloat16 hv = __float2bfloat16_rn(bf16r(gelu_tanh(gv)) * u);
                 hkey = max(hkey, In<AEOQ_BF16>::abs_key(hv));
                 hvf = __bfloat162float(hv);
@@ -525,11 +526,15 @@ struct PLayout {
   static constexpr size_t kSfa = kF8 ? 0 : 4 * 512;
   static constexpr size_t kSfb = kF8 ? 0 : (size_t)4 * 512 * kSfbAtoms;
   static constexpr size_t kStage = kA + kB + kSfa + kSfb;
-  static constexpr size_t kXchg = 64 * (size_t)BN * 2;   // GeGLU up half, bf16
+  // GeGLU up half, bf16, row pitch BN + 2 (an odd number of words: the 32
+  // lanes of a warp, 32 rows, hit 32 banks)
+  static constexpr int kXs = BN + 2;
+  static constexpr size_t kXchg = 64 * (size_t)kXs * 2;
   struct Smem {
     uint64_t full[kTcMaxStages], empty[kTcMaxStages], acc_full[2], acc_empty[2];
     uint32_t tmem_base;
     float colscale[256];
+    float roww[256];       // kEpiScaleRow: the tile's per-row weights
     // grouped mode: the expert tile and row offsets, so every role resolves
     // a tile from shared memory instead of a chain of dependent L2 loads
     int tile_off[kPMaxExperts + 1];
@@ -732,11 +737,17 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
         alpha = p.sb_rows[ti.expert * p.n_out + wrow];
         for (int c = tid - 128; c < BN; c += 32 * kPEpiWarps)
           colscale[c] = c < ti.n_valid ? p.sa_rows[ti.b_row0 + c] : 0.0f;
-        asm volatile("bar.sync 1, %0;" ::"n"(32 * kPEpiWarps) : "memory");
       } else {
         if (p.epi == kEpiScaleRow) alpha = p.grp_alpha_ts[ti.expert] * load_scalar_f(p.w_ts, p.w_ts_dt);
         else alpha = load_scalar_f(p.a_ts, p.a_ts_dt) * load_scalar_f(p.w_ts, p.w_ts_dt);
       }
+      // the tile's row weights in shared memory: one load per row, not one
+      // per (row, output column)
+      float* roww = sh->roww;
+      if (p.epi == kEpiScaleRow)
+        for (int c = tid - 128; c < BN; c += 32 * kPEpiWarps)
+          roww[c] = c < ti.n_valid ? __bfloat162float(p.row_w[ti.c_row0 + c]) : 0.0f;
+      if (kF8 || p.epi == kEpiScaleRow) asm volatile("bar.sync 1, %0;" ::"n"(32 * kPEpiWarps) : "memory");
       auto scaled = [&](float acc, int c) { return kF8 ? (acc * colscale[c]) * alpha : acc * alpha; };
       const bool ok = sm100::mbar_wait(&sh->acc_full[b], accp, p.err, 64);
       sm100::tc_fence_after();
@@ -758,7 +769,7 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
             for (int j = 0; j < 8; ++j) {
               const int c = t0 + j;
               float val = (c < ti.n_valid) ? scaled(v[g8 + j], c) : 0.0f;
-              if (p.epi == kEpiScaleRow && c < ti.n_valid) val = bf16r(val) * __bfloat162float(p.row_w[ti.c_row0 + c]);
+              if (p.epi == kEpiScaleRow && c < ti.n_valid) val = bf16r(val) * roww[c];
               y[j] = val;
             }
             if (!ok) continue;
@@ -781,7 +792,7 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
             tmem_chunk<kChunk>(tq + (uint32_t)c0, v);
 #pragma unroll
             for (int j = 0; j < kChunk; ++j)
-              if (c0 + j < tend) xchg[(row - 64) * BN + c0 + j] = __float2bfloat16_rn(scaled(v[j], c0 + j));
+              if (c0 + j < tend) xchg[(row - 64) * L::kXs + c0 + j] = __float2bfloat16_rn(scaled(v[j], c0 + j));
           }
           sm100::tc_fence_before();
           __syncwarp();
@@ -803,7 +814,7 @@ __global__ void __launch_bounds__(kPThreads, 1) tc_gemm_persistent_kernel(const 
                 float hvf = 0.0f;
                 if (c < ti.n_valid) {
                   const float gv = bf16r(scaled(v[g8 + j], c));
-                  const float u = __bfloat162float(xchg[row * BN + c]);
+                  const float u = __bfloat162float(xchg[row * L::kXs + c]);
                   const __nv_bfloat16 hv = __float2bfloat16_rn(bf16r(gelu_tanh(gv)) * u);
                   hkey = max(hkey, In<AEOQ_BF16>::abs_key(hv));
                   hvf = __bfloat162float(hv);
