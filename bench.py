@@ -493,24 +493,29 @@ def run_ep(args, rank, world, local, steps, warmup):
         ms = timed(lambda: step(hid), steps)
     phases = None
     if world > 1:
-        # phase split of one instrumented step (CUDA events at each phase start)
-        evs = []
+        # phase split: CUDA events at each phase start (device-timeline gaps,
+        # so idle time waiting on the host counts in the phase it delays);
+        # the per-phase median of three instrumented steps
+        runs = []
+        for _ in range(3):
+            evs = []
 
-        def mark(name):
-            ev = torch.cuda.Event(enable_timing=True)
-            ev.record()
-            evs.append((name, ev))
-        for lay in layers:
-            lay.mark = mark
-        step(hid)
-        torch.cuda.synchronize()
-        for lay in layers:
-            lay.mark = None
-        acc = {"dispatch": 0.0, "experts": 0.0, "combine": 0.0}
-        for (n0, a), (_, b) in zip(evs, evs[1:]):
-            if n0 in acc:
-                acc[n0] += a.elapsed_time(b)
-        ph = torch.tensor([acc["dispatch"], acc["experts"], acc["combine"]], device=dev)
+            def mark(name, evs=evs):
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                evs.append((name, ev))
+            for lay in layers:
+                lay.mark = mark
+            step(hid)
+            torch.cuda.synchronize()
+            for lay in layers:
+                lay.mark = None
+            acc = {"dispatch": 0.0, "experts": 0.0, "combine": 0.0}
+            for (n0, a), (_, b) in zip(evs, evs[1:]):
+                if n0 in acc:
+                    acc[n0] += a.elapsed_time(b)
+            runs.append([acc["dispatch"], acc["experts"], acc["combine"]])
+        ph = torch.tensor(runs, device=dev).median(dim=0).values
         dist.all_reduce(ph, op=dist.ReduceOp.MAX)
         phases = dict(zip(("dispatch", "experts", "combine"), [round(v, 3) for v in ph.tolist()]))
     # e2e: this rank's tokens from pinned host memory, the output back
