@@ -210,14 +210,15 @@ def _ep_dense(hidden, top_k_index, top_k_weights, num_experts, group, ops, owner
     dev = hidden.device
     lid, present = plan_dense_dispatch(top_k_index, num_experts, world, owner)
     ts = ops.tensor_scale(global_amax(hidden, group), hidden.dtype)
-    send_payload = [p.unsqueeze(0).expand(world, *p.shape).reshape(world * T, *p.shape[1:])
-                    for p in ops.encode(hidden, ts)]
     wbits = top_k_weights.to(torch.bfloat16).contiguous().view(torch.int16).to(torch.int32)
     meta = torch.cat([lid.reshape(world * T, k), wbits.unsqueeze(0).expand(world, T, k).reshape(world * T, k)], 1)
+    # every rank receives every rank's quantized rows (block r = rank r's
+    # tokens): an all-gather, with no per-destination copy of the payload
     recv_payload = []
-    for p in send_payload:
-        r = torch.empty_like(p)
-        dist.all_to_all_single(r, p, group=group)
+    for p in ops.encode(hidden, ts):
+        p = p.contiguous()
+        r = torch.empty((world * T, *p.shape[1:]), dtype=p.dtype, device=dev)
+        dist.all_gather_into_tensor(r, p, group=group)
         recv_payload.append(r)
     recv_meta = torch.empty_like(meta)
     dist.all_to_all_single(recv_meta, meta, group=group)
