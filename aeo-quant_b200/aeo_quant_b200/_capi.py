@@ -73,7 +73,20 @@ _SIGS["aeoq_moe_combine"] = [_P, _P, _P, _I, _L, _L, _L, _I, _P, _P]
 _SIGS["aeoq_nvfp4_gemm_tc"] = [_P, _P, _P, _I, _L, _P, _P, _P, _I, _L, _P, _I, _L, _L, _L, _L, _I, _P, _I, _P, _P]
 _SIGS["aeoq_moe_nvfp4_decode_fused_noalloc"] = [_P, _P, _I, _P, _L, _P, _P, _P, _I, _P, _P, _P, _I, _L, _L, _L,
                                                 _P, _P]
+_SIGS["aeoq_ep_nccl_unique_id_bytes"] = []
+_SIGS["aeoq_ep_nccl_unique_id"] = [_P, _Z]
+_SIGS["aeoq_ep_nccl_comm_init"] = [_P, _I, _I, _P]
+_SIGS["aeoq_ep_nccl_comm_destroy"] = [_P]
+_SIGS["aeoq_ep_dispatch_workspace_size"] = [_I, _L, _L, _L]
+_SIGS["aeoq_ep_dispatch"] = [_P, _I, _I, _P, _L, _L, _P, _I, _P, _L, _L, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P]
+_SIGS["aeoq_ep_experts_nvfp4_workspace_size"] = [_L, _L, _L, _L, _L, _L]
+_SIGS["aeoq_ep_experts_nvfp4"] = [_P, _P, _P, _L, _P, _P, _L, _L, _P, _P, _P, _I, _P, _P, _P, _I, _L, _L, _L, _P, _P,
+                                  _Z, _P, _P]
+_SIGS["aeoq_ep_combine_workspace_size"] = [_I, _L, _L]
+_SIGS["aeoq_ep_combine"] = [_P, _I, _I, _P, _P, _L, _L, _P, _P, _Z, _P]
 _RESTYPE = {"aeoq_moe_nvfp4_decode_tc_workspace_size": C.c_size_t,
+            "aeoq_ep_nccl_unique_id_bytes": C.c_size_t, "aeoq_ep_dispatch_workspace_size": C.c_size_t,
+            "aeoq_ep_experts_nvfp4_workspace_size": C.c_size_t, "aeoq_ep_combine_workspace_size": C.c_size_t,
             "aeoq_moe_nvfp4_decode_stream_workspace_size": C.c_size_t,
             "aeoq_nvfp4_weight_atoms_size": C.c_size_t, "aeoq_nvfp4_act_atoms_size": C.c_size_t,
             "aeoq_last_error": C.c_char_p, "aeoq_nvfp4_quantize_workspace_size": C.c_size_t,

@@ -96,6 +96,25 @@ Nvfp4Bufs carve_nvfp4(Carver& c, int64_t T, int64_t k, int64_t E, int64_t H, int
   return b;
 }
 
+// The buffers of the grouped pipeline over rows that arrive already
+// quantized (the expert-parallel experts step): the same as carve_nvfp4
+// without the activation quantizer's.
+Nvfp4Bufs carve_nvfp4_rows(Carver& c, int64_t n, int64_t k, int64_t E, int64_t H, int64_t I, int tile_n) {
+  const int64_t P = n * k;
+  const int64_t max_tiles = (P + tile_n - 1) / tile_n + E;
+  Nvfp4Bufs b{};
+  b.r = carve_route(c, P, E);
+  b.a_sorted = c.take<uint8_t>((size_t)P * H / 2);
+  b.a_sorted_sf = c.take<uint8_t>(aeoq_nvfp4_act_atoms_size(max_tiles, H, tile_n));
+  b.amax = c.take<uint32_t>(4 * E);
+  b.h_sorted = c.take<__nv_bfloat16>((size_t)P * I * 2);
+  b.hq = c.take<uint8_t>((size_t)P * I / 2);
+  b.hq_sf = c.take<uint8_t>(aeoq_nvfp4_act_atoms_size(max_tiles, I, tile_n));
+  b.ts_e = c.take<float>(4 * E);
+  b.c_sorted = c.take<__nv_bfloat16>((size_t)P * H * 2);
+  return b;
+}
+
 struct Fp8Bufs {
   RouteBufs r;
   uint8_t *xq, *hq;
@@ -224,4 +243,59 @@ extern "C" int aeoq_moe_fp8_forward(const void* hidden, int64_t T, const void* t
   AEOQ_TRY(aeoq_fp8_gemm_grouped(b.hq, b.sh, P, b.r.grp_off, b.r.tile_off, tile_n, down, down_scale, E, H, I, 2,
                                  b.r.row_w, b.c, H * 2, err_word, stream));
   return aeoq_moe_combine(b.c, b.r.pair_row, top_k_index, idx_dtype, T, k, H, 0, out, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Expert-parallel experts step: the grouped forward of rows that arrived
+// NVFP4-quantized (aeoq_ep_dispatch) over this rank's experts, each row's
+// local experts folded in ascending id with bf16 rounding after every add.
+// The launch sequence of NVFP4EpOps.experts
+// (aeo_quant_b200/bridges/gemma4/expert_parallel.py).
+// ---------------------------------------------------------------------------
+extern "C" size_t aeoq_ep_experts_nvfp4_workspace_size(int64_t n_rows, int64_t top_k, int64_t pairs_hint,
+                                                       int64_t local_experts, int64_t hidden, int64_t inter) {
+  if (n_rows <= 0 || top_k <= 0 || local_experts <= 0 || hidden <= 0 || inter <= 0) return 0;
+  Carver c(nullptr);
+  carve_nvfp4_rows(c, n_rows, top_k, local_experts, hidden, inter,
+                   pick_tile_n(pairs_hint > 0 ? pairs_hint : n_rows * top_k / 2, local_experts));
+  return c.off;
+}
+
+extern "C" int aeoq_ep_experts_nvfp4(const uint8_t* packed, const uint8_t* sf, const void* ts, int64_t n_rows,
+                                     const int32_t* local_ids, const void* weights, int64_t top_k,
+                                     int64_t pairs_hint, const uint8_t* gate_up, const uint8_t* gate_up_atoms,
+                                     const void* gate_up_ts, int gate_up_ts_dtype, const uint8_t* down,
+                                     const uint8_t* down_atoms, const void* down_ts, int down_ts_dtype,
+                                     int64_t local_experts, int64_t hidden_size, int64_t inter, void* out,
+                                     void* workspace, size_t workspace_bytes, int* err_word, void* stream) {
+  const int64_t E = local_experts, H = hidden_size, I = inter, k = top_k, n = n_rows;
+  AEOQ_TRY(check_shape(n, k, E, H, I, "ep_experts_nvfp4"));
+  if (n == 0) return AEOQ_OK;
+  AEOQ_REQUIRE(packed && sf && ts && local_ids && weights && gate_up && gate_up_atoms && gate_up_ts && down &&
+                   down_atoms && down_ts && out && err_word,
+               AEOQ_ERR_INVALID, "ep_experts_nvfp4: null pointer");
+  const size_t need = aeoq_ep_experts_nvfp4_workspace_size(n, k, pairs_hint, E, H, I);
+  AEOQ_REQUIRE(workspace && workspace_bytes >= need, AEOQ_ERR_WORKSPACE,
+               "ep_experts_nvfp4: workspace of %zu bytes, %zu needed", workspace_bytes, need);
+  AEOQ_REQUIRE((uintptr_t)workspace % 256 == 0, AEOQ_ERR_INVALID, "ep_experts_nvfp4: workspace not 256-byte aligned");
+  const int64_t P = n * k;
+  const int tile_n = pick_tile_n(pairs_hint > 0 ? pairs_hint : P / 2, E);
+  Carver c(workspace);
+  const Nvfp4Bufs b = carve_nvfp4_rows(c, n, k, E, H, I, tile_n);
+  const int* n_rows_dev = b.r.grp_off + E;
+  cudaStream_t st = (cudaStream_t)stream;
+  AEOQ_TRY(aeoq_moe_route(local_ids, AEOQ_I32, weights, n, k, E, tile_n, b.r.cnt, b.r.fill, b.r.grp_off, b.r.tile_off,
+                          b.r.pair_row, b.r.row_tok, b.r.row_w, b.r.row_exp, stream));
+  AEOQ_TRY(aeoq_gather_rows(packed, sf, b.r.row_tok, b.r.row_exp, b.r.grp_off, b.r.tile_off, tile_n, n_rows_dev, P,
+                            H / 2, H / 16, b.a_sorted, b.a_sorted_sf, stream));
+  if (cudaMemsetAsync(b.amax, 0, sizeof(uint32_t) * E, st) != cudaSuccess) return check_launch("ep_experts_nvfp4");
+  AEOQ_TRY(aeoq_nvfp4_gemm_grouped(b.a_sorted, b.a_sorted_sf, P, b.r.grp_off, b.r.tile_off, tile_n, gate_up,
+                                   gate_up_atoms, E, 2 * I, H, 1, ts, AEOQ_BF16, gate_up_ts, gate_up_ts_dtype,
+                                   nullptr, nullptr, b.amax, b.h_sorted, I * 2, err_word, stream));
+  AEOQ_TRY(aeoq_requant_rows(b.h_sorted, I, b.r.row_exp, b.r.grp_off, b.r.tile_off, tile_n, n_rows_dev, P, b.amax, E,
+                             0, b.hq, b.hq_sf, b.ts_e, stream));
+  AEOQ_TRY(aeoq_nvfp4_gemm_grouped(b.hq, b.hq_sf, P, b.r.grp_off, b.r.tile_off, tile_n, down, down_atoms, E, H, I, 2,
+                                   nullptr, 0, down_ts, down_ts_dtype, b.ts_e, b.r.row_w, nullptr, b.c_sorted, H * 2,
+                                   err_word, stream));
+  return aeoq_moe_combine(b.c_sorted, b.r.pair_row, local_ids, AEOQ_I32, n, k, H, 0, out, stream);
 }

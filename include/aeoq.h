@@ -278,6 +278,58 @@ AEOQ_API int aeoq_moe_fp8_forward(const void* hidden, int64_t T, const void* top
                                   void* workspace, size_t workspace_bytes, int* err_word, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Expert-parallel NVFP4 layer over NCCL (config 4), one rank per GPU, every
+ * rank with the same T tokens (sequence-sharded prefill). Replaces, for a
+ * host without Python, the layer's three phases in
+ * aeo_quant_b200/bridges/gemma4/expert_parallel.py (_ep_dense); the
+ * reference runs its experts on one GPU (modeling_nvfp4.py:188-255), and
+ * this layer's output is within the bf16 re-association of the rank fold
+ * of that forward (bit-identical to the Python layer).
+ *
+ *   aeoq_ep_dispatch        (comm, ...) -> recv_packed (world*T, H/2) u8,
+ *                           recv_sf (world*T, H/16) e4m3 rows,
+ *                           recv_local_ids (world*T, k) i32,
+ *                           recv_weights (world*T, k) bf16, ts_out bf16 0-d,
+ *                           slot_row (T, world) i32 for the combine
+ *   aeoq_ep_experts_nvfp4   the received rows through this rank's E/world
+ *                           experts (weights of those experts only, scale
+ *                           atoms as for aeoq_moe_nvfp4_forward; pairs_hint
+ *                           = T*k picks the tile width, any gives the same
+ *                           bits) -> out (world*T, H) bf16
+ *   aeoq_ep_combine         those rows back to their home ranks and each
+ *                           token's partials folded in rank order -> out (T, H)
+ *
+ * comm is an ncclComm_t: the host's own, or one from aeoq_ep_nccl_comm_init
+ * (unique id from aeoq_ep_nccl_unique_id on one rank, passed to the others
+ * by the host). placement: null = experts [r*E/world, (r+1)*E/world) on rank
+ * r; else device int32 [2E]: owner rank of expert e, then its index among
+ * that rank's experts (ascending id). libnccl.so.2 is opened at the first
+ * call; AEOQ_ERR_UNSUPPORTED if it is absent. Workspaces 256-byte aligned.
+ * ------------------------------------------------------------------------ */
+AEOQ_API size_t aeoq_ep_nccl_unique_id_bytes(void);
+AEOQ_API int aeoq_ep_nccl_unique_id(void* out, size_t out_bytes);
+AEOQ_API int aeoq_ep_nccl_comm_init(void** comm, int world, int rank, const void* unique_id);
+AEOQ_API int aeoq_ep_nccl_comm_destroy(void* comm);
+AEOQ_API size_t aeoq_ep_dispatch_workspace_size(int world, int64_t T, int64_t top_k, int64_t hidden);
+AEOQ_API int aeoq_ep_dispatch(void* comm, int world, int rank, const void* hidden, int64_t T, int64_t H,
+                              const void* top_k_index, int idx_dtype, const void* top_k_weights, int64_t top_k,
+                              int64_t num_experts, const int32_t* placement, uint8_t* recv_packed, uint8_t* recv_sf,
+                              int32_t* recv_local_ids, void* recv_weights, void* ts_out, int32_t* slot_row,
+                              void* workspace, size_t workspace_bytes, void* stream);
+AEOQ_API size_t aeoq_ep_experts_nvfp4_workspace_size(int64_t n_rows, int64_t top_k, int64_t pairs_hint,
+                                                     int64_t local_experts, int64_t hidden, int64_t inter);
+AEOQ_API int aeoq_ep_experts_nvfp4(const uint8_t* packed, const uint8_t* sf, const void* ts, int64_t n_rows,
+                                   const int32_t* local_ids, const void* weights, int64_t top_k, int64_t pairs_hint,
+                                   const uint8_t* gate_up, const uint8_t* gate_up_atoms, const void* gate_up_ts,
+                                   int gate_up_ts_dtype, const uint8_t* down, const uint8_t* down_atoms,
+                                   const void* down_ts, int down_ts_dtype, int64_t local_experts, int64_t hidden_size,
+                                   int64_t inter, void* out, void* workspace, size_t workspace_bytes, int* err_word,
+                                   void* stream);
+AEOQ_API size_t aeoq_ep_combine_workspace_size(int world, int64_t T, int64_t hidden);
+AEOQ_API int aeoq_ep_combine(void* comm, int world, int rank, const void* rows, const int32_t* slot_row, int64_t T,
+                             int64_t H, void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * One-token NVFP4 MoE expert forward, fully fused (two launches).
  * Replaces Gemma4TextExpertsNVFP4._forward_decode_3d
  * (src/aeo_quant/bridges/gemma4/modeling_nvfp4.py:132-186): hidden quant ->

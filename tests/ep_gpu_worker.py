@@ -17,6 +17,60 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 
+def capi_layer(m, x, ids, w, E):
+    """The same layer through the C ABI only: aeoq_ep_dispatch ->
+    aeoq_ep_experts_nvfp4 -> aeoq_ep_combine over a communicator made by
+    aeoq_ep_nccl_comm_init (the unique id travels over the process group, as
+    a host would pass it)."""
+    import ctypes
+    from aeo_quant_b200 import _capi as A
+    lib = A.load()
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = x.device
+    n_id = lib.aeoq_ep_nccl_unique_id_bytes()
+    buf = ctypes.create_string_buffer(n_id)
+    if rank == 0:
+        A.check(lib.aeoq_ep_nccl_unique_id(buf, n_id))
+    uid = torch.frombuffer(bytearray(buf.raw), dtype=torch.uint8).to(dev)
+    dist.broadcast(uid, 0)
+    uid_host = ctypes.create_string_buffer(bytes(uid.cpu().numpy().tobytes()), n_id)
+    comm = ctypes.c_void_p()
+    A.check(lib.aeoq_ep_nccl_comm_init(ctypes.byref(comm), world, rank, uid_host))
+    T, H = x.shape
+    k = ids.shape[1]
+    I = m.down_proj.shape[2] * 2
+    e_loc = m.gate_up_proj.shape[0]
+    x, ids, w = x.contiguous(), ids.contiguous(), w.to(torch.bfloat16).contiguous()
+    u8, i32 = dict(dtype=torch.uint8, device=dev), dict(dtype=torch.int32, device=dev)
+    n = world * T
+    rp, rs = torch.empty(n, H // 2, **u8), torch.empty(n, H // 16, **u8)
+    rl, rw = torch.empty(n, k, **i32), torch.empty(n, k, dtype=torch.bfloat16, device=dev)
+    ts = torch.empty((), dtype=torch.bfloat16, device=dev)
+    slot_row = torch.empty(T, world, **i32)
+    st = A.stream_ptr(dev)
+    ws = torch.empty(lib.aeoq_ep_dispatch_workspace_size(world, T, k, H), **u8)
+    A.check(lib.aeoq_ep_dispatch(comm, world, rank, x.data_ptr(), T, H, ids.data_ptr(), A.dtype_code(ids.dtype),
+                                 w.data_ptr(), k, E, None, rp.data_ptr(), rs.data_ptr(), rl.data_ptr(), rw.data_ptr(),
+                                 ts.data_ptr(), slot_row.data_ptr(), ws.data_ptr(), ws.numel(), st))
+    gu_atoms = A.weight_atoms(m.gate_up_proj_scale, e_loc, 2 * I, H, geglu_inter=I)
+    dw_atoms = A.weight_atoms(m.down_proj_scale, e_loc, H, I)
+    rows = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+    ws2 = torch.empty(lib.aeoq_ep_experts_nvfp4_workspace_size(n, k, T * k, e_loc, H, I), **u8)
+    A.check(lib.aeoq_ep_experts_nvfp4(rp.data_ptr(), rs.data_ptr(), ts.data_ptr(), n, rl.data_ptr(), rw.data_ptr(), k,
+                                      T * k, m.gate_up_proj.data_ptr(), gu_atoms.data_ptr(),
+                                      m.gate_up_proj_scale_2.data_ptr(), A.dtype_code(m.gate_up_proj_scale_2.dtype),
+                                      m.down_proj.data_ptr(), dw_atoms.data_ptr(), m.down_proj_scale_2.data_ptr(),
+                                      A.dtype_code(m.down_proj_scale_2.dtype), e_loc, H, I, rows.data_ptr(),
+                                      ws2.data_ptr(), ws2.numel(), A.err_word(dev).data_ptr(), st))
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    ws3 = torch.empty(lib.aeoq_ep_combine_workspace_size(world, T, H), **u8)
+    A.check(lib.aeoq_ep_combine(comm, world, rank, rows.data_ptr(), slot_row.data_ptr(), T, H, out.data_ptr(),
+                                ws3.data_ptr(), ws3.numel(), st))
+    torch.cuda.synchronize(dev)
+    A.check(lib.aeoq_ep_nccl_comm_destroy(comm))
+    return out.cpu()
+
+
 def main():
     rank, world, port, out_path = int(sys.argv[1]), int(sys.argv[2]), sys.argv[3], sys.argv[4]
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -50,7 +104,8 @@ def main():
     y = ep(hid[lo:hi], ids[lo:hi], w[lo:hi])
     ep.equal_tokens = True                                 # fixed-size all-to-alls, no host sync
     y_dense = ep(hid[lo:hi], ids[lo:hi], w[lo:hi])
-    res = {"y": y.cpu(), "y_dense": y_dense.cpu(), "lo": lo, "hi": hi}
+    res = {"y": y.cpu(), "y_dense": y_dense.cpu(), "y_capi": capi_layer(m, hid[lo:hi], ids[lo:hi], w[lo:hi], E),
+           "lo": lo, "hi": hi}
     if rank == 0:
         res["ref"] = moe_ops.nvfp4_experts_grouped(hid, ids, w, gp, gs, gt.float(), dp, ds, dt.float()).cpu()
         res["inputs"] = {"hid": hid.cpu(), "ids": ids.cpu(), "w": w.cpu(),

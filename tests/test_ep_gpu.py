@@ -54,3 +54,6 @@ def test_ep_two_gpus_match_one_gpu(tmp_path):
     assert np.all(np.abs(y.astype(np.float64) - ref) <= lim)
     # the fixed-size, host-sync-free dispatch gives the same bits
     assert torch.equal(torch.cat([r0["y_dense"], r1["y_dense"]]), torch.cat([r0["y"], r1["y"]]))
+    # the C-ABI layer (dispatch, experts, combine over its own NCCL
+    # communicator) gives the Python layer's bits
+    assert torch.equal(torch.cat([r0["y_capi"], r1["y_capi"]]), torch.cat([r0["y"], r1["y"]]))
