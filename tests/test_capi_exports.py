@@ -109,3 +109,27 @@ def test_matmul_shape_errors_match_reference():
     with pytest.raises(ValueError, match="expert_ids must be 1D"):
         NM.nvfp4_linear_3d_gather(a, s, t, torch.zeros(2, 128, 64, dtype=torch.uint8), s, t,
                                   torch.zeros(2, 1, dtype=torch.int64))
+
+
+def test_expert_parallel_entries_without_gpu(lib):
+    """The expert-parallel C entries check their arguments before any NCCL or
+    CUDA call, and size their workspaces from the shapes alone."""
+    assert lib.aeoq_ep_nccl_unique_id_bytes() == 128
+    # no communicator
+    rc = lib.aeoq_ep_dispatch(None, 2, 0, None, 48, 2816, None, 4, None, 8, 16, None, None, None, None, None, None,
+                              None, None, 0, None)
+    assert rc == -1 and b"ep_dispatch" in lib.aeoq_last_error()
+    # experts not divisible over the ranks
+    rc = lib.aeoq_ep_dispatch(1, 3, 0, None, 48, 2816, None, 4, None, 8, 16, None, None, None, None, None, None,
+                              None, None, 0, None)
+    assert rc == -1 and b"multiple of world" in lib.aeoq_last_error()
+    rc = lib.aeoq_ep_combine(None, 2, 5, None, None, 48, 2816, None, None, 0, None)
+    assert rc == -1
+    # dispatch: amax + this rank's quantized rows + the per-destination ids
+    n = lib.aeoq_ep_dispatch_workspace_size(2, 48, 8, 2816)
+    assert n >= 48 * 2816 // 2 + 48 * 2816 // 16 + 2 * 48 * 8 * 4
+    assert lib.aeoq_ep_dispatch_workspace_size(2, 0, 8, 2816) == 0
+    # combine: the returned rows of every rank
+    assert lib.aeoq_ep_combine_workspace_size(2, 48, 2816) >= 2 * 48 * 2816 * 2
+    # experts: at least the sorted (pairs, H) bf16 outputs
+    assert lib.aeoq_ep_experts_nvfp4_workspace_size(96, 8, 384, 8, 2816, 704) >= 96 * 8 * 2816 * 2
